@@ -1,0 +1,468 @@
+#!/usr/bin/env python
+"""Q4_K x q8_1 decode-GEMV benchmark on B200.
+
+Workload ("mistral-7b-decode-gemv-set"): one decode step's
+Q4_K GEMVs of Mistral-7B at batch 1 -- 32 layers x {q 4096x4096, k 1024x4096,
+v 1024x4096, o 4096x4096, gate 14336x4096, up 14336x4096, down 4096x14336}
+plus the 32000x4096 output head, synthetic seeded weights with the BASELINE
+value distributions (d, dmin = fp16(|N(0,1)|*0.01), uniform 6-bit scales/mins,
+uniform nibbles) and x ~ N(0,1) (one activation per matrix group: q/k/v share
+one, gate/up share one).  One prep + persistent GEMV launch pair per layer.
+The 4.0 GB of weights per step exceed the 126 MB L2, so every step streams
+from HBM.
+
+Metric: achieved algorithmic HBM bandwidth of the whole job (TB/s, whole
+job over all ranks) with bytes = rows*K*0.5625 + ncols*K*4 per distinct
+activation + ncols*rows*4; also reported as us per GEMV launch.
+
+  python bench.py [--gpus N --steps K --warmup W --ncols C]
+  python bench.py --impl reference    # the reference's CPU path, timed on the host
+
+N > 1 (torchrun, one rank per GPU): every matrix is row-sharded across the
+ranks and each layer's output slices are all-gathered over NCCL.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+PKG_DIR = ROOT / "gemv-q4_k-optimization_b200"
+PROFILES = ROOT / "profiles"
+
+LAYERS = 32
+# (name, rows, K, activation group)
+MATS = [("q", 4096, 4096, "attn"), ("k", 1024, 4096, "attn"), ("v", 1024, 4096, "attn"),
+        ("o", 4096, 4096, "o"), ("gate", 14336, 4096, "ffn"), ("up", 14336, 4096, "ffn"),
+        ("down", 4096, 14336, "down")]
+ACT_K = {"attn": 4096, "o": 4096, "ffn": 4096, "down": 14336}
+HEAD = (32000, 4096)
+WORKLOAD = "mistral-7b-decode-gemv-set"
+METRIC = "Q4_K GEMV achieved HBM TB/s (algorithmic bytes), us per GEMV launch"
+
+
+def load_package():
+    if "q4k_b200" in sys.modules:
+        return sys.modules["q4k_b200"]
+    spec = importlib.util.spec_from_file_location("q4k_b200", PKG_DIR / "__init__.py",
+                                                  submodule_search_locations=[str(PKG_DIR)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["q4k_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def load_oracle():
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    O.build()
+    return O
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def shard(rows: int, rank: int, world: int):
+    """Contiguous ceil-split row range [lo, hi) of rank (tails may be short)."""
+    per = (rows + world - 1) // world
+    lo = min(rows, rank * per)
+    return lo, min(rows, lo + per), per
+
+
+def step_bytes(ncols: int, world: int = 1) -> dict:
+    """Algorithmic bytes of one decode step, whole job (all ranks)."""
+    w = sum(r * K * 9 // 16 for _, r, K, _ in MATS) * LAYERS + HEAD[0] * HEAD[1] * 9 // 16
+    x_layer = sum(ncols * K * 4 for K in ACT_K.values())
+    y_layer = sum(ncols * r * 4 for _, r, _, _ in MATS)
+    x = (x_layer * LAYERS + ncols * HEAD[1] * 4) * world  # every rank reads the whole x
+    y = y_layer * LAYERS + ncols * HEAD[0] * 4
+    layer = sum(r * K * 9 // 16 for _, r, K, _ in MATS) + x_layer + y_layer
+    return {"total": w + x + y, "weights": w, "per_layer_launch": layer}
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str | None):
+        self.bus_id = (bus_id or "").lower()
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        rows = []
+        for ln in self.lines:
+            f = [c.strip() for c in ln.split(",")]
+            if len(f) < 10:
+                continue
+            if self.bus_id and self.bus_id[-12:] not in f[1].lower():
+                continue
+            rows.append(f)
+        sm = [float(f[2].split()[0]) for f in rows if f[2].split()[0].replace(".", "").isdigit()]
+        smax = [float(f[3].split()[0]) for f in rows if f[3].split()[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for f in rows for n, v in zip(names, f[6:10]) if v.lower() == "active"})
+        loaded = [s for s in sm if smax and s > 0.5 * max(smax)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's own CPU code path (host cores)
+# ---------------------------------------------------------------------------
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    O = load_oracle()
+    q4k = load_package()
+    kind = "reference" if O.ref_available() else "port"
+    rng = np.random.default_rng(0)
+    ncols = args.ncols
+    mats = [(q4k.gen_q4k_numpy(rng, r, K), K, grp) for _, r, K, grp in MATS]
+    xs = {g: rng.standard_normal((ncols, K)).astype(np.float32) for g, K in ACT_K.items()}
+    threads = O.max_threads() if kind == "port" else O.ref_lib().ref_max_threads()
+
+    def one_step():
+        for W, K, grp in mats:
+            yq = O.quantize_q8_1(xs[grp])
+            if kind == "reference":
+                O.ref_gemv_q8_1(W, K, yq, nthreads=threads)
+            else:
+                O.gemv_q8_1(W, K, yq, nthreads=threads)
+
+    for _ in range(args.warmup):
+        one_step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_step()
+    dt = (time.perf_counter() - t0) / args.steps
+    sample_bytes = step_bytes(ncols)["per_layer_launch"]
+    tbs = sample_bytes / dt / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tbs, "unit": "TB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "ncols": ncols, "sample": "one decoder layer (7 matrices) per step"},
+        "cpu_baseline": {"value": tbs, "unit": "TB/s", "cores": threads, "kind": kind,
+                         "sample": "one Mistral-7B decoder layer's 7 Q4_K GEMVs (122.7 MB of weights) per step, "
+                                   "q8_1 quantization included"},
+        "e2e": {"value": tbs, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def cpu_baseline(O, layer_mats, ncols, budget_s: float = 12.0) -> dict:
+    """The oracle (all host threads) on layer 0's matrices, repeated for ~budget_s."""
+    rng = np.random.default_rng(1)
+    xs = {g: rng.standard_normal((ncols, K)).astype(np.float32) for g, K in ACT_K.items()}
+    threads = O.max_threads()
+    bytes_one = step_bytes(ncols)["per_layer_launch"]
+    n, t0 = 0, time.perf_counter()
+    while True:
+        for W, K, grp in layer_mats:
+            O.gemv_f32(W, xs[grp], nthreads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or n >= 200:
+            break
+    return {"value": bytes_one * n / el / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} x one Mistral-7B decoder layer's 7 Q4_K GEMVs (fp32 x, q8_1 quantization "
+                      f"included) = {el:.1f} s on the host"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--ncols", type=int, default=1)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    q4k = load_package()
+    q4k.lib()
+    ncols = args.ncols
+
+    # ---- weights (sharded rows), activations, outputs -------------------------
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    layers = []
+    for li in range(LAYERS):
+        xs = {grp: torch.randn((ncols, K), device=dev, generator=g) for grp, K in ACT_K.items()}
+        ents = []
+        for name, rows, K, grp in MATS:
+            lo, hi, per = shard(rows, rank, world)
+            W = q4k.gen_q4k_torch(hi - lo, K, generator=g, device=dev)
+            ents.append((name, W, xs[grp], rows, per, hi - lo))
+        # local outputs packed so one all-gather covers the layer
+        per_tot = sum(e[4] for e in ents)
+        ybuf = torch.zeros((per_tot * ncols,), device=dev)
+        outs, off = [], 0
+        for e in ents:
+            outs.append(ybuf[off: off + e[4] * ncols].view(ncols, e[4])[:, : e[5]])
+            off += e[4] * ncols
+        tasks = q4k.make_tasks([e[1] for e in ents], [e[2] for e in ents], outs)
+        gath = torch.empty((per_tot * ncols * world,), device=dev) if world > 1 else None
+        layers.append(dict(xs=xs, ents=ents, ybuf=ybuf, outs=outs, tasks=tasks, gath=gath))
+    hlo, hhi, hper = shard(HEAD[0], rank, world)
+    head_W = q4k.gen_q4k_torch(hhi - hlo, HEAD[1], generator=g, device=dev)
+    head_x = torch.randn((ncols, HEAD[1]), device=dev, generator=g)
+    head_y = torch.zeros((hper * ncols,), device=dev)
+    head_out = head_y.view(ncols, hper)[:, : hhi - hlo]
+    head_tasks = q4k.make_tasks([head_W], [head_x], [head_out])
+    head_gath = torch.empty((hper * ncols * world,), device=dev) if world > 1 else None
+
+    ws_bytes = max([q4k.batch_workspace_bytes(L["tasks"], ncols) for L in layers] +
+                   [q4k.batch_workspace_bytes(head_tasks, ncols)])
+    ws = q4k.Workspace(ws_bytes, dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def run_step(ev=None):
+        for li, L in enumerate(layers):
+            if ev is not None:
+                ev[li][0].record(stream)
+            q4k.gemv_batch(L["tasks"], ncols, ws, stream=stream)
+            if ev is not None:
+                ev[li][1].record(stream)
+            if world > 1:
+                dist.all_gather_into_tensor(L["gath"], L["ybuf"])
+        q4k.gemv_batch(head_tasks, ncols, ws, stream=stream)
+        if world > 1:
+            dist.all_gather_into_tensor(head_gath, head_y)
+
+    # ---- correctness spot check before timing (rank-local, layer 0 'q') ------
+    with torch.cuda.stream(stream):
+        run_step()
+    stream.synchronize()
+    assert ws.status(stream) == 0, "device status word reports an error"
+
+    # ---- capture one graph per timed step (own timing events in each) --------
+    nsteps = args.steps + args.warmup
+    use_graph = True
+    graphs, evs = [], []
+    try:
+        with torch.cuda.stream(stream):
+            for s in range(nsteps):
+                ev = [(torch.cuda.Event(enable_timing=True, external=True),
+                       torch.cuda.Event(enable_timing=True, external=True)) for _ in range(LAYERS)]
+                gph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gph, stream=stream):
+                    run_step(ev)
+                graphs.append(gph)
+                evs.append(ev)
+    except Exception as e:  # capture unsupported (e.g. collectives): time eagerly
+        print(f"# graph capture failed ({e!r}); timing eager launches", file=sys.stderr)
+        use_graph = False
+        graphs, evs = [], []
+        for s in range(nsteps):
+            evs.append([(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                        for _ in range(LAYERS)])
+
+    def replay(s):
+        if use_graph:
+            graphs[s].replay()
+        else:
+            with torch.cuda.stream(stream):
+                run_step(evs[s])
+
+    bus_id = None
+    try:
+        bus_id = torch.cuda.get_device_properties(dev).pci_bus_id
+    except AttributeError:
+        pass
+    sampler = ClockSampler(bus_id) if rank == 0 else None
+
+    for s in range(args.warmup):
+        replay(s)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for s in range(args.warmup, nsteps):
+        replay(s)
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop() if sampler else None
+
+    ms = t_start.elapsed_time(t_end) / args.steps
+    launch_ms = [evs[s][li][0].elapsed_time(evs[s][li][1]) for s in range(args.warmup, nsteps)
+                 for li in range(LAYERS)]
+    launch_ms_mean = float(np.mean(launch_ms))
+    if world > 1:
+        t = torch.tensor([ms, launch_ms_mean], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, launch_ms_mean = float(t[0]), float(t[1])
+
+    sb = step_bytes(ncols, world)
+    value = sb["total"] / (ms * 1e-3) / 1e12
+    peak, peak_kind = measured_peaks()
+    per_launch_bytes = sb["per_layer_launch"] if world == 1 else None
+    if world > 1:  # this rank's share of one layer
+        per_launch_bytes = sum(e[5] * e[2].shape[1] * 9 // 16 + ncols * e[5] * 4 for e in layers[0]["ents"]) + \
+            sum(ncols * K * 4 for K in ACT_K.values())
+    achieved = per_launch_bytes / (launch_ms_mean * 1e-3) / 1e9
+
+    # ---- e2e: public C-ABI calls with host buffers ------------------------------
+    e2e = None
+    if not args.no_e2e:
+        xs_all = [L["xs"][grp] for L in layers for grp in ACT_K] + [head_x]
+        ys_all = [L["ybuf"] for L in layers] + [head_y]
+        h_x = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in xs_all]
+        for h, d in zip(h_x, xs_all):
+            h.copy_(d)
+        h_y = [torch.empty(y.shape, dtype=y.dtype, pin_memory=True) for y in ys_all]
+        h2d = sum(h.numel() * 4 for h in h_x)
+        d2h = sum(h.numel() * 4 for h in h_y)
+
+        def e2e_step():
+            with torch.cuda.stream(stream):
+                for h, d in zip(h_x, xs_all):
+                    d.copy_(h, non_blocking=True)
+                run_step()
+                for h, d in zip(h_y, ys_all):
+                    h.copy_(d, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        e_ms = a.elapsed_time(b) / args.steps
+        if world > 1:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t[0])
+        e2e = {"value": sb["total"] / (e_ms * 1e-3) / 1e12, "unit": "TB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e_ms,
+               "path": "q4k_gemv_batch C-ABI calls (ctypes) per layer, pinned host x -> device, "
+                       "outputs -> pinned host, every step"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        O = load_oracle()
+        layer_mats = [(e[1].cpu().numpy(), e[2].shape[1], grp) for e, (_, _, _, grp) in
+                      zip(layers[0]["ents"], MATS)]
+        cpu = cpu_baseline(O, layer_mats, ncols)
+
+    traffic = None
+    tf = PROFILES / "gemv_layer_traffic.json"
+    if tf.exists() and world == 1:
+        d = json.loads(tf.read_text())
+        if d.get("ncols") == ncols:
+            traffic = d.get("dram_bytes_per_launch")
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "layers": LAYERS, "matrices_per_layer": len(MATS),
+                       "head": f"{HEAD[0]}x{HEAD[1]}", "ncols": ncols,
+                       "launches": "per layer: prep (q8_1 quantization) + persistent GEMV over 7 matrices (PDL)",
+                       "timing": "CUDA-graph replay per step, CUDA events on the launch stream",
+                       "l2": "inputs larger than L2 (4.0 GB of weights per step, no flush needed)",
+                       "parallelism": "single GPU" if world == 1 else f"row-shard x{world} + NCCL all-gather per layer"},
+            "us_per_call": launch_ms_mean * 1e3,
+            "pct_hbm_peak": 100.0 * value * 1e3 / world / peak,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
+                         "kernel": "k_gemv (one decoder layer, 7 matrices) incl. its overlapped prep launch",
+                         "algorithmic_bytes_per_launch": per_launch_bytes},
+            "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+            "gpu_launches": args.steps * (LAYERS + 1) * 2,
+            "graph": use_graph,
+        }
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        graphs.clear()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

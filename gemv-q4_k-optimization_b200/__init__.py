@@ -1,0 +1,324 @@
+"""Python front-end of libq4k_gemv.so, the sm_100a Q4_K x q8_1 decode GEMV.
+
+The library's C ABI (include/q4k_gemv.h) is the drop-in boundary; this module
+binds it with ctypes and uses torch only for device memory and streams.  The
+function names follow the reference entry points they stand in for
+(paths relative to the reference project):
+
+  mul_mat_vec_q        ggml_cuda_mul_mat_vec_q       kernels/mmvq.cu:666-762
+  mul_mat_vec_q8_1     mul_mat_vec_q_switch_type Q4_K kernels/mmvq.cu:479-593
+  op_mul_mat_vec_q     ggml_cuda_op_mul_mat_vec_q    kernels/mmvq.cu:764-793
+  quantize_row_q8_1    quantize_row_q8_1_cuda call   kernels/mmvq.cu:734
+  custom_q4k_gemv      custom_q4k_gemv hook launch   kernels/mmvq.cu:10-18, :563-584
+
+Tensor conventions: a Q4_K matrix is a uint8 tensor (nrows, K/256*144);
+fp32 activations are (ncols, K) (column j = row j of the tensor, so the ggml
+column stride is x.stride(0)); outputs are (ncols, nrows).  There is no CPU
+fallback: every call goes to the CUDA library, which must be built
+(`make -C gemv-q4_k-optimization_b200`) and fails loudly otherwise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+from pathlib import Path
+from typing import Sequence
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libq4k_gemv.so"
+HEADER_PATH = HERE.parent / "include" / "q4k_gemv.h"
+
+QK_K = 256
+BLOCK_BYTES = 144
+QK8_1 = 32
+Q8_1_BYTES = 36
+ROW_PADDING = 512
+MAX_NCOLS = 8
+MAX_TASKS = 16
+
+STATUS_NAMES = {0: "Q4K_OK", 1: "Q4K_EINVAL", 2: "Q4K_ECUDA", 3: "Q4K_ETIMEOUT", 4: "Q4K_ENCCL",
+                5: "Q4K_EWORKSPACE"}
+
+
+class Q4KError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class Task(ctypes.Structure):
+    """struct q4k_task (include/q4k_gemv.h)."""
+    _fields_ = [("W", ctypes.c_void_p), ("x", ctypes.c_void_p), ("dst", ctypes.c_void_p),
+                ("nrows", ctypes.c_int64), ("K", ctypes.c_int64), ("stride_row_x", ctypes.c_int64),
+                ("stride_col_x", ctypes.c_int64), ("stride_col_dst", ctypes.c_int64)]
+
+
+_lib = None
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+_SZ = ctypes.c_size_t
+
+
+def build() -> None:
+    """Compile libq4k_gemv.so for sm_100a in-tree (nvcc cross-compiles without a GPU)."""
+    import subprocess
+    subprocess.run(["make", "-C", str(HERE)], check=True)
+
+
+def lib() -> ctypes.CDLL:
+    """Load the CUDA library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: build the CUDA library first "
+                               f"(make -C {HERE})")
+        L = ctypes.CDLL(str(LIB_PATH))
+        L.q4k_status_string.restype = ctypes.c_char_p
+        L.q4k_status_string.argtypes = [_I]
+        L.q4k_last_error.restype = ctypes.c_char_p
+        L.q4k_version.restype = _I
+        L.q4k_device_supported.restype = _I
+        L.q4k_row_bytes.restype = _SZ
+        L.q4k_row_bytes.argtypes = [_I64]
+        L.q4k_q8_1_bytes.restype = _SZ
+        L.q4k_q8_1_bytes.argtypes = [_I64, _I]
+        L.q4k_gemv_workspace_bytes.restype = _SZ
+        L.q4k_gemv_workspace_bytes.argtypes = [_I64, _I64, _I]
+        L.q4k_batch_workspace_bytes.restype = _SZ
+        L.q4k_batch_workspace_bytes.argtypes = [ctypes.POINTER(Task), _I, _I]
+        L.q4k_quantize_q8_1.argtypes = [_P, _I64, _I64, _I64, _I, _P, _P]
+        L.q4k_mul_mat_vec_q8_1.argtypes = [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _SZ, _P]
+        L.q4k_mul_mat_vec.argtypes = [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _SZ, _P]
+        L.q4k_op_mul_mat_vec_q.argtypes = [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P]
+        L.q4k_custom_q4k_gemv.argtypes = [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]
+        L.q4k_gemv_batch.argtypes = [ctypes.POINTER(Task), _I, _I, _P, _SZ, _P]
+        L.q4k_debug_subblock_sums.argtypes = [_P, _P, _I64, _I64, _I, _I64, _I64, _P, _P, _P, _SZ, _P]
+        L.q4k_workspace_status.argtypes = [_P, ctypes.POINTER(_I), _P]
+        _lib = L
+    return _lib
+
+
+def declared_symbols() -> list[str]:
+    """Entry points declared in include/q4k_gemv.h."""
+    text = HEADER_PATH.read_text()
+    return sorted(set(re.findall(r"^Q4K_API\s+[\w\s\*]*?\b(q4k_\w+)\s*\(", text, flags=re.M)))
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        msg = lib().q4k_last_error().decode(errors="replace")
+        raise Q4KError(status, msg)
+
+
+def _stream(stream) -> int:
+    import torch
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def kpad(K: int) -> int:
+    return (K + ROW_PADDING - 1) // ROW_PADDING * ROW_PADDING
+
+
+def row_bytes(K: int) -> int:
+    return int(lib().q4k_row_bytes(K))
+
+
+# ---------------------------------------------------------------------------
+# workspace
+# ---------------------------------------------------------------------------
+class Workspace:
+    """Device scratch owned by the caller (the library never allocates).
+
+    Grows on demand; one Workspace must not serve two calls that can overlap
+    on the GPU (e.g. on two streams)."""
+
+    def __init__(self, nbytes: int = 0, device=None):
+        import torch
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=self.device)
+
+    def ensure(self, nbytes: int) -> "Workspace":
+        import torch
+        if nbytes > self.buf.numel():
+            self.buf = torch.empty(int(nbytes), dtype=torch.uint8, device=self.device)
+        return self
+
+    @property
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+    @property
+    def nbytes(self) -> int:
+        return self.buf.numel()
+
+    def status(self, stream=None) -> int:
+        v = ctypes.c_int(0)
+        _check(lib().q4k_workspace_status(self.ptr, ctypes.byref(v), _stream(stream)))
+        return v.value
+
+
+_default_ws: dict = {}
+
+
+def _ws_for(nbytes: int, ws: Workspace | None, device) -> Workspace:
+    if ws is not None:
+        return ws.ensure(nbytes)
+    key = str(device)
+    w = _default_ws.get(key)
+    if w is None:
+        w = _default_ws[key] = Workspace(nbytes, device)
+    return w.ensure(nbytes)
+
+
+def gemv_workspace_bytes(nrows: int, K: int, ncols: int) -> int:
+    return int(lib().q4k_gemv_workspace_bytes(nrows, K, ncols))
+
+
+# ---------------------------------------------------------------------------
+# entry points
+# ---------------------------------------------------------------------------
+def quantize_row_q8_1(x, Kpad: int | None = None, out=None, stream=None):
+    """fp32 (ncols, K) -> ggml q8_1 (ncols, Kpad/32*36) uint8 on the device."""
+    import torch
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    assert x.dtype == torch.float32 and x.is_cuda and x.stride(1) == 1
+    ncols, K = x.shape
+    Kp = kpad(K) if Kpad is None else int(Kpad)
+    if out is None:
+        out = torch.empty((ncols, Kp // QK8_1 * Q8_1_BYTES), dtype=torch.uint8, device=x.device)
+    _check(lib().q4k_quantize_q8_1(x.data_ptr(), K, x.stride(0), Kp, ncols, out.data_ptr(), _stream(stream)))
+    return out
+
+
+def mul_mat_vec_q(W, x, out=None, ws: Workspace | None = None, stream=None):
+    """y = W @ x with fp32 activations x (ncols, K); returns (ncols, nrows) fp32."""
+    import torch
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    assert W.dtype == torch.uint8 and W.is_cuda and x.is_cuda and x.dtype == torch.float32
+    assert x.stride(1) == 1 and W.stride(1) == 1
+    ncols, K = x.shape
+    nrows = W.shape[0]
+    if W.stride(0) % BLOCK_BYTES:
+        raise Q4KError(1, "W row stride is not a whole number of super-blocks")
+    if out is None:
+        out = torch.empty((ncols, nrows), dtype=torch.float32, device=x.device)
+    w = _ws_for(gemv_workspace_bytes(nrows, K, ncols), ws, x.device)
+    _check(lib().q4k_mul_mat_vec(W.data_ptr(), x.data_ptr(), out.data_ptr(), K, nrows, ncols,
+                                 W.stride(0) // BLOCK_BYTES, x.stride(0), out.stride(0),
+                                 w.ptr, w.nbytes, _stream(stream)))
+    return out
+
+
+def mul_mat_vec_q8_1(W, yq, K: int, out=None, ws: Workspace | None = None, stream=None):
+    """y = W @ q8_1 activations yq (ncols, blocks*36 uint8); returns (ncols, nrows)."""
+    import torch
+    if yq.dim() == 1:
+        yq = yq.unsqueeze(0)
+    ncols = yq.shape[0]
+    nrows = W.shape[0]
+    if out is None:
+        out = torch.empty((ncols, nrows), dtype=torch.float32, device=W.device)
+    w = _ws_for(gemv_workspace_bytes(nrows, K, ncols), ws, W.device)
+    _check(lib().q4k_mul_mat_vec_q8_1(W.data_ptr(), yq.data_ptr(), out.data_ptr(), K, nrows, ncols,
+                                      W.stride(0) // BLOCK_BYTES, yq.stride(0) // Q8_1_BYTES, out.stride(0),
+                                      w.ptr, w.nbytes, _stream(stream)))
+    return out
+
+
+def op_mul_mat_vec_q(W_slice, K: int, yq, row_low: int, row_high: int, src1_padded_row_size: int,
+                     out=None, nrows_dst: int | None = None, ws: Workspace | None = None, stream=None):
+    """Row-split slice: rows [row_low, row_high) of the matrix, src1 pre-quantized."""
+    import torch
+    ncols = yq.shape[0]
+    rows = row_high - row_low
+    nd = rows if nrows_dst is None else nrows_dst
+    if out is None:
+        out = torch.empty((ncols, nd), dtype=torch.float32, device=W_slice.device)
+    w = _ws_for(gemv_workspace_bytes(rows, K, ncols), ws, W_slice.device)
+    _check(lib().q4k_op_mul_mat_vec_q(W_slice.data_ptr(), K, yq.data_ptr(), out.data_ptr(), row_low, row_high,
+                                      ncols, src1_padded_row_size, nd, w.ptr, w.nbytes, _stream(stream)))
+    return out
+
+
+def custom_q4k_gemv(vx, vy, dst, num_blocks_total: int, stride_col_y_blocks: int, stride_col_dst: int,
+                    ncols_dst: int, ws: Workspace | None = None, stream=None):
+    """The reference hook's 6-argument launch contract (+ ncols and workspace)."""
+    w = _ws_for(gemv_workspace_bytes(stride_col_dst, num_blocks_total * QK_K, ncols_dst), ws, dst.device)
+    _check(lib().q4k_custom_q4k_gemv(vx.data_ptr(), vy.data_ptr(), dst.data_ptr(), num_blocks_total,
+                                     stride_col_y_blocks, stride_col_dst, ncols_dst, w.ptr, w.nbytes,
+                                     _stream(stream)))
+    return dst
+
+
+def make_tasks(mats: Sequence, xs: Sequence, outs: Sequence):
+    """ctypes task array for gemv_batch from (W, x, out) tensor triples."""
+    n = len(mats)
+    arr = (Task * n)()
+    for i, (W, x, o) in enumerate(zip(mats, xs, outs)):
+        if x.dim() == 1:
+            x = x.unsqueeze(0)
+        arr[i].W = W.data_ptr()
+        arr[i].x = x.data_ptr()
+        arr[i].dst = o.data_ptr()
+        arr[i].nrows = W.shape[0]
+        arr[i].K = x.shape[1]
+        arr[i].stride_row_x = W.stride(0) // BLOCK_BYTES
+        arr[i].stride_col_x = x.stride(0)
+        arr[i].stride_col_dst = o.stride(0) if o.dim() > 1 else W.shape[0]
+    return arr
+
+
+def batch_workspace_bytes(tasks, ncols: int) -> int:
+    return int(lib().q4k_batch_workspace_bytes(tasks, len(tasks), ncols))
+
+
+def gemv_batch(tasks, ncols: int, ws: Workspace, stream=None) -> None:
+    """Every task's GEMV in one prep + one persistent GEMV launch."""
+    ws.ensure(batch_workspace_bytes(tasks, ncols))
+    _check(lib().q4k_gemv_batch(tasks, len(tasks), ncols, ws.ptr, ws.nbytes, _stream(stream)))
+
+
+def debug_subblock_sums(W, yq, K: int, ws: Workspace | None = None, stream=None):
+    """Exact (S, T) as the kernels form them: S (ncols, nrows, K/32), T (ncols, K/32) int32."""
+    import torch
+    ncols, nrows = yq.shape[0], W.shape[0]
+    S = torch.empty((ncols, nrows, K // QK8_1), dtype=torch.int32, device=W.device)
+    T = torch.empty((ncols, K // QK8_1), dtype=torch.int32, device=W.device)
+    w = _ws_for(gemv_workspace_bytes(nrows, K, ncols), ws, W.device)
+    _check(lib().q4k_debug_subblock_sums(W.data_ptr(), yq.data_ptr(), K, nrows, ncols,
+                                         W.stride(0) // BLOCK_BYTES, yq.stride(0) // Q8_1_BYTES,
+                                         S.data_ptr(), T.data_ptr(), w.ptr, w.nbytes, _stream(stream)))
+    return S, T
+
+
+# ---------------------------------------------------------------------------
+# synthetic data with the benchmark's value distributions
+# ---------------------------------------------------------------------------
+def gen_q4k_numpy(rng: np.random.Generator, nrows: int, K: int) -> np.ndarray:
+    """Q4_K matrix (nrows, K/256*144) uint8: d, dmin = fp16(|N(0,1)|*0.01); scale/min
+    bytes uniform (so every 6-bit scale and min is uniform on 0..63); nibbles uniform."""
+    nb = K // QK_K
+    W = rng.integers(0, 256, size=(nrows, nb, BLOCK_BYTES), dtype=np.uint8)
+    d = (np.abs(rng.standard_normal((nrows, nb, 2))) * 0.01).astype(np.float16)
+    W[:, :, 0:4] = d.view(np.uint8).reshape(nrows, nb, 4)
+    return W.reshape(nrows, nb * BLOCK_BYTES)
+
+
+def gen_q4k_torch(nrows: int, K: int, generator=None, device="cuda"):
+    """Same distributions as gen_q4k_numpy, generated on the device (large matrices)."""
+    import torch
+    nb = K // QK_K
+    W = torch.randint(0, 256, (nrows, nb, BLOCK_BYTES), dtype=torch.uint8, device=device, generator=generator)
+    d = (torch.randn((nrows, nb, 2), device=device, generator=generator).abs_() * 0.01).to(torch.float16)
+    W[:, :, 0:4] = d.view(torch.uint8).reshape(nrows, nb, 4)
+    return W.view(nrows, nb * BLOCK_BYTES)

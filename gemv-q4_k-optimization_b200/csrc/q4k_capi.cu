@@ -1,0 +1,420 @@
+// q4k_capi.cu -- host runtime and C ABI of libq4k_gemv.so (declared in
+// include/q4k_gemv.h).
+//
+// Responsibilities: argument validation (status codes instead of the
+// reference's aborts), workspace layout, de-duplication of shared
+// activations, the flattened work schedule (atoms and row groups) and the
+// two-launch sequence prep -> GEMV (the GEMV is a programmatic dependent
+// launch, so its weight stream overlaps the activation quantization).
+#include "q4k_gemv.h"
+#include "q4k_internal.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+using namespace q4k;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(Q4K_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+constexpr size_t kAlign = 256;
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Upper bound on workers when no device can be queried.
+constexpr int kFallbackSMs = 256;
+
+int num_sms_or_bound() {
+    int n = 0;
+    if (device_setup(&n) == cudaSuccess && n > 0) return n;
+    cudaGetLastError();
+    return kFallbackSMs;
+}
+
+// Workspace layout: [status word | pad][counters][partials][activations].
+struct Layout {
+    size_t counters_off = 0, partials_off = 0, act_off = 0, total = 0;
+};
+
+Layout make_layout(int64_t n_rowgroups, int ncols, size_t act_bytes, int num_sms) {
+    Layout L;
+    L.counters_off = kAlign;
+    L.partials_off = L.counters_off + round_up(static_cast<size_t>(n_rowgroups) * 4, kAlign);
+    const size_t workers = static_cast<size_t>(num_sms) * kWarps;
+    L.act_off = L.partials_off + round_up(workers * 2 * ncols * 32 * sizeof(float), kAlign);
+    L.total = L.act_off + round_up(act_bytes, kAlign);
+    return L;
+}
+
+// One matrix as the runtime sees it: activations are fp32 or ggml q8_1.
+struct Job {
+    const void *W;
+    const void *src;
+    float *dst;
+    int64_t nrows, K, stride_row_x, src_col_stride, stride_col_dst;
+    int kind;  // kPrepF32 / kPrepQ81
+};
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int validate_job(const Job &j, int ncols, int idx) {
+    if (ncols < 1 || ncols > Q4K_MAX_NCOLS)
+        return fail(Q4K_EINVAL, "ncols=%d outside 1..%d", ncols, Q4K_MAX_NCOLS);
+    if (j.nrows < 0) return fail(Q4K_EINVAL, "task %d: nrows=%lld < 0", idx, (long long)j.nrows);
+    if (j.K < 0 || j.K % Q4K_QK_K != 0)
+        return fail(Q4K_EINVAL, "task %d: K=%lld is not a non-negative multiple of 256", idx, (long long)j.K);
+    if (j.K > (int64_t(1) << 30)) return fail(Q4K_EINVAL, "task %d: K=%lld too large", idx, (long long)j.K);
+    if (j.nrows > (int64_t(1) << 30)) return fail(Q4K_EINVAL, "task %d: nrows too large", idx);
+    if (j.nrows == 0) return Q4K_OK;
+    if (!j.dst) return fail(Q4K_EINVAL, "task %d: null dst", idx);
+    if (ncols > 1 && j.stride_col_dst < j.nrows)
+        return fail(Q4K_EINVAL, "task %d: stride_col_dst=%lld < nrows", idx, (long long)j.stride_col_dst);
+    if (j.K == 0) return Q4K_OK;  // empty sums: dst is zeroed
+    if (!j.W || !j.src) return fail(Q4K_EINVAL, "task %d: null pointer", idx);
+    if (!aligned16(j.W)) return fail(Q4K_EINVAL, "task %d: W is not 16-byte aligned", idx);
+    if (j.stride_row_x < j.K / Q4K_QK_K)
+        return fail(Q4K_EINVAL, "task %d: stride_row_x=%lld < K/256", idx, (long long)j.stride_row_x);
+    if (j.kind == kPrepF32) {
+        if (ncols > 1 && j.src_col_stride < j.K)
+            return fail(Q4K_EINVAL, "task %d: stride_col_x=%lld < K", idx, (long long)j.src_col_stride);
+    } else {
+        if (ncols > 1 && j.src_col_stride < j.K / Q4K_QK8_1)
+            return fail(Q4K_EINVAL, "task %d: stride_col_y=%lld < K/32", idx, (long long)j.src_col_stride);
+    }
+    return Q4K_OK;
+}
+
+struct Plan {
+    PrepParams prep{};
+    GemvParams gemv{};
+    Layout layout{};
+    int64_t n_rowgroups = 0;
+    size_t act_bytes = 0;
+    int act_of_job[kMaxTasks] = {};
+    int n_act = 0;
+    bool any_work = false;
+};
+
+// Build the schedule (no device memory touched).  ws may be null (sizing).
+int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, Plan &P,
+              int32_t *dump_T = nullptr) {
+    if (njobs < 1 || njobs > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..%d", njobs, kMaxTasks);
+    for (int i = 0; i < njobs; ++i) {
+        int st = validate_job(jobs[i], ncols, i);
+        if (st != Q4K_OK) return st;
+    }
+    // distinct activations
+    struct Act { const void *src; int64_t K, stride; int kind; size_t off; };
+    Act acts[kMaxTasks];
+    P.n_act = 0;
+    P.act_bytes = 0;
+    for (int i = 0; i < njobs; ++i) {
+        const Job &j = jobs[i];
+        P.act_of_job[i] = -1;
+        if (j.nrows == 0 || j.K == 0) continue;
+        int found = -1;
+        for (int a = 0; a < P.n_act; ++a)
+            if (acts[a].src == j.src && acts[a].K == j.K && acts[a].stride == j.src_col_stride &&
+                acts[a].kind == j.kind)
+                found = a;
+        if (found < 0) {
+            found = P.n_act++;
+            acts[found] = {j.src, j.K, j.src_col_stride, j.kind, P.act_bytes};
+            P.act_bytes += round_up(static_cast<size_t>(ncols) * (j.K / Q4K_QK_K) * kActSBBytes, kAlign);
+        }
+        P.act_of_job[i] = found;
+    }
+    // row groups and atoms
+    int64_t atoms = 0, rgs = 0;
+    int nt = 0;
+    for (int i = 0; i < njobs; ++i) {
+        const Job &j = jobs[i];
+        if (P.act_of_job[i] < 0) continue;
+        const int64_t groups = (j.nrows + 31) / 32;
+        const int64_t nb = j.K / Q4K_QK_K;
+        const int64_t apr = (nb + kKS - 1) / kKS;
+        TaskDesc &T = P.gemv.task[nt++];
+        T.W = static_cast<const uint8_t *>(j.W);
+        T.dst = j.dst;
+        T.row_stride = j.stride_row_x * Q4K_BLOCK_BYTES;
+        T.act_col_stride = nb * kActSBBytes;
+        T.dst_col_stride = j.stride_col_dst;
+        T.atom_base = atoms;
+        T.nrows = static_cast<int32_t>(j.nrows);
+        T.nb = static_cast<int32_t>(nb);
+        T.apr = static_cast<int32_t>(apr);
+        T.rg_base = static_cast<int32_t>(rgs);
+        atoms += groups * apr;
+        rgs += groups;
+    }
+    P.n_rowgroups = rgs;
+    P.layout = make_layout(rgs, ncols, P.act_bytes, num_sms);
+    P.any_work = atoms > 0;
+    P.gemv.ntasks = nt;
+    P.gemv.natoms = atoms;
+    const int64_t max_workers = static_cast<int64_t>(num_sms) * kWarps;
+    P.gemv.nworkers = static_cast<int32_t>(atoms < max_workers ? atoms : max_workers);
+    if (ws == nullptr) return Q4K_OK;
+
+    // pointers into the workspace
+    P.gemv.status = reinterpret_cast<int32_t *>(ws);
+    P.gemv.counters = reinterpret_cast<int32_t *>(ws + P.layout.counters_off);
+    P.gemv.partials = reinterpret_cast<float *>(ws + P.layout.partials_off);
+    P.gemv.dump_S = nullptr;
+    nt = 0;
+    for (int i = 0; i < njobs; ++i) {
+        if (P.act_of_job[i] < 0) continue;
+        P.gemv.task[nt++].act = ws + P.layout.act_off + acts[P.act_of_job[i]].off;
+    }
+    // prep jobs: one per distinct activation
+    int64_t items = 0;
+    for (int a = 0; a < P.n_act; ++a) {
+        PrepJob &J = P.prep.job[a];
+        J.src = acts[a].src;
+        J.act = ws + P.layout.act_off + acts[a].off;
+        J.q81_out = nullptr;
+        J.dump_T = dump_T;
+        J.src_col_stride = acts[a].stride;
+        J.act_col_stride = (acts[a].K / Q4K_QK_K) * kActSBBytes;
+        J.q81_col_stride = 0;
+        J.item_base = items;
+        J.K = static_cast<int32_t>(acts[a].K);
+        J.nblk = static_cast<int32_t>(acts[a].K / Q4K_QK8_1);
+        J.ncols = ncols;
+        J.kind = acts[a].kind;
+        items += static_cast<int64_t>(ncols) * J.nblk;
+    }
+    P.prep.njobs = P.n_act;
+    P.prep.nitems = items;
+    P.prep.zero_ptr = reinterpret_cast<int32_t *>(ws);
+    P.prep.zero_count = static_cast<int32_t>((P.layout.counters_off + rgs * 4) / 4);
+    return Q4K_OK;
+}
+
+// Zero the outputs of empty-K tasks (an empty sum).
+int zero_outputs(const Job *jobs, int njobs, int ncols, cudaStream_t s) {
+    for (int i = 0; i < njobs; ++i) {
+        const Job &j = jobs[i];
+        if (j.K != 0 || j.nrows == 0) continue;
+        for (int c = 0; c < ncols; ++c) {
+            cudaError_t e = cudaMemsetAsync(j.dst + c * j.stride_col_dst, 0, j.nrows * sizeof(float), s);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+        }
+    }
+    return Q4K_OK;
+}
+
+int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes, cudaStream_t s,
+        int32_t *dump_S = nullptr, int32_t *dump_T = nullptr) {
+    Plan P;
+    // Arguments are validated before the device is touched.
+    int st = make_plan(jobs, njobs, ncols, nullptr, kFallbackSMs, P);
+    if (st != Q4K_OK) return st;
+    int num_sms = 0;
+    cudaError_t e = device_setup(&num_sms);
+    if (e != cudaSuccess) return cuda_fail(e, "device setup");
+    st = make_plan(jobs, njobs, ncols, nullptr, num_sms, P);
+    if (st != Q4K_OK) return st;
+    st = zero_outputs(jobs, njobs, ncols, s);
+    if (st != Q4K_OK) return st;
+    if (!P.any_work) return Q4K_OK;
+    if (workspace == nullptr) return fail(Q4K_EWORKSPACE, "workspace is null");
+    if (!aligned16(workspace)) return fail(Q4K_EWORKSPACE, "workspace is not 16-byte aligned");
+    if (ws_bytes < P.layout.total)
+        return fail(Q4K_EWORKSPACE, "workspace of %zu bytes < %zu required", ws_bytes, P.layout.total);
+    st = make_plan(jobs, njobs, ncols, static_cast<uint8_t *>(workspace), num_sms, P, dump_T);
+    if (st != Q4K_OK) return st;
+    P.gemv.dump_S = dump_S;
+    if ((e = launch_prep(P.prep, s)) != cudaSuccess) return cuda_fail(e, "prep launch");
+    if ((e = launch_gemv(P.gemv, ncols, dump_S != nullptr, num_sms, s)) != cudaSuccess)
+        return cuda_fail(e, "gemv launch");
+    return Q4K_OK;
+}
+
+size_t plan_bytes(const Job *jobs, int njobs, int ncols) {
+    Plan P;
+    if (make_plan(jobs, njobs, ncols, nullptr, num_sms_or_bound(), P) != Q4K_OK) return 0;
+    return P.layout.total;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *q4k_status_string(int status) {
+    switch (status) {
+        case Q4K_OK: return "Q4K_OK";
+        case Q4K_EINVAL: return "Q4K_EINVAL";
+        case Q4K_ECUDA: return "Q4K_ECUDA";
+        case Q4K_ETIMEOUT: return "Q4K_ETIMEOUT";
+        case Q4K_ENCCL: return "Q4K_ENCCL";
+        case Q4K_EWORKSPACE: return "Q4K_EWORKSPACE";
+        default: return "Q4K_UNKNOWN";
+    }
+}
+
+const char *q4k_last_error(void) { return g_last_error.c_str(); }
+
+int q4k_version(void) { return 100; }
+
+int q4k_device_supported(void) {
+    int dev = 0, major = 0, minor = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return 0; }
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return major == 10 && minor == 0;
+}
+
+size_t q4k_row_bytes(int64_t K) {
+    if (K < 0 || K % Q4K_QK_K) return 0;
+    return static_cast<size_t>(K / Q4K_QK_K) * Q4K_BLOCK_BYTES;
+}
+
+size_t q4k_q8_1_bytes(int64_t Kpad, int ncols) {
+    if (Kpad < 0 || Kpad % Q4K_QK8_1 || ncols < 0) return 0;
+    return static_cast<size_t>(Kpad / Q4K_QK8_1) * Q8_1_BLOCK_BYTES * ncols;
+}
+
+size_t q4k_gemv_workspace_bytes(int64_t nrows, int64_t K, int ncols) {
+    static const float dummy = 0.0f;
+    static float dummy_out = 0.0f;
+    Job j{reinterpret_cast<const void *>(uintptr_t(256)), &dummy, &dummy_out, nrows, K, K / Q4K_QK_K,
+          K, nrows, kPrepF32};
+    return plan_bytes(&j, 1, ncols);
+}
+
+size_t q4k_batch_workspace_bytes(const q4k_task *tasks, int ntasks, int ncols) {
+    if (!tasks || ntasks < 1 || ntasks > kMaxTasks) return 0;
+    Job jobs[kMaxTasks];
+    for (int i = 0; i < ntasks; ++i)
+        jobs[i] = {tasks[i].W, tasks[i].x, tasks[i].dst, tasks[i].nrows, tasks[i].K,
+                   tasks[i].stride_row_x, tasks[i].stride_col_x, tasks[i].stride_col_dst, kPrepF32};
+    return plan_bytes(jobs, ntasks, ncols);
+}
+
+int q4k_quantize_q8_1(const float *x, int64_t K, int64_t stride_col_x, int64_t Kpad, int ncols,
+                      void *y_q8_1, q4k_stream_t stream) {
+    if (ncols < 1 || ncols > Q4K_MAX_NCOLS) return fail(Q4K_EINVAL, "ncols=%d outside 1..8", ncols);
+    if (K < 0 || Kpad < K || Kpad % Q4K_QK8_1 || Kpad > (int64_t(1) << 30))
+        return fail(Q4K_EINVAL, "need 0 <= K <= Kpad, Kpad %% 32 == 0 (K=%lld Kpad=%lld)", (long long)K,
+                    (long long)Kpad);
+    if (Kpad == 0) return Q4K_OK;
+    if (!y_q8_1 || (K > 0 && !x)) return fail(Q4K_EINVAL, "null pointer");
+    if (ncols > 1 && stride_col_x < K) return fail(Q4K_EINVAL, "stride_col_x < K");
+    int num_sms = 0;
+    cudaError_t e = device_setup(&num_sms);
+    if (e != cudaSuccess) return cuda_fail(e, "device setup");
+    PrepParams p{};
+    PrepJob &J = p.job[0];
+    J.src = x;
+    J.act = nullptr;
+    J.q81_out = static_cast<uint8_t *>(y_q8_1);
+    J.dump_T = nullptr;
+    J.src_col_stride = stride_col_x;
+    J.q81_col_stride = Kpad / Q4K_QK8_1;
+    J.item_base = 0;
+    J.K = static_cast<int32_t>(K);
+    J.nblk = static_cast<int32_t>(Kpad / Q4K_QK8_1);
+    J.ncols = ncols;
+    J.kind = kPrepF32;
+    p.njobs = 1;
+    p.nitems = static_cast<int64_t>(ncols) * J.nblk;
+    p.zero_ptr = nullptr;
+    p.zero_count = 0;
+    if ((e = launch_prep(p, reinterpret_cast<cudaStream_t>(stream))) != cudaSuccess)
+        return cuda_fail(e, "quantize launch");
+    return Q4K_OK;
+}
+
+int q4k_mul_mat_vec_q8_1(const void *W, const void *y_q8_1, float *dst, int64_t K, int64_t nrows, int ncols,
+                         int64_t stride_row_x, int64_t stride_col_y, int64_t stride_col_dst, void *workspace,
+                         size_t workspace_bytes, q4k_stream_t stream) {
+    Job j{W, y_q8_1, dst, nrows, K, stride_row_x, stride_col_y, stride_col_dst, kPrepQ81};
+    return run(&j, 1, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int q4k_mul_mat_vec(const void *W, const float *x, float *dst, int64_t K, int64_t nrows, int ncols,
+                    int64_t stride_row_x, int64_t stride_col_x, int64_t stride_col_dst, void *workspace,
+                    size_t workspace_bytes, q4k_stream_t stream) {
+    Job j{W, x, dst, nrows, K, stride_row_x, stride_col_x, stride_col_dst, kPrepF32};
+    return run(&j, 1, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int q4k_op_mul_mat_vec_q(const void *W_slice, int64_t K, const void *y_q8_1, float *dst_slice, int64_t row_low,
+                         int64_t row_high, int64_t src1_ncols, int64_t src1_padded_row_size, int64_t nrows_dst,
+                         void *workspace, size_t workspace_bytes, q4k_stream_t stream) {
+    if (row_high < row_low) return fail(Q4K_EINVAL, "row_high < row_low");
+    if (src1_padded_row_size < K || src1_padded_row_size % Q4K_QK8_1)
+        return fail(Q4K_EINVAL, "src1_padded_row_size must be >= K and a multiple of 32");
+    if (src1_ncols < 1 || src1_ncols > Q4K_MAX_NCOLS)
+        return fail(Q4K_EINVAL, "src1_ncols=%lld outside 1..8", (long long)src1_ncols);
+    const int64_t rows = row_high - row_low;
+    if (nrows_dst < rows) return fail(Q4K_EINVAL, "nrows_dst < row_high - row_low");
+    Job j{W_slice, y_q8_1, dst_slice, rows, K, K / Q4K_QK_K, src1_padded_row_size / Q4K_QK8_1, nrows_dst,
+          kPrepQ81};
+    return run(&j, 1, static_cast<int>(src1_ncols), workspace, workspace_bytes,
+               reinterpret_cast<cudaStream_t>(stream));
+}
+
+int q4k_custom_q4k_gemv(const void *vx, const void *vy, float *dst, int num_blocks_total, int stride_col_y_blocks,
+                        int stride_col_dst, int ncols_dst, void *workspace, size_t workspace_bytes,
+                        q4k_stream_t stream) {
+    if (num_blocks_total < 0) return fail(Q4K_EINVAL, "num_blocks_total < 0");
+    Job j{vx, vy, dst, stride_col_dst, static_cast<int64_t>(num_blocks_total) * Q4K_QK_K, num_blocks_total,
+          stride_col_y_blocks, stride_col_dst, kPrepQ81};
+    return run(&j, 1, ncols_dst, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int q4k_gemv_batch(const q4k_task *tasks, int ntasks, int ncols, void *workspace, size_t workspace_bytes,
+                   q4k_stream_t stream) {
+    if (!tasks || ntasks < 1 || ntasks > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..16", ntasks);
+    Job jobs[kMaxTasks];
+    for (int i = 0; i < ntasks; ++i)
+        jobs[i] = {tasks[i].W, tasks[i].x, tasks[i].dst, tasks[i].nrows, tasks[i].K,
+                   tasks[i].stride_row_x, tasks[i].stride_col_x, tasks[i].stride_col_dst, kPrepF32};
+    return run(jobs, ntasks, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int q4k_debug_subblock_sums(const void *W, const void *y_q8_1, int64_t K, int64_t nrows, int ncols,
+                            int64_t stride_row_x, int64_t stride_col_y, int32_t *S_out, int32_t *T_out,
+                            void *workspace, size_t workspace_bytes, q4k_stream_t stream) {
+    if (!S_out || !T_out) return fail(Q4K_EINVAL, "null S_out/T_out");
+    float *dummy_dst = reinterpret_cast<float *>(S_out);  // never written in dump mode
+    Job j{W, y_q8_1, dummy_dst, nrows, K, stride_row_x, stride_col_y, nrows, kPrepQ81};
+    if (K == 0 || nrows == 0) return validate_job(j, ncols, 0);
+    return run(&j, 1, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), S_out, T_out);
+}
+
+int q4k_workspace_status(const void *workspace, int *device_status, q4k_stream_t stream) {
+    if (!workspace || !device_status) return fail(Q4K_EINVAL, "null pointer");
+    int32_t v = 0;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "status read");
+    *device_status = v;
+    return Q4K_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,94 @@
+// q4k_internal.h -- launch parameters shared by the host runtime and the kernels.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace q4k {
+
+constexpr int kQK = 256;          // weights per super-block
+constexpr int kSBBytes = 144;     // bytes per super-block
+constexpr int kQ81Bytes = 36;     // bytes per q8_1 block
+constexpr int kActSBBytes = 320;  // q8a bytes per super-block and column
+constexpr int kActMetaOff = 256;  // q8a: offset of the per-pair float4 metadata
+constexpr int kMaxCols = 8;
+constexpr int kMaxTasks = 16;
+constexpr int kMaxJobs = 16;
+
+// GEMV geometry.  A "worker" is one warp; it owns a contiguous range of
+// "atoms" (32 weight rows x kKS super-blocks) of the flattened work of all
+// tasks, streamed through a private kStages-deep ring of shared-memory stages
+// by bulk asynchronous copies.  Lane = weight row.
+constexpr int kWarps = 8;
+constexpr int kStages = 2;
+constexpr int kKS = 2;                                // super-blocks per atom and row
+constexpr int kPitch = kKS * 144 + 16;                // smem bytes per row (odd multiple of 16)
+constexpr int kStageBytes = 32 * kPitch;
+constexpr int kSmemBytes = kWarps * kStages * kStageBytes;
+static_assert((kPitch / 16) % 2 == 1, "row pitch must be an odd number of 16-byte units");
+
+// Device status codes (match q4k_status).
+constexpr int kStatusOk = 0;
+constexpr int kStatusTimeout = 3;
+// Bounded waits: a bulk copy that has not landed after this long is an error.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr unsigned long long kDrainLimitNs = 20000000ull;   // 20 ms
+
+struct TaskDesc {
+    const uint8_t *W;        // weight row 0 (16-byte aligned)
+    const uint8_t *act;      // q8a column 0
+    float *dst;              // output column 0
+    int64_t row_stride;      // bytes between weight rows
+    int64_t act_col_stride;  // bytes between q8a columns
+    int64_t dst_col_stride;  // floats between output columns
+    int64_t atom_base;       // first global atom of this task
+    int32_t nrows;
+    int32_t nb;              // super-blocks per row
+    int32_t apr;             // atoms per row group = ceil(nb / kKS)
+    int32_t rg_base;         // global row-group index of row group 0
+};
+
+struct GemvParams {
+    TaskDesc task[kMaxTasks];
+    int32_t ntasks;
+    int32_t nworkers;        // active workers (<= gridDim.x * kWarps, <= natoms)
+    int64_t natoms;
+    int32_t *counters;       // one per global row group, zero at kernel start
+    float *partials;         // [nworkers][2][ncols][32]
+    int32_t *status;
+    int32_t *dump_S;         // debug: sub-block sums (nullptr in the product path)
+};
+
+enum PrepKind : int32_t { kPrepF32 = 0, kPrepQ81 = 1 };
+
+struct PrepJob {
+    const void *src;         // fp32 columns or ggml q8_1 columns
+    uint8_t *act;            // q8a output (nullptr: none)
+    uint8_t *q81_out;        // ggml q8_1 output (nullptr: none)
+    int32_t *dump_T;         // debug: T per (column, block) (nullptr: none)
+    int64_t src_col_stride;  // floats (fp32) or blocks (q8_1)
+    int64_t act_col_stride;  // bytes
+    int64_t q81_col_stride;  // blocks
+    int64_t item_base;       // first global warp item of this job
+    int32_t K;               // valid activations per column
+    int32_t nblk;            // q8 blocks per column to produce
+    int32_t ncols;
+    int32_t kind;
+};
+
+struct PrepParams {
+    PrepJob job[kMaxJobs];
+    int32_t njobs;
+    int32_t zero_count;      // int32 words to clear at zero_ptr (counters, status)
+    int64_t nitems;
+    int32_t *zero_ptr;
+};
+
+// Launchers (q4k_kernels.cu).  Return cudaSuccess or the launch error.
+cudaError_t launch_prep(const PrepParams &p, cudaStream_t s);
+cudaError_t launch_gemv(const GemvParams &p, int ncols, bool dump, int grid, cudaStream_t s);
+// Per-device setup (SM count, shared-memory opt-in); thread-safe, idempotent.
+cudaError_t device_setup(int *num_sms);
+
+}  // namespace q4k

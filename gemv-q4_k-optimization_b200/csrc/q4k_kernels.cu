@@ -1,0 +1,454 @@
+// q4k_kernels.cu -- sm_100a kernels of the Q4_K x q8_1 decode GEMV.
+//
+//   k_prep  : fp32 -> q8_1 quantization (and/or ggml q8_1 -> q8a repack) of
+//             every activation column of the call, one warp per 32-value
+//             block; also clears the GEMV's split counters.  It triggers the
+//             dependent GEMV launch immediately, so the GEMV's weight stream
+//             starts while the activations are being quantized.
+//   k_gemv  : persistent GEMV over a list of matrices ("tasks").  Each warp
+//             owns an equal share of the flattened weight stream and pulls it
+//             into shared memory with bulk asynchronous copies (one per row
+//             segment, issued by the 32 lanes at once), then lane r computes
+//             row r of its 32-row group.  Row groups split between warps are
+//             completed by whichever contributor finishes last (atomic
+//             counter, fixed summation order, no waiting).
+//
+// Semantics restated from the reference (paths relative to the reference
+// project):
+//   q8_1 quantization: the call at kernels/mmvq.cu:734 (upstream
+//     quantize_q8_1, not vendored: d = amax/127, q = roundf(x/d)).
+//   super-block dot: kernels/vecdotq.cuh:775-819 (nibble/q8 pairing, 6-bit
+//     scale/min unpacking) and :461-483 (d*sum d8*sc*S - dmin*sum d8*m*T).
+//   row/column strides and output layout: kernels/mmvq.cu:233-247, :285, :337.
+#include "q4k_device.cuh"
+#include "q4k_internal.h"
+
+#include <mutex>
+
+namespace q4k {
+
+// ============================================================================
+// prep: quantize / repack activations, clear counters
+// ============================================================================
+__global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams P) {
+    // Let the dependent GEMV grid launch now: it only issues weight copies
+    // before its griddepcontrol.wait, which returns after this grid completes.
+    pdl_launch_dependents();
+
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = tid; i < P.zero_count; i += nthr) P.zero_ptr[i] = 0;
+
+    const int lane = threadIdx.x & 31;
+    const int64_t wid = tid >> 5, nw = nthr >> 5;
+    for (int64_t item = wid; item < P.nitems; item += nw) {
+        int j = 0;
+        while (j + 1 < P.njobs && item >= P.job[j + 1].item_base) ++j;
+        const PrepJob &J = P.job[j];
+        const int64_t local = item - J.item_base;
+        const int col = static_cast<int>(local / J.nblk);
+        const int b = static_cast<int>(local - static_cast<int64_t>(col) * J.nblk);
+        const int pos = b * 32 + lane;
+
+        int q;
+        __half dh;
+        if (J.kind == kPrepF32) {
+            const float *xc = static_cast<const float *>(J.src) + col * J.src_col_stride;
+            const float x = pos < J.K ? xc[pos] : 0.0f;
+            const float amax = warp_max_f32(fabsf(x));
+            const float d = amax / 127.0f;  // IEEE division (no fast-math in this build)
+            q = amax == 0.0f ? 0 : static_cast<int>(roundf(x / d));
+            dh = __float2half_rn(d);
+            if (J.q81_out != nullptr) {
+                const float sum = warp_sum_f32(x);
+                uint8_t *blk = J.q81_out + (col * J.q81_col_stride + b) * kQ81Bytes;
+                blk[4 + lane] = static_cast<uint8_t>(static_cast<int8_t>(q));
+                if (lane == 0) {
+                    *reinterpret_cast<__half2 *>(blk) = __halves2half2(dh, __float2half_rn(sum));
+                }
+            }
+        } else {
+            const uint8_t *blk = static_cast<const uint8_t *>(J.src) +
+                                 (col * J.src_col_stride + b) * kQ81Bytes;
+            q = static_cast<int8_t>(blk[4 + lane]);
+            dh = *reinterpret_cast<const __half *>(blk);
+        }
+
+        if (J.act != nullptr && b * 32 < J.K) {
+            const int T = warp_sum_i32(q);
+            uint8_t *rec = J.act + col * J.act_col_stride + static_cast<int64_t>(b >> 3) * kActSBBytes;
+            const int s = b & 7;
+            rec[s * 32 + lane] = static_cast<uint8_t>(static_cast<int8_t>(q));
+            if (lane == 0) {
+                const float d8 = __half2float(dh);
+                float *meta = reinterpret_cast<float *>(rec + kActMetaOff + 16 * (s >> 1));
+                meta[s & 1] = (s & 1) ? d8 * 0.0625f : d8;
+                meta[2 + (s & 1)] = d8 * static_cast<float>(T);
+                if (J.dump_T != nullptr) J.dump_T[static_cast<int64_t>(col) * (J.K / 32) + b] = T;
+            }
+        }
+    }
+}
+
+// ============================================================================
+// GEMV
+// ============================================================================
+struct AtomPos {
+    int t;   // task
+    int g;   // row group within the task
+    int kp;  // atom within the row group
+};
+
+__device__ __forceinline__ AtomPos decode_atom(const GemvParams &P, int64_t a) {
+    int t = 0;
+    while (t + 1 < P.ntasks && a >= P.task[t + 1].atom_base) ++t;
+    const int64_t local = a - P.task[t].atom_base;
+    const int apr = P.task[t].apr;
+    AtomPos r;
+    r.t = t;
+    r.g = static_cast<int>(local / apr);
+    r.kp = static_cast<int>(local - static_cast<int64_t>(r.g) * apr);
+    return r;
+}
+
+// First atom of worker w under the uniform partition of natoms over nworkers.
+__device__ __forceinline__ int64_t worker_begin(const GemvParams &P, int64_t w) {
+    return P.natoms * w / P.nworkers;
+}
+// Worker whose range holds atom a.
+__device__ __forceinline__ int64_t worker_of(const GemvParams &P, int64_t a) {
+    return ((a + 1) * P.nworkers - 1) / P.natoms;
+}
+
+// Issue the bulk copies of atom a into a ring stage: lane r copies row r's
+// kKS-super-block segment; lane 0 first announces the byte count.
+__device__ __forceinline__ void issue_atom(const GemvParams &P, int64_t a, uint32_t stage,
+                                           uint32_t bar, int lane) {
+    const AtomPos ap = decode_atom(P, a);
+    const TaskDesc &T = P.task[ap.t];
+    const int rows = min(32, T.nrows - ap.g * 32);
+    const int kb0 = ap.kp * kKS;
+    const int nsb = min(kKS, T.nb - kb0);
+    const uint32_t seg = static_cast<uint32_t>(nsb * kSBBytes);
+    if (lane == 0) mbar_expect_tx(bar, static_cast<uint32_t>(rows) * seg);
+    __syncwarp();
+    if (lane < rows) {
+        const uint8_t *src = T.W + static_cast<int64_t>(ap.g * 32 + lane) * T.row_stride +
+                             static_cast<int64_t>(kb0) * kSBBytes;
+        bulk_g2s(stage + lane * kPitch, src, seg, bar);
+    }
+}
+
+// Bounded wait on an mbarrier phase.  false after `limit_ns` without completion.
+__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+    }
+}
+
+// One super-block of one row (smem at p) against the q8a records of all NC
+// columns.  acc[j] holds a packed pair of partial sums for column j.
+template <int NC, bool DUMP>
+__device__ __forceinline__ void sb_dot(uint32_t p, const uint8_t *act, int64_t acs, uint64_t (&acc)[NC],
+                                       int32_t *dumpS) {
+    const uint4 h = lds128(p);
+    const float2 dm = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
+    const float d = dm.x, dmin = dm.y;
+    // 6-bit scales sc0..7 and mins m0..7, four per word (vecdotq.cuh:796-807).
+    const uint32_t sc03 = h.y & 0x3F3F3F3Fu;
+    const uint32_t m03 = h.z & 0x3F3F3F3Fu;
+    const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    const uint32_t m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    // (byte + 2^23) * x - 2^23 * x == byte * x exactly (one rounding).
+    const float nd23 = -8388608.0f * d;
+    const float pm23 = 8388608.0f * dmin;
+    const uint64_t magic2 = f2_pack(-kMagicF, -kMagicF);
+
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t scw = c < 2 ? sc03 : sc47;
+        const uint32_t mw = c < 2 ? m03 : m47;
+        const int b0 = (c & 1) * 2;
+        // d*sc and -dmin*m for sub-blocks 2c, 2c+1
+        const uint64_t dsc = f2_pack(fmaf(byte_magic(scw, b0), d, nd23), fmaf(byte_magic(scw, b0 + 1), d, nd23));
+        const uint64_t ndm = f2_pack(fmaf(byte_magic(mw, b0), -dmin, pm23), fmaf(byte_magic(mw, b0 + 1), -dmin, pm23));
+        const uint4 wa = lds128(p + 16 + 32 * c);
+        const uint4 wb = lds128(p + 32 + 32 * c);
+        const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        uint32_t lo[8], hi[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            lo[k] = w[k] & 0x0F0F0F0Fu;
+            hi[k] = w[k] & 0xF0F0F0F0u;  // 16 x nibble, unsigned bytes
+        }
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+            const uint8_t *aj = act + j * acs;
+            const uint4 qe0 = ldg_nc128(aj + 64 * c);
+            const uint4 qe1 = ldg_nc128(aj + 64 * c + 16);
+            const uint4 qo0 = ldg_nc128(aj + 64 * c + 32);
+            const uint4 qo1 = ldg_nc128(aj + 64 * c + 48);
+            const uint4 meta = ldg_nc128(aj + kActMetaOff + 16 * c);
+            const uint32_t qe[8] = {qe0.x, qe0.y, qe0.z, qe0.w, qe1.x, qe1.y, qe1.z, qe1.w};
+            const uint32_t qo[8] = {qo0.x, qo0.y, qo0.z, qo0.w, qo1.x, qo1.y, qo1.z, qo1.w};
+            int se = kMagicI, so = kMagicI;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                se = dp4a_us(lo[k], qe[k], se);
+                so = dp4a_us(hi[k], qo[k], so);
+            }
+            if constexpr (DUMP) {
+                // Called with NC == 1 per column: the exact sub-block sums
+                // (the odd one was formed on 16 x nibble).
+                dumpS[2 * c] = se - kMagicI;
+                dumpS[2 * c + 1] = (so - kMagicI) >> 4;
+            }
+            const uint64_t sf = f2_add(f2_pack(__int_as_float(se), __int_as_float(so)), magic2);
+            const uint64_t g = f2_mul(sf, f2_pack(__uint_as_float(meta.x), __uint_as_float(meta.y)));
+            acc[j] = f2_fma(g, dsc, acc[j]);
+            acc[j] = f2_fma(f2_pack(__uint_as_float(meta.z), __uint_as_float(meta.w)), ndm, acc[j]);
+        }
+    }
+}
+
+template <int NC, bool DUMP>
+__device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomPos &ap, uint32_t stage, int lane,
+                                             uint64_t (&acc)[NC]) {
+    const TaskDesc &T = P.task[ap.t];
+    const int rows = min(32, T.nrows - ap.g * 32);
+    const int kb0 = ap.kp * kKS;
+    const int nsb = min(kKS, T.nb - kb0);
+    if (lane >= rows) return;
+#pragma unroll 1
+    for (int i = 0; i < kKS; ++i) {
+        if (i < nsb) {
+            const int kb = kb0 + i;
+            if constexpr (DUMP) {
+                // Per-column dump of this row's 8 sub-block sums.
+#pragma unroll
+                for (int j = 0; j < NC; ++j) {
+                    uint64_t one[1] = {acc[j]};
+                    int32_t *dS = P.dump_S + (static_cast<int64_t>(j) * T.nrows + ap.g * 32 + lane) *
+                                                 (static_cast<int64_t>(T.nb) * 8) + kb * 8;
+                    sb_dot<1, true>(stage + lane * kPitch + i * kSBBytes, T.act + static_cast<int64_t>(kb) * kActSBBytes +
+                                        j * T.act_col_stride, 0, one, dS);
+                    acc[j] = one[0];
+                }
+            } else {
+                sb_dot<NC, false>(stage + lane * kPitch + i * kSBBytes,
+                                  T.act + static_cast<int64_t>(kb) * kActSBBytes, T.act_col_stride, acc, nullptr);
+            }
+        }
+    }
+}
+
+// Finish a row group this warp worked on: write it out directly if the warp
+// covered all of its atoms, otherwise deposit the partial sums and let the
+// last of the contributing warps add them up (in worker order) and write.
+template <int NC, bool DUMP>
+__device__ __forceinline__ void flush_group(const GemvParams &P, const AtomPos &cur, uint64_t (&acc)[NC],
+                                            int64_t worker, int64_t a0, int64_t a1, int lane) {
+    const TaskDesc &T = P.task[cur.t];
+    float v[NC];
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+        const float2 p = f2_unpack(acc[j]);
+        v[j] = p.x + p.y;
+    }
+    const int64_t sg = T.atom_base + static_cast<int64_t>(cur.g) * T.apr;
+    const int64_t eg = sg + T.apr;
+    const int row = cur.g * 32 + lane;
+    const bool valid = row < T.nrows;
+    if (sg >= a0 && eg <= a1) {
+        if (!DUMP && valid) {
+#pragma unroll
+            for (int j = 0; j < NC; ++j) T.dst[j * T.dst_col_stride + row] = v[j];
+        }
+        return;
+    }
+    const int slot = (a0 > sg) ? 0 : 1;  // 0: group began before this worker, 1: it covers the start
+    float *mine = P.partials + ((worker * 2 + slot) * NC) * 32;
+#pragma unroll
+    for (int j = 0; j < NC; ++j) mine[j * 32 + lane] = v[j];
+    __threadfence();
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) old = atomicAdd(&P.counters[T.rg_base + cur.g], 1);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    const int64_t w1 = worker_of(P, sg), w2 = worker_of(P, eg - 1);
+    if (old != static_cast<int>(w2 - w1)) return;  // not the last contributor
+    __threadfence();
+    float tot[NC];
+#pragma unroll
+    for (int j = 0; j < NC; ++j) tot[j] = 0.0f;
+    for (int64_t w = w1; w <= w2; ++w) {
+        const float *src = P.partials + ((w * 2 + (w == w1 ? 1 : 0)) * NC) * 32;
+#pragma unroll
+        for (int j = 0; j < NC; ++j) tot[j] += ldcg_f32(src + j * 32 + lane);
+    }
+    if (!DUMP && valid) {
+#pragma unroll
+        for (int j = 0; j < NC; ++j) T.dst[j * T.dst_col_stride + row] = tot[j];
+    }
+    if (lane == 0) P.counters[T.rg_base + cur.g] = 0;
+}
+
+template <int NC, bool DUMP>
+__global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bars[kWarps][kStages];
+
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    // Consecutive workers sit on different SMs, so small problems spread out.
+    const int64_t worker = static_cast<int64_t>(warp) * gridDim.x + blockIdx.x;
+    if (worker >= P.nworkers) return;
+    const int64_t a0 = worker_begin(P, worker);
+    const int64_t a1 = worker_begin(P, worker + 1);
+    const int64_t n = a1 - a0;
+
+    const uint32_t ring = smem_addr(smem) + static_cast<uint32_t>(warp * kStages * kStageBytes);
+    uint32_t bar[kStages];
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) bar[s] = smem_addr(&bars[warp][s]);
+    if (lane == 0) {
+#pragma unroll
+        for (int s = 0; s < kStages; ++s) mbar_init(bar[s], 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+
+    // Weight bytes do not depend on the prep kernel: start streaming now.
+#pragma unroll
+    for (int s = 0; s < kStages; ++s)
+        if (s < n) issue_atom(P, a0 + s, ring + s * kStageBytes, bar[s], lane);
+
+    pdl_wait();  // activations and cleared counters are visible after this
+
+    uint64_t acc[NC];
+#pragma unroll
+    for (int j = 0; j < NC; ++j) acc[j] = 0ull;
+    AtomPos cur{-1, -1, 0};
+
+    for (int64_t i = 0; i < n; ++i) {
+        const int s = static_cast<int>(i % kStages);
+        const uint32_t parity = static_cast<uint32_t>((i / kStages) & 1);
+        const AtomPos ap = decode_atom(P, a0 + i);
+        if (ap.t != cur.t || ap.g != cur.g) {
+            if (cur.t >= 0) flush_group<NC, DUMP>(P, cur, acc, worker, a0, a1, lane);
+            cur = ap;
+#pragma unroll
+            for (int j = 0; j < NC; ++j) acc[j] = 0ull;
+        }
+        if (!wait_phase(bar[s], parity, kWaitLimitNs)) {
+            if (lane == 0) atomicExch(P.status, kStatusTimeout);
+            // Let this warp's other copies in flight land (bounded) before leaving.
+            for (int k = 1; k < kStages; ++k) {
+                const int64_t ii = i + k;
+                if (ii < n) wait_phase(bar[ii % kStages], static_cast<uint32_t>((ii / kStages) & 1), kDrainLimitNs);
+            }
+            return;
+        }
+        compute_atom<NC, DUMP>(P, ap, ring + s * kStageBytes, lane, acc);
+        __syncwarp();
+        if (i + kStages < n) {
+            fence_proxy_async_smem();
+            issue_atom(P, a0 + i + kStages, ring + s * kStageBytes, bar[s], lane);
+        }
+    }
+    if (cur.t >= 0) flush_group<NC, DUMP>(P, cur, acc, worker, a0, a1, lane);
+}
+
+// ============================================================================
+// host-side launchers
+// ============================================================================
+namespace {
+std::mutex g_setup_mu;
+struct DevState {
+    bool ready = false;
+    int num_sms = 0;
+};
+DevState g_dev[64];
+
+template <int NC, bool DUMP>
+cudaError_t set_attrs() {
+    return cudaFuncSetAttribute(k_gemv<NC, DUMP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+}
+
+template <bool DUMP>
+cudaError_t set_attrs_all() {
+    cudaError_t e;
+    if ((e = set_attrs<1, DUMP>()) != cudaSuccess) return e;
+    if ((e = set_attrs<2, DUMP>()) != cudaSuccess) return e;
+    if ((e = set_attrs<3, DUMP>()) != cudaSuccess) return e;
+    if ((e = set_attrs<4, DUMP>()) != cudaSuccess) return e;
+    if ((e = set_attrs<5, DUMP>()) != cudaSuccess) return e;
+    if ((e = set_attrs<6, DUMP>()) != cudaSuccess) return e;
+    if ((e = set_attrs<7, DUMP>()) != cudaSuccess) return e;
+    return set_attrs<8, DUMP>();
+}
+
+template <bool DUMP>
+void *gemv_fn(int ncols) {
+    switch (ncols) {
+        case 1: return reinterpret_cast<void *>(k_gemv<1, DUMP>);
+        case 2: return reinterpret_cast<void *>(k_gemv<2, DUMP>);
+        case 3: return reinterpret_cast<void *>(k_gemv<3, DUMP>);
+        case 4: return reinterpret_cast<void *>(k_gemv<4, DUMP>);
+        case 5: return reinterpret_cast<void *>(k_gemv<5, DUMP>);
+        case 6: return reinterpret_cast<void *>(k_gemv<6, DUMP>);
+        case 7: return reinterpret_cast<void *>(k_gemv<7, DUMP>);
+        case 8: return reinterpret_cast<void *>(k_gemv<8, DUMP>);
+        default: return nullptr;
+    }
+}
+}  // namespace
+
+cudaError_t device_setup(int *num_sms) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_setup_mu);
+    DevState &st = g_dev[dev];
+    if (!st.ready) {
+        if ((e = cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+        if ((e = set_attrs_all<false>()) != cudaSuccess) return e;
+        if ((e = set_attrs_all<true>()) != cudaSuccess) return e;
+        st.ready = true;
+    }
+    *num_sms = st.num_sms;
+    return cudaSuccess;
+}
+
+cudaError_t launch_prep(const PrepParams &p, cudaStream_t s) {
+    int64_t blocks = (p.nitems * 32 + 255) / 256;
+    const int64_t zb = (p.zero_count + 255) / 256;
+    if (zb > blocks) blocks = zb;
+    if (blocks < 1) blocks = 1;
+    if (blocks > 4096) blocks = 4096;
+    k_prep<<<static_cast<unsigned>(blocks), 256, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemv(const GemvParams &p, int ncols, bool dump, int grid, cudaStream_t s) {
+    void *fn = dump ? gemv_fn<true>(ncols) : gemv_fn<false>(ncols);
+    if (fn == nullptr) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *args[] = {const_cast<GemvParams *>(&p)};
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace q4k

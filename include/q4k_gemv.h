@@ -1,0 +1,182 @@
+/*
+ * q4k_gemv.h -- C ABI of the B200 (sm_100a) Q4_K x q8_1 decode GEMV library
+ * (libq4k_gemv.so).
+ *
+ * Drop-in boundary for the Q4_K branch of llama.cpp's ggml-cuda mul_mat_vec_q
+ * dispatch as the reference wires it.  Reference interfaces replaced
+ * (paths relative to the reference project, vijay-kodamalla/gemv-q4_k-optimization):
+ *
+ *   kernels/mmvq.cu:479-486, :536-593  mul_mat_vec_q_switch_type, Q4_K case
+ *                                      -> q4k_mul_mat_vec_q8_1()
+ *   kernels/mmvq.cu:10-18, :563-584    custom_q4k_gemv<...> launch (6 args)
+ *                                      -> q4k_custom_q4k_gemv()
+ *   kernels/mmvq.cu:666-762            ggml_cuda_mul_mat_vec_q (fp32 src1:
+ *                                      quantize, then GEMV)  -> q4k_mul_mat_vec()
+ *   kernels/mmvq.cu:734                quantize_row_q8_1_cuda call
+ *                                      -> q4k_quantize_q8_1()
+ *   kernels/mmvq.cu:764-793            ggml_cuda_op_mul_mat_vec_q (row-split
+ *                                      slice per device) -> q4k_op_mul_mat_vec_q()
+ *
+ * Data formats (unchanged from ggml, so tensors pass through untouched):
+ *   Q4_K super-block, 144 bytes per 256 weights: half d, half dmin,
+ *     uint8 scales[12] (8 six-bit scales + 8 six-bit mins), uint8 qs[128].
+ *   q8_1 block, 36 bytes per 32 activations: half d, half sum, int8 qs[32].
+ * Weight row r of a matrix starts at W + r*stride_row_x*144 bytes; W must be
+ * 16-byte aligned (rows are streamed with bulk asynchronous copies).
+ * Column j of an fp32 activation starts at x + j*stride_col_x, of a q8_1
+ * activation at block j*stride_col_y, and of the output at
+ * dst + j*stride_col_dst (the column-major ggml dst layout, mmvq.cu:337).
+ *
+ * Conventions (differences from the reference, on purpose):
+ *   - every entry point returns a q4k_status instead of aborting the process
+ *     (the reference asserts: mmvq.cu:375, :393-394, :472-474, :669-686);
+ *   - all work is asynchronous on the caller's stream; the library never
+ *     synchronises and never allocates on the call path;
+ *   - the caller owns all memory, including the scratch "workspace" (it may
+ *     come from a pool and need not be initialised); one workspace must not
+ *     be used by two calls that can overlap on the GPU (e.g. two streams).
+ */
+#ifndef Q4K_GEMV_H
+#define Q4K_GEMV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define Q4K_API __attribute__((visibility("default")))
+#else
+#define Q4K_API
+#endif
+
+/* cudaStream_t without including the CUDA headers. */
+typedef struct CUstream_st *q4k_stream_t;
+
+#define Q4K_QK_K 256          /* weights per super-block */
+#define Q4K_BLOCK_BYTES 144   /* sizeof(block_q4_K)  (kernels/w_tile.cu:6) */
+#define Q4K_QK8_1 32          /* activations per q8_1 block */
+#define Q8_1_BLOCK_BYTES 36   /* sizeof(block_q8_1)  (kernels/w_tile.cu:7) */
+#define Q4K_ROW_PADDING 512   /* q8_1 row padding, MATRIX_ROW_PADDING (mmvq.cu:728) */
+#define Q4K_MAX_NCOLS 8       /* MMVQ_MAX_BATCH_SIZE (mmvq.cu:394) */
+#define Q4K_MAX_TASKS 16      /* matrices per q4k_gemv_batch launch */
+
+typedef enum q4k_status {
+    Q4K_OK = 0,
+    Q4K_EINVAL = 1,     /* bad shape, stride, alignment, ncols outside 1..8, K % 256 != 0 */
+    Q4K_ECUDA = 2,      /* a CUDA runtime call or launch failed (message via q4k_last_error) */
+    Q4K_ETIMEOUT = 3,   /* a bounded device-side wait expired (status word) */
+    Q4K_ENCCL = 4,      /* a collective failed */
+    Q4K_EWORKSPACE = 5  /* workspace missing, too small or misaligned */
+} q4k_status;
+
+/* Human-readable name of a status; detail of the last failure on this thread. */
+Q4K_API const char *q4k_status_string(int status);
+Q4K_API const char *q4k_last_error(void);
+
+/* Library version, and whether the CUDA device of the calling thread is
+ * supported (compute capability 10.0: the library is built for sm_100a only). */
+Q4K_API int q4k_version(void);
+Q4K_API int q4k_device_supported(void);
+
+/* ---- sizes ---------------------------------------------------------------- */
+
+/* Bytes of one Q4_K row of length K (K % 256 == 0). */
+Q4K_API size_t q4k_row_bytes(int64_t K);
+/* Bytes of ncols q8_1 activation columns of padded length Kpad (Kpad % 32 == 0). */
+Q4K_API size_t q4k_q8_1_bytes(int64_t Kpad, int ncols);
+/* Workspace bytes for one GEMV of nrows x K with ncols activation columns. */
+Q4K_API size_t q4k_gemv_workspace_bytes(int64_t nrows, int64_t K, int ncols);
+
+/* ---- q8_1 quantization ------------------------------------------------------ */
+
+/* fp32 -> ggml q8_1 blocks (the src1 quantization of mmvq.cu:728-735).
+ * Output column j starts at block j*(Kpad/32); positions K <= i < Kpad are
+ * zero padding.  Per block: d = amax/127, q = roundf(x/d), ds = (half d,
+ * half of the sum of x in xor-butterfly order). */
+Q4K_API int q4k_quantize_q8_1(const float *x, int64_t K, int64_t stride_col_x, int64_t Kpad,
+                      int ncols, void *y_q8_1, q4k_stream_t stream);
+
+/* ---- single GEMV ------------------------------------------------------------ */
+
+/* dst[j*stride_col_dst + r] = sum_k W[r,k] * q8_1 column j, r < nrows, j < ncols.
+ * Same arguments as the Q4_K case of mul_mat_vec_q_switch_type
+ * (mmvq.cu:479-486: vx, vy, dst, ncols_x = K, nrows_x, ncols_dst,
+ * stride_row_x, stride_col_y, stride_col_dst) plus the workspace. */
+Q4K_API int q4k_mul_mat_vec_q8_1(const void *W, const void *y_q8_1, float *dst,
+                         int64_t K, int64_t nrows, int ncols,
+                         int64_t stride_row_x, int64_t stride_col_y, int64_t stride_col_dst,
+                         void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+
+/* fp32 activations: the q8_1 quantization is fused into the GEMV launch
+ * sequence (ggml_cuda_mul_mat_vec_q, mmvq.cu:666-762, without ids/fusion). */
+Q4K_API int q4k_mul_mat_vec(const void *W, const float *x, float *dst,
+                    int64_t K, int64_t nrows, int ncols,
+                    int64_t stride_row_x, int64_t stride_col_x, int64_t stride_col_dst,
+                    void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+
+/* Row-split slice on one device (ggml_cuda_op_mul_mat_vec_q, mmvq.cu:764-793):
+ * W_slice holds rows [row_low, row_high) of a K-column Q4_K matrix, y_q8_1 is
+ * the already quantized src1 (src1_ncols columns, src1_padded_row_size
+ * values per column), dst_slice receives the slice with column stride
+ * nrows_dst. */
+Q4K_API int q4k_op_mul_mat_vec_q(const void *W_slice, int64_t K, const void *y_q8_1,
+                         float *dst_slice, int64_t row_low, int64_t row_high,
+                         int64_t src1_ncols, int64_t src1_padded_row_size, int64_t nrows_dst,
+                         void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+
+/* The custom kernel hook's launch contract (mmvq.cu:10-18, :548-584):
+ * num_blocks_total = super-blocks per row (the reference passes stride_row_x,
+ * mmvq.cu:548), stride_col_dst doubles as the row count (2rowCTA.cu:62),
+ * ncols_dst in 1..8 (the reference's hook stops at 4, mmvq.cu:541). */
+Q4K_API int q4k_custom_q4k_gemv(const void *vx, const void *vy, float *dst, int num_blocks_total,
+                        int stride_col_y_blocks, int stride_col_dst, int ncols_dst,
+                        void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+
+/* ---- persistent multi-matrix launch ----------------------------------------- */
+
+/* One matrix of a batched launch.  Tasks that name the same x (same pointer,
+ * K and stride) share one quantization. */
+typedef struct q4k_task {
+    const void *W;          /* nrows x K Q4_K, 16-byte aligned */
+    const float *x;         /* K x ncols fp32, column stride stride_col_x */
+    float *dst;             /* nrows x ncols fp32, column stride stride_col_dst */
+    int64_t nrows;
+    int64_t K;
+    int64_t stride_row_x;   /* super-blocks between rows (>= K/256) */
+    int64_t stride_col_x;   /* floats between activation columns (>= K) */
+    int64_t stride_col_dst; /* floats between output columns (>= nrows) */
+} q4k_task;
+
+/* Workspace bytes for q4k_gemv_batch over these tasks. */
+Q4K_API size_t q4k_batch_workspace_bytes(const q4k_task *tasks, int ntasks, int ncols);
+
+/* Every task's GEMV in one launch sequence: one quantization launch for all
+ * distinct activations, then one persistent GEMV launch whose warps stream the
+ * weight bytes of all tasks, balanced across the SMs. */
+Q4K_API int q4k_gemv_batch(const q4k_task *tasks, int ntasks, int ncols,
+                   void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+
+/* ---- diagnostics ------------------------------------------------------------- */
+
+/* Per-sub-block integer sums as the kernels form them, for bit-exact parity
+ * checks (the GEMV kernel runs in a dump mode and writes no dst):
+ *   S_out[(j*nrows + r)*(K/32) + b] = sum over sub-block b of row r of
+ *                                     nibble * q8 (column j),
+ *   T_out[j*(K/32) + b]             = sum of the 32 quants of q8_1 block b
+ *                                     of column j (the min-term sum). */
+Q4K_API int q4k_debug_subblock_sums(const void *W, const void *y_q8_1, int64_t K, int64_t nrows,
+                            int ncols, int64_t stride_row_x, int64_t stride_col_y,
+                            int32_t *S_out, int32_t *T_out,
+                            void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+
+/* Device status word of the last call that used this workspace (0 = OK,
+ * otherwise a q4k_status such as Q4K_ETIMEOUT).  Synchronises the stream. */
+Q4K_API int q4k_workspace_status(const void *workspace, int *device_status, q4k_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q4K_GEMV_H */

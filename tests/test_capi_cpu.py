@@ -1,0 +1,86 @@
+"""The C-ABI library without a GPU: it loads, exports every entry point the
+header declares, sizes buffers, and rejects bad arguments with Q4K_EINVAL
+before touching a device."""
+from __future__ import annotations
+
+import ctypes
+import subprocess
+
+import pytest
+
+EINVAL, EWORKSPACE = 1, 5
+
+
+def test_library_loads_and_exports_header_symbols(q4k):
+    L = q4k.lib()
+    declared = q4k.declared_symbols()
+    assert len(declared) >= 16
+    for name in declared:
+        assert hasattr(L, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(q4k.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    assert set(declared) <= exported
+    # nothing else of the library's internals leaks out
+    assert all(e.startswith("q4k_") for e in exported)
+
+
+def test_sizes(q4k):
+    L = q4k.lib()
+    assert L.q4k_row_bytes(4096) == 16 * 144
+    assert L.q4k_row_bytes(100) == 0
+    assert L.q4k_q8_1_bytes(4608, 3) == 4608 // 32 * 36 * 3
+    ws1 = q4k.gemv_workspace_bytes(4096, 4096, 1)
+    ws8 = q4k.gemv_workspace_bytes(4096, 4096, 8)
+    assert 0 < ws1 < ws8
+    assert ws8 >= 8 * 16 * 320  # the activation pack
+    assert L.q4k_version() >= 100
+    assert L.q4k_status_string(1) == b"Q4K_EINVAL"
+
+
+def _call(L, W=256, x=512, dst=1024, K=4096, nrows=8, ncols=1, srx=None, scx=None, scd=None, ws=4096,
+          wsb=1 << 30):
+    srx = K // 256 if srx is None else srx
+    scx = K if scx is None else scx
+    scd = nrows if scd is None else scd
+    return L.q4k_mul_mat_vec(W, x, dst, K, nrows, ncols, srx, scx, scd, ws, wsb, None)
+
+
+@pytest.mark.parametrize("kw", [
+    dict(K=100), dict(K=-256), dict(ncols=0), dict(ncols=9), dict(nrows=-1),
+    dict(W=258), dict(W=0), dict(x=0), dict(dst=0), dict(srx=15),
+    dict(ncols=2, scx=4000), dict(ncols=2, scd=4),
+])
+def test_invalid_arguments_rejected_without_gpu(q4k, kw):
+    L = q4k.lib()
+    assert _call(L, **kw) == EINVAL
+    assert len(L.q4k_last_error()) > 0
+
+
+def test_workspace_checks(q4k):
+    L = q4k.lib()
+    # size and alignment are checked after the device is known; without a GPU the
+    # call reports the CUDA failure instead, never a crash
+    st = _call(L, ws=0)
+    assert st in (EWORKSPACE, 2)
+
+
+def test_batch_rejects_bad_task_count(q4k):
+    L = q4k.lib()
+    tasks = (q4k.Task * 17)()
+    assert L.q4k_gemv_batch(tasks, 17, 1, None, 0, None) == EINVAL
+    assert L.q4k_gemv_batch(tasks, 0, 1, None, 0, None) == EINVAL
+
+
+def test_quantize_rejects_bad_padding(q4k):
+    L = q4k.lib()
+    assert L.q4k_quantize_q8_1(256, 100, 100, 96, 1, 512, None) == EINVAL   # Kpad < K
+    assert L.q4k_quantize_q8_1(256, 100, 100, 120, 1, 512, None) == EINVAL  # Kpad % 32
+    assert L.q4k_quantize_q8_1(256, 100, 100, 128, 9, 512, None) == EINVAL  # ncols
+
+
+def test_op_mul_mat_vec_q_rejects_bad_rows(q4k):
+    L = q4k.lib()
+    assert L.q4k_op_mul_mat_vec_q(256, 4096, 512, 1024, 10, 5, 1, 4096, 16, None, 0, None) == EINVAL
+    assert L.q4k_op_mul_mat_vec_q(256, 4096, 512, 1024, 0, 32, 1, 4096, 16, None, 0, None) == EINVAL
+    assert L.q4k_op_mul_mat_vec_q(256, 4096, 512, 1024, 0, 8, 1, 4000, 16, None, 0, None) == EINVAL
