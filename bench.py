@@ -84,13 +84,13 @@ def shard(rows: int, rank: int, world: int):
     return lo, min(rows, lo + per), per
 
 
-def step_bytes(ncols: int, world: int = 1) -> dict:
+def step_bytes(ncols: int, world: int = 1, layers: int = LAYERS) -> dict:
     """Algorithmic bytes of one decode step, whole job (all ranks)."""
-    w = sum(r * K * 9 // 16 for _, r, K, _ in MATS) * LAYERS + HEAD[0] * HEAD[1] * 9 // 16
+    w = sum(r * K * 9 // 16 for _, r, K, _ in MATS) * layers + HEAD[0] * HEAD[1] * 9 // 16
     x_layer = sum(ncols * K * 4 for K in ACT_K.values())
     y_layer = sum(ncols * r * 4 for _, r, _, _ in MATS)
-    x = (x_layer * LAYERS + ncols * HEAD[1] * 4) * world  # every rank reads the whole x
-    y = y_layer * LAYERS + ncols * HEAD[0] * 4
+    x = (x_layer * layers + ncols * HEAD[1] * 4) * world  # every rank reads the whole x
+    y = y_layer * layers + ncols * HEAD[0] * 4
     layer = sum(r * K * 9 // 16 for _, r, K, _ in MATS) + x_layer + y_layer
     return {"total": w + x + y, "weights": w, "per_layer_launch": layer}
 
@@ -99,12 +99,12 @@ def step_bytes(ncols: int, world: int = 1) -> dict:
 # clocks
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, bus_id: str | None):
-        self.bus_id = (bus_id or "").lower()
+    def __init__(self, uuid: str | None):
+        self.uuid = str(uuid or "").lower()
         self.proc = None
         self.lines: list[str] = []
         self.thread = None
@@ -139,7 +139,7 @@ class ClockSampler:
             f = [c.strip() for c in ln.split(",")]
             if len(f) < 10:
                 continue
-            if self.bus_id and self.bus_id[-12:] not in f[1].lower():
+            if self.uuid and self.uuid not in f[1].lower():
                 continue
             rows.append(f)
         sm = [float(f[2].split()[0]) for f in rows if f[2].split()[0].replace(".", "").isdigit()]
@@ -211,7 +211,7 @@ def cpu_baseline(O, layer_mats, ncols, budget_s: float = 12.0) -> dict:
             O.gemv_f32(W, xs[grp], nthreads=threads)
         n += 1
         el = time.perf_counter() - t0
-        if el > budget_s or n >= 200:
+        if el > budget_s:
             break
     return {"value": bytes_one * n / el / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
             "sample": f"{n} x one Mistral-7B decoder layer's 7 Q4_K GEMVs (fp32 x, q8_1 quantization "
@@ -225,6 +225,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--ncols", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers to build (profiling: fewer)")
+    ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -254,8 +256,9 @@ def main():
     # ---- weights (sharded rows), activations, outputs -------------------------
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
+    nlayers = args.layers
     layers = []
-    for li in range(LAYERS):
+    for li in range(nlayers):
         xs = {grp: torch.randn((ncols, K), device=dev, generator=g) for grp, K in ACT_K.items()}
         ents = []
         for name, rows, K, grp in MATS:
@@ -306,39 +309,42 @@ def main():
 
     # ---- capture one graph per timed step (own timing events in each) --------
     nsteps = args.steps + args.warmup
-    use_graph = True
+    use_graph = not args.no_graph
     graphs, evs = [], []
     try:
+        if not use_graph:
+            raise RuntimeError("--no-graph")
         with torch.cuda.stream(stream):
             for s in range(nsteps):
                 ev = [(torch.cuda.Event(enable_timing=True, external=True),
-                       torch.cuda.Event(enable_timing=True, external=True)) for _ in range(LAYERS)]
+                       torch.cuda.Event(enable_timing=True, external=True)) for _ in range(nlayers)]
                 gph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(gph, stream=stream):
                     run_step(ev)
                 graphs.append(gph)
                 evs.append(ev)
     except Exception as e:  # capture unsupported (e.g. collectives): time eagerly
-        print(f"# graph capture failed ({e!r}); timing eager launches", file=sys.stderr)
+        if use_graph:
+            print(f"# graph capture failed ({e!r}); timing eager launches", file=sys.stderr)
         use_graph = False
         graphs, evs = [], []
         for s in range(nsteps):
             evs.append([(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                        for _ in range(LAYERS)])
+                        for _ in range(nlayers)])
 
     def replay(s):
-        if use_graph:
-            graphs[s].replay()
-        else:
-            with torch.cuda.stream(stream):
+        with torch.cuda.stream(stream):  # replay() launches on the current stream
+            if use_graph:
+                graphs[s].replay()
+            else:
                 run_step(evs[s])
 
-    bus_id = None
+    uuid = None
     try:
-        bus_id = torch.cuda.get_device_properties(dev).pci_bus_id
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
     except AttributeError:
         pass
-    sampler = ClockSampler(bus_id) if rank == 0 else None
+    sampler = ClockSampler(uuid) if rank == 0 else None
 
     for s in range(args.warmup):
         replay(s)
@@ -363,14 +369,14 @@ def main():
 
     ms = t_start.elapsed_time(t_end) / args.steps
     launch_ms = [evs[s][li][0].elapsed_time(evs[s][li][1]) for s in range(args.warmup, nsteps)
-                 for li in range(LAYERS)]
+                 for li in range(nlayers)]
     launch_ms_mean = float(np.mean(launch_ms))
     if world > 1:
         t = torch.tensor([ms, launch_ms_mean], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, launch_ms_mean = float(t[0]), float(t[1])
 
-    sb = step_bytes(ncols, world)
+    sb = step_bytes(ncols, world, nlayers)
     value = sb["total"] / (ms * 1e-3) / 1e12
     peak, peak_kind = measured_peaks()
     per_launch_bytes = sb["per_layer_launch"] if world == 1 else None
@@ -440,7 +446,8 @@ def main():
             "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "layers": LAYERS, "matrices_per_layer": len(MATS),
+            "config": {"workload": WORKLOAD if nlayers == LAYERS else f"{WORKLOAD} (profiling subset)",
+                       "layers": nlayers, "matrices_per_layer": len(MATS),
                        "head": f"{HEAD[0]}x{HEAD[1]}", "ncols": ncols,
                        "launches": "per layer: prep (q8_1 quantization) + persistent GEMV over 7 matrices (PDL)",
                        "timing": "CUDA-graph replay per step, CUDA events on the launch stream",
@@ -453,7 +460,7 @@ def main():
                          "kernel": "k_gemv (one decoder layer, 7 matrices) incl. its overlapped prep launch",
                          "algorithmic_bytes_per_launch": per_launch_bytes},
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
-            "gpu_launches": args.steps * (LAYERS + 1) * 2,
+            "gpu_launches": args.steps * (nlayers + 1) * 2,
             "graph": use_graph,
         }
         print(json.dumps(line), flush=True)

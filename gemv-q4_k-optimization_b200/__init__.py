@@ -28,7 +28,7 @@ from typing import Sequence
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-LIB_PATH = HERE / "libq4k_gemv.so"
+LIB_PATH = Path(os.environ.get("Q4K_LIB", str(HERE / "libq4k_gemv.so")))  # Q4K_LIB: another build
 HEADER_PATH = HERE.parent / "include" / "q4k_gemv.h"
 
 QK_K = 256

@@ -14,6 +14,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 using namespace q4k;
@@ -58,7 +59,7 @@ Layout make_layout(int64_t n_rowgroups, int ncols, size_t act_bytes, int num_sms
     Layout L;
     L.counters_off = kAlign;
     L.partials_off = L.counters_off + round_up(static_cast<size_t>(n_rowgroups) * 4, kAlign);
-    const size_t workers = static_cast<size_t>(num_sms) * kWarps;
+    const size_t workers = static_cast<size_t>(num_sms) * kMaxWarps;
     L.act_off = L.partials_off + round_up(workers * 2 * ncols * 32 * sizeof(float), kAlign);
     L.total = L.act_off + round_up(act_bytes, kAlign);
     return L;
@@ -74,6 +75,42 @@ struct Job {
 };
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// cuTensorMapEncodeTiled, fetched through the runtime (no link against libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn tensor_map_encoder() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// Weight matrix as a 2D uint32 tensor {nb*36 words, nrows}, row stride in
+// bytes, box {36 words = one super-block, 32 rows}.
+int encode_weight_map(CUtensorMap *tm, const void *W, int64_t nrows, int64_t nb, int64_t row_stride_bytes) {
+    EncodeTiledFn enc = tensor_map_encoder();
+    if (!enc) return fail(Q4K_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(nb * 36), static_cast<cuuint64_t>(nrows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_bytes)};
+    const cuuint32_t box[2] = {36, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(W), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(Q4K_ECUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+    return Q4K_OK;
+}
 
 int validate_job(const Job &j, int ncols, int idx) {
     if (ncols < 1 || ncols > Q4K_MAX_NCOLS)
@@ -162,6 +199,8 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         T.nb = static_cast<int32_t>(nb);
         T.apr = static_cast<int32_t>(apr);
         T.rg_base = static_cast<int32_t>(rgs);
+        T.ngroups = static_cast<int32_t>(groups);
+        T.pad_ = 0;
         atoms += groups * apr;
         rgs += groups;
     }
@@ -170,7 +209,7 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.any_work = atoms > 0;
     P.gemv.ntasks = nt;
     P.gemv.natoms = atoms;
-    const int64_t max_workers = static_cast<int64_t>(num_sms) * kWarps;
+    const int64_t max_workers = static_cast<int64_t>(num_sms) * warps_for(ncols);
     P.gemv.nworkers = static_cast<int32_t>(atoms < max_workers ? atoms : max_workers);
     if (ws == nullptr) return Q4K_OK;
 
@@ -182,6 +221,9 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     nt = 0;
     for (int i = 0; i < njobs; ++i) {
         if (P.act_of_job[i] < 0) continue;
+        const Job &j = jobs[i];
+        int st = encode_weight_map(&P.gemv.tmap[nt], j.W, j.nrows, j.K / Q4K_QK_K, j.stride_row_x * Q4K_BLOCK_BYTES);
+        if (st != Q4K_OK) return st;
         P.gemv.task[nt++].act = ws + P.layout.act_off + acts[P.act_of_job[i]].off;
     }
     // prep jobs: one per distinct activation

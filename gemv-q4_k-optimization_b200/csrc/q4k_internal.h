@@ -3,6 +3,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>  // CUtensorMap (type only; the encoder is fetched at run time)
 #include <cuda_runtime.h>
 
 namespace q4k {
@@ -17,16 +18,40 @@ constexpr int kMaxTasks = 16;
 constexpr int kMaxJobs = 16;
 
 // GEMV geometry.  A "worker" is one warp; it owns a contiguous range of
-// "atoms" (32 weight rows x kKS super-blocks) of the flattened work of all
-// tasks, streamed through a private kStages-deep ring of shared-memory stages
-// by bulk asynchronous copies.  Lane = weight row.
-constexpr int kWarps = 8;
-constexpr int kStages = 2;
-constexpr int kKS = 2;                                // super-blocks per atom and row
-constexpr int kPitch = kKS * 144 + 16;                // smem bytes per row (odd multiple of 16)
-constexpr int kStageBytes = 32 * kPitch;
-constexpr int kSmemBytes = kWarps * kStages * kStageBytes;
-static_assert((kPitch / 16) % 2 == 1, "row pitch must be an odd number of 16-byte units");
+// "atoms" (32 weight rows x kKS super-blocks, plus the kKS activation records
+// of every column) of the flattened work of all tasks, streamed through a
+// private kStages-deep ring of shared-memory stages by bulk asynchronous
+// copies.  Lane = weight row.
+#ifndef Q4K_MAX_WARPS
+#define Q4K_MAX_WARPS 8
+#endif
+#ifndef Q4K_STAGES
+#define Q4K_STAGES 2
+#endif
+#ifndef Q4K_KS
+#define Q4K_KS 2
+#endif
+constexpr int kMaxWarps = Q4K_MAX_WARPS;
+constexpr int kStages = Q4K_STAGES;
+constexpr int kKS = Q4K_KS;  // super-blocks per atom and row
+// Weights of one super-block for 32 rows: one 2D tensor-map box of 32 rows x
+// 144 bytes, landing densely at a 144-byte row pitch -- an odd number of
+// 16-byte units, so the 8 lanes of a quarter-warp (8 consecutive rows) hit
+// 8 different bank groups.
+constexpr int kPitch = 144;
+constexpr int kBoxBytes = 32 * kPitch;
+constexpr int kWStageBytes = kKS * kBoxBytes;
+constexpr int kSmemLimit = 227 * 1024;
+
+// One ring stage: weights (32 rows) then the activation records of ncols columns.
+__host__ __device__ constexpr int stage_bytes(int ncols) { return kWStageBytes + ncols * kKS * 320; }
+// Warps per CTA for ncols columns: as many private rings as fit (one CTA per SM).
+__host__ __device__ constexpr int warps_for(int ncols) {
+    return kSmemLimit / (kStages * stage_bytes(ncols)) < kMaxWarps ? kSmemLimit / (kStages * stage_bytes(ncols))
+                                                                   : kMaxWarps;
+}
+__host__ __device__ constexpr int smem_bytes(int ncols) { return warps_for(ncols) * kStages * stage_bytes(ncols); }
+static_assert(warps_for(8) >= 4, "ring too large for 8 columns");
 
 // Device status codes (match q4k_status).
 constexpr int kStatusOk = 0;
@@ -47,12 +72,15 @@ struct TaskDesc {
     int32_t nb;              // super-blocks per row
     int32_t apr;             // atoms per row group = ceil(nb / kKS)
     int32_t rg_base;         // global row-group index of row group 0
+    int32_t ngroups;         // row groups = ceil(nrows / 32)
+    int32_t pad_;
 };
 
 struct GemvParams {
+    CUtensorMap tmap[kMaxTasks];  // per task: uint32 view {nb*36, nrows}, box {36, 32}
     TaskDesc task[kMaxTasks];
     int32_t ntasks;
-    int32_t nworkers;        // active workers (<= gridDim.x * kWarps, <= natoms)
+    int32_t nworkers;        // active workers (<= gridDim.x * warps_for(ncols), <= natoms)
     int64_t natoms;
     int32_t *counters;       // one per global row group, zero at kernel start
     float *partials;         // [nworkers][2][ncols][32]

@@ -93,22 +93,34 @@ __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams
 // ============================================================================
 // GEMV
 // ============================================================================
-struct AtomPos {
-    int t;   // task
-    int g;   // row group within the task
-    int kp;  // atom within the row group
+// Position of an atom: task t, row group g of the task, atom kp of the group.
+// Workers walk their contiguous atom range with an incremental cursor.
+struct AtomCursor {
+    int t;
+    int g;
+    int kp;
 };
 
-__device__ __forceinline__ AtomPos decode_atom(const GemvParams &P, int64_t a) {
+__device__ __forceinline__ AtomCursor locate_atom(const GemvParams &P, int64_t a) {
     int t = 0;
     while (t + 1 < P.ntasks && a >= P.task[t + 1].atom_base) ++t;
-    const int64_t local = a - P.task[t].atom_base;
+    const int local = static_cast<int>(a - P.task[t].atom_base);
     const int apr = P.task[t].apr;
-    AtomPos r;
-    r.t = t;
-    r.g = static_cast<int>(local / apr);
-    r.kp = static_cast<int>(local - static_cast<int64_t>(r.g) * apr);
-    return r;
+    AtomCursor c;
+    c.t = t;
+    c.g = local / apr;
+    c.kp = local - c.g * apr;
+    return c;
+}
+
+__device__ __forceinline__ void advance(const GemvParams &P, AtomCursor &c) {
+    if (++c.kp == P.task[c.t].apr) {
+        c.kp = 0;
+        if (++c.g == P.task[c.t].ngroups) {
+            c.g = 0;
+            ++c.t;
+        }
+    }
 }
 
 // First atom of worker w under the uniform partition of natoms over nworkers.
@@ -120,22 +132,47 @@ __device__ __forceinline__ int64_t worker_of(const GemvParams &P, int64_t a) {
     return ((a + 1) * P.nworkers - 1) / P.natoms;
 }
 
-// Issue the bulk copies of atom a into a ring stage: lane r copies row r's
-// kKS-super-block segment; lane 0 first announces the byte count.
-__device__ __forceinline__ void issue_atom(const GemvParams &P, int64_t a, uint32_t stage,
-                                           uint32_t bar, int lane) {
-    const AtomPos ap = decode_atom(P, a);
-    const TaskDesc &T = P.task[ap.t];
-    const int rows = min(32, T.nrows - ap.g * 32);
-    const int kb0 = ap.kp * kKS;
+// Stage layout: [kKS boxes of 32 rows x 144 B][NC columns x kKS activation records].
+template <int NC>
+struct Stage {
+    static constexpr int kActOff = kWStageBytes;
+    static constexpr int kBytes = stage_bytes(NC);
+    // tensor-map boxes land 128-byte aligned: every stage, box and record
+    // region starts on a multiple of 128 bytes from the ring base
+    static_assert(kBoxBytes % 128 == 0 && kActOff % 128 == 0 && kBytes % 128 == 0, "stage alignment");
+};
+static_assert(sizeof(GemvParams) <= 4096, "kernel parameters exceed 4 KB");
+
+// Announce the atom's bytes and copy its weights: one tensor-map box (32 rows
+// x 144 bytes) per super-block, issued by lane 0.  Rows past the matrix end
+// are zero-filled by the copy and still counted in its byte total.
+template <int NC>
+__device__ __forceinline__ void issue_weights(const GemvParams &P, const AtomCursor &c, uint32_t stage,
+                                              uint32_t bar, int lane) {
+    const TaskDesc &T = P.task[c.t];
+    const int kb0 = c.kp * kKS;
     const int nsb = min(kKS, T.nb - kb0);
-    const uint32_t seg = static_cast<uint32_t>(nsb * kSBBytes);
-    if (lane == 0) mbar_expect_tx(bar, static_cast<uint32_t>(rows) * seg);
+    if (lane == 0) {
+        mbar_expect_tx(bar, static_cast<uint32_t>(nsb * (kBoxBytes + NC * kActSBBytes)));
+#pragma unroll
+        for (int i = 0; i < kKS; ++i)
+            if (i < nsb) tma_load_2d(stage + i * kBoxBytes, &P.tmap[c.t], (kb0 + i) * 36, c.g * 32, bar);
+    }
     __syncwarp();
-    if (lane < rows) {
-        const uint8_t *src = T.W + static_cast<int64_t>(ap.g * 32 + lane) * T.row_stride +
-                             static_cast<int64_t>(kb0) * kSBBytes;
-        bulk_g2s(stage + lane * kPitch, src, seg, bar);
+}
+
+// Copy the atom's activation records (one copy per column, lanes 0..NC-1).
+// Only after griddepcontrol.wait: the prep kernel writes them.
+template <int NC>
+__device__ __forceinline__ void issue_acts(const GemvParams &P, const AtomCursor &c, uint32_t stage,
+                                           uint32_t bar, int lane) {
+    const TaskDesc &T = P.task[c.t];
+    const int kb0 = c.kp * kKS;
+    const int nsb = min(kKS, T.nb - kb0);
+    if (lane < NC) {
+        const uint8_t *src = T.act + lane * T.act_col_stride + static_cast<int64_t>(kb0) * kActSBBytes;
+        bulk_g2s(stage + Stage<NC>::kActOff + lane * (kKS * kActSBBytes), src,
+                 static_cast<uint32_t>(nsb * kActSBBytes), bar);
     }
 }
 
@@ -149,11 +186,61 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, unsign
     }
 }
 
-// One super-block of one row (smem at p) against the q8a records of all NC
-// columns.  acc[j] holds a packed pair of partial sums for column j.
+// Sub-block pair c (sub-blocks 2c, 2c+1) of one super-block of one row
+// (weights at p) against NC activation records (act, column stride acs).
+// acc[j] holds a packed pair of partial sums for column j.
 template <int NC, bool DUMP>
-__device__ __forceinline__ void sb_dot(uint32_t p, const uint8_t *act, int64_t acs, uint64_t (&acc)[NC],
-                                       int32_t *dumpS) {
+__device__ __forceinline__ void pair_dot(uint32_t p, uint32_t act, int c, float d, float nd23, float dmin,
+                                         float pm23, uint32_t scw, uint32_t mw, uint64_t (&acc)[NC],
+                                         int32_t *dumpS, int64_t dump_col_stride) {
+    const int b0 = (c & 1) * 2;
+    // d*sc and -dmin*m of sub-blocks 2c, 2c+1: (byte + 2^23)*x - 2^23*x == byte*x, one rounding
+    const uint64_t dsc = f2_pack(fmaf(byte_magic(scw, b0), d, nd23), fmaf(byte_magic(scw, b0 + 1), d, nd23));
+    const uint64_t ndm =
+        f2_pack(fmaf(byte_magic(mw, b0), -dmin, pm23), fmaf(byte_magic(mw, b0 + 1), -dmin, pm23));
+    const uint4 wa = lds128(p + 16 + 32 * c);
+    const uint4 wb = lds128(p + 32 + 32 * c);
+    const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    uint32_t lo[8], hi[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        lo[k] = w[k] & 0x0F0F0F0Fu;
+        hi[k] = w[k] & 0xF0F0F0F0u;  // 16 x nibble, unsigned bytes
+    }
+    const uint64_t magic2 = f2_pack(-kMagicF, -kMagicF);
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+        const uint32_t aj = act + j * (kKS * kActSBBytes);
+        const uint4 qe0 = lds128(aj + 64 * c);
+        const uint4 qe1 = lds128(aj + 64 * c + 16);
+        const uint4 qo0 = lds128(aj + 64 * c + 32);
+        const uint4 qo1 = lds128(aj + 64 * c + 48);
+        const uint4 meta = lds128(aj + kActMetaOff + 16 * c);
+        const uint32_t qe[8] = {qe0.x, qe0.y, qe0.z, qe0.w, qe1.x, qe1.y, qe1.z, qe1.w};
+        const uint32_t qo[8] = {qo0.x, qo0.y, qo0.z, qo0.w, qo1.x, qo1.y, qo1.z, qo1.w};
+        int se = kMagicI, so = kMagicI;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            se = dp4a_us(lo[k], qe[k], se);
+            so = dp4a_us(hi[k], qo[k], so);
+        }
+        if constexpr (DUMP) {
+            // exact sub-block sums (the odd one was formed on 16 x nibble)
+            dumpS[j * dump_col_stride + 2 * c] = se - kMagicI;
+            dumpS[j * dump_col_stride + 2 * c + 1] = (so - kMagicI) >> 4;
+        }
+        const uint64_t sf = f2_add(f2_pack(__int_as_float(se), __int_as_float(so)), magic2);
+        const uint64_t g = f2_mul(sf, f2_pack(__uint_as_float(meta.x), __uint_as_float(meta.y)));
+        acc[j] = f2_fma(g, dsc, acc[j]);
+        acc[j] = f2_fma(f2_pack(__uint_as_float(meta.z), __uint_as_float(meta.w)), ndm, acc[j]);
+    }
+}
+
+// One super-block of one row: weights at p, the activation records of its
+// NC columns at act.  Semantics of kernels/vecdotq.cuh:461-483, :775-819.
+template <int NC, bool DUMP>
+__device__ __forceinline__ void sb_dot(uint32_t p, uint32_t act, uint64_t (&acc)[NC], int32_t *dumpS,
+                                       int64_t dump_col_stride) {
     const uint4 h = lds128(p);
     const float2 dm = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
     const float d = dm.x, dmin = dm.y;
@@ -162,85 +249,41 @@ __device__ __forceinline__ void sb_dot(uint32_t p, const uint8_t *act, int64_t a
     const uint32_t m03 = h.z & 0x3F3F3F3Fu;
     const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
     const uint32_t m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-    // (byte + 2^23) * x - 2^23 * x == byte * x exactly (one rounding).
     const float nd23 = -8388608.0f * d;
     const float pm23 = 8388608.0f * dmin;
-    const uint64_t magic2 = f2_pack(-kMagicF, -kMagicF);
-
+    if constexpr (NC <= 2) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            pair_dot<NC, DUMP>(p, act, c, d, nd23, dmin, pm23, c < 2 ? sc03 : sc47, c < 2 ? m03 : m47, acc,
+                               dumpS, dump_col_stride);
+    } else {
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-        const uint32_t scw = c < 2 ? sc03 : sc47;
-        const uint32_t mw = c < 2 ? m03 : m47;
-        const int b0 = (c & 1) * 2;
-        // d*sc and -dmin*m for sub-blocks 2c, 2c+1
-        const uint64_t dsc = f2_pack(fmaf(byte_magic(scw, b0), d, nd23), fmaf(byte_magic(scw, b0 + 1), d, nd23));
-        const uint64_t ndm = f2_pack(fmaf(byte_magic(mw, b0), -dmin, pm23), fmaf(byte_magic(mw, b0 + 1), -dmin, pm23));
-        const uint4 wa = lds128(p + 16 + 32 * c);
-        const uint4 wb = lds128(p + 32 + 32 * c);
-        const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-        uint32_t lo[8], hi[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            lo[k] = w[k] & 0x0F0F0F0Fu;
-            hi[k] = w[k] & 0xF0F0F0F0u;  // 16 x nibble, unsigned bytes
-        }
-#pragma unroll
-        for (int j = 0; j < NC; ++j) {
-            const uint8_t *aj = act + j * acs;
-            const uint4 qe0 = ldg_nc128(aj + 64 * c);
-            const uint4 qe1 = ldg_nc128(aj + 64 * c + 16);
-            const uint4 qo0 = ldg_nc128(aj + 64 * c + 32);
-            const uint4 qo1 = ldg_nc128(aj + 64 * c + 48);
-            const uint4 meta = ldg_nc128(aj + kActMetaOff + 16 * c);
-            const uint32_t qe[8] = {qe0.x, qe0.y, qe0.z, qe0.w, qe1.x, qe1.y, qe1.z, qe1.w};
-            const uint32_t qo[8] = {qo0.x, qo0.y, qo0.z, qo0.w, qo1.x, qo1.y, qo1.z, qo1.w};
-            int se = kMagicI, so = kMagicI;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                se = dp4a_us(lo[k], qe[k], se);
-                so = dp4a_us(hi[k], qo[k], so);
-            }
-            if constexpr (DUMP) {
-                // Called with NC == 1 per column: the exact sub-block sums
-                // (the odd one was formed on 16 x nibble).
-                dumpS[2 * c] = se - kMagicI;
-                dumpS[2 * c + 1] = (so - kMagicI) >> 4;
-            }
-            const uint64_t sf = f2_add(f2_pack(__int_as_float(se), __int_as_float(so)), magic2);
-            const uint64_t g = f2_mul(sf, f2_pack(__uint_as_float(meta.x), __uint_as_float(meta.y)));
-            acc[j] = f2_fma(g, dsc, acc[j]);
-            acc[j] = f2_fma(f2_pack(__uint_as_float(meta.z), __uint_as_float(meta.w)), ndm, acc[j]);
-        }
+        for (int c = 0; c < 4; ++c)
+            pair_dot<NC, DUMP>(p, act, c, d, nd23, dmin, pm23, c < 2 ? sc03 : sc47, c < 2 ? m03 : m47, acc,
+                               dumpS, dump_col_stride);
     }
 }
 
 template <int NC, bool DUMP>
-__device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomPos &ap, uint32_t stage, int lane,
+__device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCursor &c, uint32_t stage, int lane,
                                              uint64_t (&acc)[NC]) {
-    const TaskDesc &T = P.task[ap.t];
-    const int rows = min(32, T.nrows - ap.g * 32);
-    const int kb0 = ap.kp * kKS;
+    const TaskDesc &T = P.task[c.t];
+    const int rows = min(32, T.nrows - c.g * 32);
+    const int kb0 = c.kp * kKS;
     const int nsb = min(kKS, T.nb - kb0);
     if (lane >= rows) return;
-#pragma unroll 1
+    const int row = c.g * 32 + lane;
+#pragma unroll
     for (int i = 0; i < kKS; ++i) {
         if (i < nsb) {
-            const int kb = kb0 + i;
+            int32_t *dS = nullptr;
+            int64_t dcs = 0;
             if constexpr (DUMP) {
-                // Per-column dump of this row's 8 sub-block sums.
-#pragma unroll
-                for (int j = 0; j < NC; ++j) {
-                    uint64_t one[1] = {acc[j]};
-                    int32_t *dS = P.dump_S + (static_cast<int64_t>(j) * T.nrows + ap.g * 32 + lane) *
-                                                 (static_cast<int64_t>(T.nb) * 8) + kb * 8;
-                    sb_dot<1, true>(stage + lane * kPitch + i * kSBBytes, T.act + static_cast<int64_t>(kb) * kActSBBytes +
-                                        j * T.act_col_stride, 0, one, dS);
-                    acc[j] = one[0];
-                }
-            } else {
-                sb_dot<NC, false>(stage + lane * kPitch + i * kSBBytes,
-                                  T.act + static_cast<int64_t>(kb) * kActSBBytes, T.act_col_stride, acc, nullptr);
+                dcs = static_cast<int64_t>(T.nrows) * T.nb * 8;
+                dS = P.dump_S + static_cast<int64_t>(row) * T.nb * 8 + (kb0 + i) * 8;
             }
+            sb_dot<NC, DUMP>(stage + i * kBoxBytes + lane * kPitch, stage + Stage<NC>::kActOff + i * kActSBBytes,
+                             acc, dS, dcs);
         }
     }
 }
@@ -249,7 +292,7 @@ __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomPos 
 // covered all of its atoms, otherwise deposit the partial sums and let the
 // last of the contributing warps add them up (in worker order) and write.
 template <int NC, bool DUMP>
-__device__ __forceinline__ void flush_group(const GemvParams &P, const AtomPos &cur, uint64_t (&acc)[NC],
+__device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCursor &cur, uint64_t (&acc)[NC],
                                             int64_t worker, int64_t a0, int64_t a1, int lane) {
     const TaskDesc &T = P.task[cur.t];
     float v[NC];
@@ -297,9 +340,11 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomPos &
 }
 
 template <int NC, bool DUMP>
-__global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
+__global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
+    constexpr int kW = warps_for(NC);
+    constexpr int kSB = Stage<NC>::kBytes;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bars[kWarps][kStages];
+    __shared__ __align__(8) uint64_t bars[kW][kStages];
 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -308,9 +353,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const __grid_constant__
     if (worker >= P.nworkers) return;
     const int64_t a0 = worker_begin(P, worker);
     const int64_t a1 = worker_begin(P, worker + 1);
-    const int64_t n = a1 - a0;
+    const int n = static_cast<int>(a1 - a0);
 
-    const uint32_t ring = smem_addr(smem) + static_cast<uint32_t>(warp * kStages * kStageBytes);
+    const uint32_t ring = smem_addr(smem) + static_cast<uint32_t>(warp * kStages * kSB);
     uint32_t bar[kStages];
 #pragma unroll
     for (int s = 0; s < kStages; ++s) bar[s] = smem_addr(&bars[warp][s]);
@@ -321,25 +366,39 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const __grid_constant__
     }
     __syncwarp();
 
-    // Weight bytes do not depend on the prep kernel: start streaming now.
+    // Weight bytes do not depend on the prep kernel: start streaming now,
+    // activations once the prep grid has completed.
+    AtomCursor icur = locate_atom(P, a0);
+    AtomCursor pro[kStages];
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+        pro[s] = icur;
+        if (s < n) {
+            issue_weights<NC>(P, icur, ring + s * kSB, bar[s], lane);
+            advance(P, icur);
+        }
+    }
+    pdl_wait();
 #pragma unroll
     for (int s = 0; s < kStages; ++s)
-        if (s < n) issue_atom(P, a0 + s, ring + s * kStageBytes, bar[s], lane);
-
-    pdl_wait();  // activations and cleared counters are visible after this
+        if (s < n) issue_acts<NC>(P, pro[s], ring + s * kSB, bar[s], lane);
 
     uint64_t acc[NC];
 #pragma unroll
     for (int j = 0; j < NC; ++j) acc[j] = 0ull;
-    AtomPos cur{-1, -1, 0};
+    AtomCursor cur = pro[0];
+    int open_t = -1, open_g = -1;
 
-    for (int64_t i = 0; i < n; ++i) {
-        const int s = static_cast<int>(i % kStages);
+    for (int i = 0; i < n; ++i) {
+        const int s = i % kStages;
         const uint32_t parity = static_cast<uint32_t>((i / kStages) & 1);
-        const AtomPos ap = decode_atom(P, a0 + i);
-        if (ap.t != cur.t || ap.g != cur.g) {
-            if (cur.t >= 0) flush_group<NC, DUMP>(P, cur, acc, worker, a0, a1, lane);
-            cur = ap;
+        if (cur.t != open_t || cur.g != open_g) {
+            if (open_t >= 0) {
+                AtomCursor o{open_t, open_g, 0};
+                flush_group<NC, DUMP>(P, o, acc, worker, a0, a1, lane);
+            }
+            open_t = cur.t;
+            open_g = cur.g;
 #pragma unroll
             for (int j = 0; j < NC; ++j) acc[j] = 0ull;
         }
@@ -347,19 +406,25 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const __grid_constant__
             if (lane == 0) atomicExch(P.status, kStatusTimeout);
             // Let this warp's other copies in flight land (bounded) before leaving.
             for (int k = 1; k < kStages; ++k) {
-                const int64_t ii = i + k;
+                const int ii = i + k;
                 if (ii < n) wait_phase(bar[ii % kStages], static_cast<uint32_t>((ii / kStages) & 1), kDrainLimitNs);
             }
             return;
         }
-        compute_atom<NC, DUMP>(P, ap, ring + s * kStageBytes, lane, acc);
+        compute_atom<NC, DUMP>(P, cur, ring + s * kSB, lane, acc);
         __syncwarp();
         if (i + kStages < n) {
             fence_proxy_async_smem();
-            issue_atom(P, a0 + i + kStages, ring + s * kStageBytes, bar[s], lane);
+            issue_weights<NC>(P, icur, ring + s * kSB, bar[s], lane);
+            issue_acts<NC>(P, icur, ring + s * kSB, bar[s], lane);
+            advance(P, icur);
         }
+        advance(P, cur);
     }
-    if (cur.t >= 0) flush_group<NC, DUMP>(P, cur, acc, worker, a0, a1, lane);
+    if (open_t >= 0) {
+        AtomCursor o{open_t, open_g, 0};
+        flush_group<NC, DUMP>(P, o, acc, worker, a0, a1, lane);
+    }
 }
 
 // ============================================================================
@@ -375,7 +440,7 @@ DevState g_dev[64];
 
 template <int NC, bool DUMP>
 cudaError_t set_attrs() {
-    return cudaFuncSetAttribute(k_gemv<NC, DUMP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    return cudaFuncSetAttribute(k_gemv<NC, DUMP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(NC));
 }
 
 template <bool DUMP>
@@ -439,8 +504,8 @@ cudaError_t launch_gemv(const GemvParams &p, int ncols, bool dump, int grid, cud
     if (fn == nullptr) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
-    cfg.blockDim = dim3(kWarps * 32);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.blockDim = dim3(warps_for(ncols) * 32);
+    cfg.dynamicSmemBytes = smem_bytes(ncols);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
