@@ -211,6 +211,8 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.gemv.natoms = atoms;
     const int64_t max_workers = static_cast<int64_t>(num_sms) * warps_for(ncols);
     P.gemv.nworkers = static_cast<int32_t>(atoms < max_workers ? atoms : max_workers);
+    P.gemv.packed = atoms >= 4 * max_workers ? 1 : 0;
+    P.gemv.pad0_ = 0;
     if (ws == nullptr) return Q4K_OK;
 
     // pointers into the workspace

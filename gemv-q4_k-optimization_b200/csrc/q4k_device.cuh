@@ -143,6 +143,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+// ---- release/acquire counters (split-group completion) ------------------------
+// Device-scope fetch-add with acquire-release semantics.
+__device__ __forceinline__ int atom_add_acqrel_gpu(int *p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void st_relaxed_gpu(int *p, int v) {
+    asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // ---- programmatic dependent launch -------------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {

@@ -81,6 +81,9 @@ struct GemvParams {
     TaskDesc task[kMaxTasks];
     int32_t ntasks;
     int32_t nworkers;        // active workers (<= gridDim.x * warps_for(ncols), <= natoms)
+    int32_t packed;          // 1: worker = cta * warps + warp (CTA-contiguous ranges);
+                             // 0: worker = warp * gridDim.x + cta (small problems spread over SMs)
+    int32_t pad0_;
     int64_t natoms;
     int32_t *counters;       // one per global row group, zero at kernel start
     float *partials;         // [nworkers][2][ncols][32]

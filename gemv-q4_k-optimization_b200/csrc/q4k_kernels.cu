@@ -34,6 +34,9 @@ __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams
     // Let the dependent GEMV grid launch now: it only issues weight copies
     // before its griddepcontrol.wait, which returns after this grid completes.
     pdl_launch_dependents();
+    // This grid may itself be a programmatic dependent of the previous GEMV
+    // launch (which shares the workspace): wait for it before writing.
+    pdl_wait();
 
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -290,10 +293,14 @@ __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCurs
 
 // Finish a row group this warp worked on: write it out directly if the warp
 // covered all of its atoms, otherwise deposit the partial sums and let the
-// last of the contributing warps add them up (in worker order) and write.
+// last of the contributing warps add them up (always in worker order, so the
+// result is deterministic) and write.  Contributors that all belong to this
+// CTA count arrivals in shared memory under block-scope ordering; otherwise a
+// device-scope acquire-release counter in the workspace is used.
 template <int NC, bool DUMP>
 __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCursor &cur, uint64_t (&acc)[NC],
-                                            int64_t worker, int64_t a0, int64_t a1, int lane) {
+                                            int64_t worker, int64_t a0, int64_t a1, int lane, int64_t cta_w0,
+                                            int64_t cta_w1, int *cta_cnt) {
     const TaskDesc &T = P.task[cur.t];
     float v[NC];
 #pragma unroll
@@ -316,14 +323,23 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
     float *mine = P.partials + ((worker * 2 + slot) * NC) * 32;
 #pragma unroll
     for (int j = 0; j < NC; ++j) mine[j * 32 + lane] = v[j];
-    __threadfence();
-    __syncwarp();
-    int old = 0;
-    if (lane == 0) old = atomicAdd(&P.counters[T.rg_base + cur.g], 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
     const int64_t w1 = worker_of(P, sg), w2 = worker_of(P, eg - 1);
-    if (old != static_cast<int>(w2 - w1)) return;  // not the last contributor
-    __threadfence();
+    const bool local = P.packed && w1 >= cta_w0 && w2 <= cta_w1;
+    int old = 0;
+    if (local) {
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) old = atomicAdd(&cta_cnt[w1 - cta_w0], 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old != static_cast<int>(w2 - w1)) return;  // not the last contributor
+        __threadfence_block();
+    } else {
+        __syncwarp();
+        if (lane == 0) old = atom_add_acqrel_gpu(&P.counters[T.rg_base + cur.g], 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old != static_cast<int>(w2 - w1)) return;
+        __syncwarp();
+    }
     float tot[NC];
 #pragma unroll
     for (int j = 0; j < NC; ++j) tot[j] = 0.0f;
@@ -336,7 +352,12 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
 #pragma unroll
         for (int j = 0; j < NC; ++j) T.dst[j * T.dst_col_stride + row] = tot[j];
     }
-    if (lane == 0) P.counters[T.rg_base + cur.g] = 0;
+    if (lane == 0) {
+        if (local)
+            cta_cnt[w1 - cta_w0] = 0;
+        else
+            st_relaxed_gpu(&P.counters[T.rg_base + cur.g], 0);
+    }
 }
 
 template <int NC, bool DUMP>
@@ -345,11 +366,21 @@ __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_con
     constexpr int kSB = Stage<NC>::kBytes;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t bars[kW][kStages];
+    __shared__ int cta_cnt[kW];  // arrivals at row groups split between this CTA's warps
 
+    // The next prep launch may start now; it waits for this grid's completion
+    // before it touches the workspace.
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    // Consecutive workers sit on different SMs, so small problems spread out.
-    const int64_t worker = static_cast<int64_t>(warp) * gridDim.x + blockIdx.x;
+    if (threadIdx.x < kW) cta_cnt[threadIdx.x] = 0;
+    __syncthreads();
+    // Large problems: CTA-contiguous worker ranges (most split row groups stay
+    // inside a CTA).  Small ones: consecutive workers on different SMs.
+    const int64_t worker = P.packed ? static_cast<int64_t>(blockIdx.x) * kW + warp
+                                    : static_cast<int64_t>(warp) * gridDim.x + blockIdx.x;
+    const int64_t cta_w0 = static_cast<int64_t>(blockIdx.x) * kW;
+    const int64_t cta_w1 = cta_w0 + kW - 1;
     if (worker >= P.nworkers) return;
     const int64_t a0 = worker_begin(P, worker);
     const int64_t a1 = worker_begin(P, worker + 1);
@@ -395,7 +426,7 @@ __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_con
         if (cur.t != open_t || cur.g != open_g) {
             if (open_t >= 0) {
                 AtomCursor o{open_t, open_g, 0};
-                flush_group<NC, DUMP>(P, o, acc, worker, a0, a1, lane);
+                flush_group<NC, DUMP>(P, o, acc, worker, a0, a1, lane, cta_w0, cta_w1, cta_cnt);
             }
             open_t = cur.t;
             open_g = cur.g;
@@ -423,7 +454,7 @@ __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_con
     }
     if (open_t >= 0) {
         AtomCursor o{open_t, open_g, 0};
-        flush_group<NC, DUMP>(P, o, acc, worker, a0, a1, lane);
+        flush_group<NC, DUMP>(P, o, acc, worker, a0, a1, lane, cta_w0, cta_w1, cta_cnt);
     }
 }
 
@@ -495,8 +526,19 @@ cudaError_t launch_prep(const PrepParams &p, cudaStream_t s) {
     if (zb > blocks) blocks = zb;
     if (blocks < 1) blocks = 1;
     if (blocks > 4096) blocks = 4096;
-    k_prep<<<static_cast<unsigned>(blocks), 256, 0, s>>>(p);
-    return cudaGetLastError();
+    // Programmatic dependent of whatever precedes it on the stream: it can be
+    // resident before the previous GEMV ends and waits for it on the device.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_prep, p);
 }
 
 cudaError_t launch_gemv(const GemvParams &p, int ncols, bool dump, int grid, cudaStream_t s) {
