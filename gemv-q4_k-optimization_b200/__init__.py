@@ -98,6 +98,8 @@ def lib() -> ctypes.CDLL:
         L.q4k_gemv_batch.argtypes = [ctypes.POINTER(Task), _I, _I, _P, _SZ, _P]
         L.q4k_debug_subblock_sums.argtypes = [_P, _P, _I64, _I64, _I, _I64, _I64, _P, _P, _P, _SZ, _P]
         L.q4k_workspace_status.argtypes = [_P, ctypes.POINTER(_I), _P]
+        L.q4k_mul_mat_vec_noalloc.argtypes = [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P]
+        L.q4k_noalloc_scratch_bytes.restype = _SZ
         _lib = L
     return _lib
 
@@ -216,6 +218,22 @@ def mul_mat_vec_q(W, x, out=None, ws: Workspace | None = None, stream=None):
     _check(lib().q4k_mul_mat_vec(W.data_ptr(), x.data_ptr(), out.data_ptr(), K, nrows, ncols,
                                  W.stride(0) // BLOCK_BYTES, x.stride(0), out.stride(0),
                                  w.ptr, w.nbytes, _stream(stream)))
+    return out
+
+
+def mul_mat_vec_q_noalloc(W, x, out=None, stream=None):
+    """mul_mat_vec_q for callers that cannot allocate device scratch: the library
+    uses its own built-in array (q4k_noalloc_scratch_bytes(); shared by all such
+    calls on a device, so calls that may overlap on the GPU race)."""
+    import torch
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    ncols, K = x.shape
+    nrows = W.shape[0]
+    if out is None:
+        out = torch.empty((ncols, nrows), dtype=torch.float32, device=x.device)
+    _check(lib().q4k_mul_mat_vec_noalloc(W.data_ptr(), x.data_ptr(), out.data_ptr(), K, nrows, ncols,
+                                         W.stride(0) // BLOCK_BYTES, x.stride(0), out.stride(0), _stream(stream)))
     return out
 
 

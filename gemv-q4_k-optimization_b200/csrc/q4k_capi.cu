@@ -301,6 +301,11 @@ size_t plan_bytes(const Job *jobs, int njobs, int ncols) {
 
 }  // namespace
 
+namespace q4k {
+// Lets other translation units of the library report through q4k_last_error().
+void set_last_error_message(const char *msg) { g_last_error = msg; }
+}  // namespace q4k
+
 extern "C" {
 
 const char *q4k_status_string(int status) {

@@ -159,6 +159,25 @@ Q4K_API size_t q4k_batch_workspace_bytes(const q4k_task *tasks, int ntasks, int 
 Q4K_API int q4k_gemv_batch(const q4k_task *tasks, int ntasks, int ncols,
                    void *workspace, size_t workspace_bytes, q4k_stream_t stream);
 
+/* ---- callers that cannot allocate --------------------------------------------- */
+
+/* q4k_mul_mat_vec without a caller workspace.  No counterpart in the reference.
+ * For callers that may not allocate device memory at all (runtimes that plan
+ * every buffer ahead and forbid cudaMalloc on the decode path, host
+ * applications that own the GPU memory budget): the scratch comes from a
+ * 4 MiB array built into the library, held on every GPU that loads it until
+ * the process exits.  Calls that need more (q4k_gemv_workspace_bytes(nrows, K,
+ * ncols) > q4k_noalloc_scratch_bytes()) return Q4K_EINVAL with a message.
+ * The first call on a device looks up the array's device address; make that
+ * first call before any stream capture.  All calls on a device share the
+ * array: calls that can overlap on the GPU (e.g. on two streams) race. */
+Q4K_API int q4k_mul_mat_vec_noalloc(const void *W, const float *x, float *dst,
+                                    int64_t K, int64_t nrows, int ncols,
+                                    int64_t stride_row_x, int64_t stride_col_x, int64_t stride_col_dst,
+                                    q4k_stream_t stream);
+/* Size of that built-in scratch array in bytes. */
+Q4K_API size_t q4k_noalloc_scratch_bytes(void);
+
 /* ---- diagnostics ------------------------------------------------------------- */
 
 /* Per-sub-block integer sums as the kernels form them, for bit-exact parity
