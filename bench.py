@@ -229,6 +229,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers to build (profiling: fewer)")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: fused peer-store all-gather in the GEMV (default) or NCCL all_gather per layer")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -259,6 +261,9 @@ def main():
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
     nlayers = args.layers
+    peer = world > 1 and args.gather == "peer"
+    layer_elems = sum(r * ncols for _, r, _, _ in MATS)
+    pg = q4k.PeerGather(nlayers * layer_elems + HEAD[0] * ncols) if peer else None
     layers = []
     for li in range(nlayers):
         xs = {grp: torch.randn((ncols, K), device=dev, generator=g) for grp, K in ACT_K.items()}
@@ -266,41 +271,66 @@ def main():
         for name, rows, K, grp in MATS:
             lo, hi, per = shard(rows, rank, world)
             W = q4k.gen_q4k_torch(hi - lo, K, generator=g, device=dev)
-            ents.append((name, W, xs[grp], rows, per, hi - lo))
-        # local outputs packed so one all-gather covers the layer
-        per_tot = sum(e[4] for e in ents)
-        ybuf = torch.zeros((per_tot * ncols,), device=dev)
-        outs, off = [], 0
-        for e in ents:
-            outs.append(ybuf[off: off + e[4] * ncols].view(ncols, e[4])[:, : e[5]])
-            off += e[4] * ncols
+            ents.append((name, W, xs[grp], rows, per, hi - lo, lo))
+        if peer:
+            # this layer's full outputs live in the shared buffer; the shard
+            # writes its rows there and the kernel stores them into every peer
+            base, outs = li * layer_elems, []
+            for e in ents:
+                full = pg.out[base: base + e[3] * ncols].view(ncols, e[3])
+                outs.append(full[:, e[6]: e[6] + e[5]])
+                base += e[3] * ncols
+            ybuf, gath = pg.out[li * layer_elems: (li + 1) * layer_elems], None
+        else:
+            # local outputs packed so one all-gather covers the layer
+            per_tot = sum(e[4] for e in ents)
+            ybuf = torch.zeros((per_tot * ncols,), device=dev)
+            outs, off = [], 0
+            for e in ents:
+                outs.append(ybuf[off: off + e[4] * ncols].view(ncols, e[4])[:, : e[5]])
+                off += e[4] * ncols
+            gath = torch.empty((per_tot * ncols * world,), device=dev) if world > 1 else None
         tasks = q4k.make_tasks([e[1] for e in ents], [e[2] for e in ents], outs)
-        gath = torch.empty((per_tot * ncols * world,), device=dev) if world > 1 else None
+        for i, e in enumerate(ents):
+            tasks[i].stride_col_dst = e[3] if peer else e[4]
         layers.append(dict(xs=xs, ents=ents, ybuf=ybuf, outs=outs, tasks=tasks, gath=gath))
     hlo, hhi, hper = shard(HEAD[0], rank, world)
     head_W = q4k.gen_q4k_torch(hhi - hlo, HEAD[1], generator=g, device=dev)
     head_x = torch.randn((ncols, HEAD[1]), device=dev, generator=g)
-    head_y = torch.zeros((hper * ncols,), device=dev)
-    head_out = head_y.view(ncols, hper)[:, : hhi - hlo]
+    if peer:
+        hbase = nlayers * layer_elems
+        head_y = pg.out[hbase: hbase + HEAD[0] * ncols]
+        head_out = head_y.view(ncols, HEAD[0])[:, hlo:hhi]
+        head_gath = None
+    else:
+        head_y = torch.zeros((hper * ncols,), device=dev)
+        head_out = head_y.view(ncols, hper)[:, : hhi - hlo]
+        head_gath = torch.empty((hper * ncols * world,), device=dev) if world > 1 else None
     head_tasks = q4k.make_tasks([head_W], [head_x], [head_out])
-    head_gath = torch.empty((hper * ncols * world,), device=dev) if world > 1 else None
+    head_tasks[0].stride_col_dst = HEAD[0] if peer else hper
 
     ws_bytes = max([q4k.batch_workspace_bytes(L["tasks"], ncols) for L in layers] +
                    [q4k.batch_workspace_bytes(head_tasks, ncols)])
     ws = q4k.Workspace(ws_bytes, dev)
     stream = torch.cuda.Stream(device=dev)
 
+    def gemv(tasks):
+        if peer:
+            q4k.gemv_batch_allgather(tasks, ncols, pg, ws, stream=stream)
+        else:
+            q4k.gemv_batch(tasks, ncols, ws, stream=stream)
+
     def run_step(ev=None):
         for li, L in enumerate(layers):
             if ev is not None:
                 ev[li][0].record(stream)
-            q4k.gemv_batch(L["tasks"], ncols, ws, stream=stream)
+            gemv(L["tasks"])
             if ev is not None:
                 ev[li][1].record(stream)
-            if world > 1:
+            if world > 1 and not peer:
                 dist.all_gather_into_tensor(L["gath"], L["ybuf"])
-        q4k.gemv_batch(head_tasks, ncols, ws, stream=stream)
-        if world > 1:
+        gemv(head_tasks)
+        if world > 1 and not peer:
             dist.all_gather_into_tensor(head_gath, head_y)
 
     # ---- one untimed step: checks the device status word before timing ------
@@ -397,7 +427,7 @@ def main():
     e2e = None
     if not args.no_e2e:
         xs_all = [L["xs"][grp] for L in layers for grp in ACT_K] + [head_x]
-        ys_all = [L["ybuf"] for L in layers] + [head_y]
+        ys_all = [pg.out] if peer else [L["ybuf"] for L in layers] + [head_y]
         h_x = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in xs_all]
         for h, d in zip(h_x, xs_all):
             h.copy_(d)
@@ -461,7 +491,9 @@ def main():
                        "timing": "one CUDA graph per step (launches chained with programmatic dependencies), "
                                  "CUDA events on the launch stream around all timed steps",
                        "l2": "inputs larger than L2 (4.0 GB of weights per step, no flush needed)",
-                       "parallelism": "single GPU" if world == 1 else f"row-shard x{world} + NCCL all-gather per layer"},
+                       "parallelism": "single GPU" if world == 1 else (
+                           f"row-shard x{world}, outputs all-gathered inside the GEMV over NVLink peer stores"
+                           if peer else f"row-shard x{world} + NCCL all-gather per layer")},
             "us_per_call": launch_us,
             "us_per_layer_launch_isolated": iso_ms * 1e3,
             "pct_hbm_peak": 100.0 * value * 1e3 / world / peak,
@@ -480,7 +512,10 @@ def main():
 
     if world > 1:
         step_graph = None
+        torch.cuda.synchronize(dev)
         dist.barrier()
+        if pg is not None:
+            pg.close()
         dist.destroy_process_group()
 
 

@@ -49,6 +49,16 @@ class Q4KError(RuntimeError):
         self.status = status
 
 
+MAX_PEERS = 8
+
+
+class Gather(ctypes.Structure):
+    """struct q4k_gather (include/q4k_gemv.h)."""
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("out_local", ctypes.c_void_p),
+                ("out_peer", ctypes.c_void_p * MAX_PEERS), ("flags_peer", ctypes.c_void_p * MAX_PEERS),
+                ("epoch", ctypes.c_void_p)]
+
+
 class Task(ctypes.Structure):
     """struct q4k_task (include/q4k_gemv.h)."""
     _fields_ = [("W", ctypes.c_void_p), ("x", ctypes.c_void_p), ("dst", ctypes.c_void_p),
@@ -99,6 +109,12 @@ def lib() -> ctypes.CDLL:
         L.q4k_debug_subblock_sums.argtypes = [_P, _P, _I64, _I64, _I, _I64, _I64, _P, _P, _P, _SZ, _P]
         L.q4k_workspace_status.argtypes = [_P, ctypes.POINTER(_I), _P]
         L.q4k_mul_mat_vec_noalloc.argtypes = [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P]
+        L.q4k_gemv_batch_allgather.argtypes = [ctypes.POINTER(Task), _I, _I, ctypes.POINTER(Gather), _P, _SZ, _P]
+        L.q4k_ipc_alloc.argtypes = [_SZ, ctypes.POINTER(ctypes.c_void_p)]
+        L.q4k_ipc_free.argtypes = [_P]
+        L.q4k_ipc_handle.argtypes = [_P, ctypes.c_char_p]
+        L.q4k_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+        L.q4k_ipc_close.argtypes = [_P]
         L.q4k_noalloc_scratch_bytes.restype = _SZ
         _lib = L
     return _lib
@@ -340,3 +356,106 @@ def gen_q4k_torch(nrows: int, K: int, generator=None, device="cuda"):
     d = (torch.randn((nrows, nb, 2), device=device, generator=generator).abs_() * 0.01).to(torch.float16)
     W[:, :, 0:4] = d.view(torch.uint8).reshape(nrows, nb, 4)
     return W.view(nrows, nb * BLOCK_BYTES)
+
+
+# ---------------------------------------------------------------------------
+# row-sharded multi-GPU (one process per GPU)
+# ---------------------------------------------------------------------------
+def shard_rows(rows: int, rank: int, world: int) -> tuple[int, int, int]:
+    """Contiguous ceil-split rows [lo, hi) of rank, and the per-rank capacity.
+
+    The reference's row split gives each device a contiguous row range
+    (kernels/mmvq.cu:764-793); trailing ranks may get fewer (or no) rows."""
+    per = (rows + world - 1) // world
+    lo = min(rows, rank * per)
+    return lo, min(rows, lo + per), per
+
+
+class DeviceBuffer:
+    """A torch view of device memory the library allocated (for IPC)."""
+
+    def __init__(self, ptr: int, nbytes: int, device):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+        self.device = device
+
+    def tensor(self):
+        import torch
+        return torch.as_tensor(self, device=self.device)
+
+
+class PeerGather:
+    """Full-output buffers shared by all ranks for q4k_gemv_batch_allgather.
+
+    Collective over the default torch.distributed group: every rank allocates
+    `out_elems` fp32 outputs + its flag words + its epoch word with
+    q4k_ipc_alloc, the 64-byte IPC handles are exchanged with all_gather_object,
+    and every peer's buffers are mapped with q4k_ipc_open.  `out` is this rank's
+    full output as a float32 tensor; outputs of this rank's shard of a matrix
+    go at its own row offset inside it, and every launch fills all rows."""
+
+    def __init__(self, out_elems: int):
+        import torch
+        import torch.distributed as dist
+        L = lib()
+        self.world = dist.get_world_size()
+        self.rank = dist.get_rank()
+        if self.world > MAX_PEERS:
+            raise Q4KError(1, f"world size {self.world} > {MAX_PEERS}")
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self._own = []
+        self._opened = []
+
+        def alloc(nbytes):
+            p = ctypes.c_void_p()
+            _check(L.q4k_ipc_alloc(nbytes, ctypes.byref(p)))
+            self._own.append(p.value)
+            return p.value
+
+        out_bytes = (out_elems * 4 + 255) // 256 * 256
+        out_ptr = alloc(out_bytes)
+        flags_ptr = alloc(256)
+        epoch_ptr = alloc(256)
+
+        def handle(ptr):
+            h = ctypes.create_string_buffer(64)
+            _check(L.q4k_ipc_handle(ptr, h))
+            return h.raw
+
+        mine = (handle(out_ptr), handle(flags_ptr))
+        allh = [None] * self.world
+        dist.all_gather_object(allh, mine)
+        g = Gather()
+        g.world, g.rank = self.world, self.rank
+        g.out_local = out_ptr
+        g.epoch = epoch_ptr
+        for q in range(self.world):
+            if q == self.rank:
+                g.out_peer[q], g.flags_peer[q] = out_ptr, flags_ptr
+                continue
+            ptrs = []
+            for h in allh[q]:
+                p = ctypes.c_void_p()
+                _check(L.q4k_ipc_open(h, ctypes.byref(p)))
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+            g.out_peer[q], g.flags_peer[q] = ptrs
+        self.desc = g
+        self.out = DeviceBuffer(out_ptr, out_elems * 4, self.device).tensor().view(torch.float32)
+        dist.barrier()
+
+    def close(self):
+        L = lib()
+        for p in self._opened:
+            L.q4k_ipc_close(p)
+        self._opened = []
+        for p in self._own:
+            L.q4k_ipc_free(p)
+        self._own = []
+
+
+def gemv_batch_allgather(tasks, ncols: int, gather: PeerGather, ws: Workspace, stream=None) -> None:
+    """q4k_gemv_batch on this rank's row shards, outputs gathered into every rank's buffer."""
+    ws.ensure(batch_workspace_bytes(tasks, ncols))
+    _check(lib().q4k_gemv_batch_allgather(tasks, len(tasks), ncols, ctypes.byref(gather.desc), ws.ptr, ws.nbytes,
+                                          _stream(stream)))

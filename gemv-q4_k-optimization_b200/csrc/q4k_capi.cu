@@ -266,8 +266,19 @@ int zero_outputs(const Job *jobs, int njobs, int ncols, cudaStream_t s) {
     return Q4K_OK;
 }
 
+int validate_gather(const q4k_gather *g) {
+    if (!g) return fail(Q4K_EINVAL, "gather descriptor is null");
+    if (g->world < 1 || g->world > Q4K_MAX_PEERS) return fail(Q4K_EINVAL, "gather world=%d outside 1..8", g->world);
+    if (g->rank < 0 || g->rank >= g->world) return fail(Q4K_EINVAL, "gather rank=%d outside 0..world-1", g->rank);
+    if (!g->out_local || !g->epoch) return fail(Q4K_EINVAL, "gather out_local/epoch is null");
+    for (int q = 0; q < g->world; ++q)
+        if (!g->out_peer[q] || !g->flags_peer[q]) return fail(Q4K_EINVAL, "gather peer %d pointers are null", q);
+    if (g->out_peer[g->rank] != g->out_local) return fail(Q4K_EINVAL, "gather out_peer[rank] != out_local");
+    return Q4K_OK;
+}
+
 int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes, cudaStream_t s,
-        int32_t *dump_S = nullptr, int32_t *dump_T = nullptr) {
+        int32_t *dump_S = nullptr, int32_t *dump_T = nullptr, const q4k_gather *gather = nullptr) {
     Plan P;
     // Arguments are validated before the device is touched.
     int st = make_plan(jobs, njobs, ncols, nullptr, kFallbackSMs, P);
@@ -279,7 +290,10 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     if (st != Q4K_OK) return st;
     st = zero_outputs(jobs, njobs, ncols, s);
     if (st != Q4K_OK) return st;
-    if (!P.any_work) return Q4K_OK;
+    // With a fused all-gather the launch happens even without local rows: the
+    // peers wait for this rank's epoch flag.
+    const bool gathering = gather && gather->world > 1;
+    if (!P.any_work && !gathering) return Q4K_OK;
     if (workspace == nullptr) return fail(Q4K_EWORKSPACE, "workspace is null");
     if (!aligned16(workspace)) return fail(Q4K_EWORKSPACE, "workspace is not 16-byte aligned");
     if (ws_bytes < P.layout.total)
@@ -287,6 +301,18 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     st = make_plan(jobs, njobs, ncols, static_cast<uint8_t *>(workspace), num_sms, P, dump_T);
     if (st != Q4K_OK) return st;
     P.gemv.dump_S = dump_S;
+    P.gemv.gworld = 1;
+    if (gather && gather->world > 1) {
+        P.gemv.gworld = gather->world;
+        P.gemv.grank = gather->rank;
+        P.gemv.gout_local = gather->out_local;
+        for (int q = 0; q < gather->world; ++q) {
+            P.gemv.gout_peer[q] = gather->out_peer[q];
+            P.gemv.gflags_peer[q] = gather->flags_peer[q];
+        }
+        P.gemv.gepoch = gather->epoch;
+        P.gemv.gdone = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace) + 4);
+    }
     if ((e = launch_prep(P.prep, s)) != cudaSuccess) return cuda_fail(e, "prep launch");
     if ((e = launch_gemv(P.gemv, ncols, dump_S != nullptr, num_sms, s)) != cudaSuccess)
         return cuda_fail(e, "gemv launch");
@@ -443,6 +469,59 @@ int q4k_gemv_batch(const q4k_task *tasks, int ntasks, int ncols, void *workspace
         jobs[i] = {tasks[i].W, tasks[i].x, tasks[i].dst, tasks[i].nrows, tasks[i].K,
                    tasks[i].stride_row_x, tasks[i].stride_col_x, tasks[i].stride_col_dst, kPrepF32};
     return run(jobs, ntasks, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int q4k_gemv_batch_allgather(const q4k_task *tasks, int ntasks, int ncols, const q4k_gather *gather,
+                             void *workspace, size_t workspace_bytes, q4k_stream_t stream) {
+    if (!tasks || ntasks < 1 || ntasks > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..16", ntasks);
+    int st = validate_gather(gather);
+    if (st != Q4K_OK) return st;
+    Job jobs[kMaxTasks];
+    for (int i = 0; i < ntasks; ++i) {
+        jobs[i] = {tasks[i].W, tasks[i].x, tasks[i].dst, tasks[i].nrows, tasks[i].K,
+                   tasks[i].stride_row_x, tasks[i].stride_col_x, tasks[i].stride_col_dst, kPrepF32};
+        if (tasks[i].nrows > 0 && tasks[i].K == 0)
+            return fail(Q4K_EINVAL, "task %d: K = 0 is not supported with a fused all-gather", i);
+    }
+    return run(jobs, ntasks, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr,
+               nullptr, gather);
+}
+
+int q4k_ipc_alloc(size_t bytes, void **ptr) {
+    if (!ptr || bytes == 0) return fail(Q4K_EINVAL, "q4k_ipc_alloc: null pointer or zero size");
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "q4k_ipc_alloc");
+    return Q4K_OK;
+}
+
+int q4k_ipc_free(void *ptr) {
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? Q4K_OK : cuda_fail(e, "q4k_ipc_free");
+}
+
+int q4k_ipc_handle(const void *ptr, void *handle64) {
+    if (!ptr || !handle64) return fail(Q4K_EINVAL, "q4k_ipc_handle: null pointer");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(ptr));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+    memcpy(handle64, &h, sizeof(h));
+    return Q4K_OK;
+}
+
+int q4k_ipc_open(const void *handle64, void **ptr) {
+    if (!ptr || !handle64) return fail(Q4K_EINVAL, "q4k_ipc_open: null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    return Q4K_OK;
+}
+
+int q4k_ipc_close(void *ptr) {
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? Q4K_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
 }
 
 int q4k_debug_subblock_sums(const void *W, const void *y_q8_1, int64_t K, int64_t nrows, int ncols,

@@ -16,6 +16,7 @@ constexpr int kActMetaOff = 256;  // q8a: offset of the per-pair float4 metadata
 constexpr int kMaxCols = 8;
 constexpr int kMaxTasks = 16;
 constexpr int kMaxJobs = 16;
+constexpr int kMaxPeers = 8;
 
 // GEMV geometry.  A "worker" is one warp; it owns a contiguous range of
 // "atoms" (32 weight rows x kKS super-blocks, plus the kKS activation records
@@ -59,6 +60,7 @@ constexpr int kStatusTimeout = 3;
 // Bounded waits: a bulk copy that has not landed after this long is an error.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 constexpr unsigned long long kDrainLimitNs = 20000000ull;   // 20 ms
+constexpr unsigned long long kPeerWaitLimitNs = 2000000000ull;  // 2 s for the peers' epoch
 
 struct TaskDesc {
     const uint8_t *W;        // weight row 0 (16-byte aligned)
@@ -89,6 +91,16 @@ struct GemvParams {
     float *partials;         // [nworkers][2][ncols][32]
     int32_t *status;
     int32_t *dump_S;         // debug: sub-block sums (nullptr in the product path)
+    // Fused all-gather over peer memory (gworld > 1): every output value is
+    // also stored at the same offset from gout_peer[q] for each peer q, and
+    // the grid's last CTA exchanges an epoch with every peer before exiting.
+    int32_t gworld;
+    int32_t grank;
+    float *gout_local;               // this rank's full output buffer
+    float *gout_peer[kMaxPeers];     // every rank's full output buffer, mapped here
+    uint32_t *gflags_peer[kMaxPeers];// every rank's flag words (one per sender), mapped here
+    uint32_t *gepoch;                // this rank's epoch word (persists across calls)
+    uint32_t *gdone;                 // CTAs finished (workspace; zero at kernel start)
 };
 
 enum PrepKind : int32_t { kPrepF32 = 0, kPrepQ81 = 1 };

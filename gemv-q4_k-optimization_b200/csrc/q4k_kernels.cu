@@ -291,6 +291,18 @@ __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCurs
     }
 }
 
+// Store one output value; with a fused all-gather also into every peer's
+// full output buffer (same offset, plain stores over NVLink).
+__device__ __forceinline__ void store_out(const GemvParams &P, const TaskDesc &T, int j, int row, float v) {
+    float *p = T.dst + j * T.dst_col_stride + row;
+    *p = v;
+    if (P.gworld > 1) {
+        const int64_t off = p - P.gout_local;
+        for (int q = 0; q < P.gworld; ++q)
+            if (q != P.grank) P.gout_peer[q][off] = v;
+    }
+}
+
 // Finish a row group this warp worked on: write it out directly if the warp
 // covered all of its atoms, otherwise deposit the partial sums and let the
 // last of the contributing warps add them up (always in worker order, so the
@@ -315,7 +327,7 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
     if (sg >= a0 && eg <= a1) {
         if (!DUMP && valid) {
 #pragma unroll
-            for (int j = 0; j < NC; ++j) T.dst[j * T.dst_col_stride + row] = v[j];
+            for (int j = 0; j < NC; ++j) store_out(P, T, j, row, v[j]);
         }
         return;
     }
@@ -350,7 +362,7 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
     }
     if (!DUMP && valid) {
 #pragma unroll
-        for (int j = 0; j < NC; ++j) T.dst[j * T.dst_col_stride + row] = tot[j];
+        for (int j = 0; j < NC; ++j) store_out(P, T, j, row, tot[j]);
     }
     if (lane == 0) {
         if (local)
@@ -360,42 +372,17 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
     }
 }
 
+// One worker's whole range: stream its atoms through the warp's ring and
+// flush its row groups.  Returns (never exits the kernel) so that a fused
+// all-gather can still run its CTA-wide epilogue.
 template <int NC, bool DUMP>
-__global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
-    constexpr int kW = warps_for(NC);
+__device__ __forceinline__ void run_worker(const GemvParams &P, int64_t worker, int lane, uint32_t ring,
+                                           const uint32_t (&bar)[kStages], int64_t cta_w0, int64_t cta_w1,
+                                           int *cta_cnt) {
     constexpr int kSB = Stage<NC>::kBytes;
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bars[kW][kStages];
-    __shared__ int cta_cnt[kW];  // arrivals at row groups split between this CTA's warps
-
-    // The next prep launch may start now; it waits for this grid's completion
-    // before it touches the workspace.
-    pdl_launch_dependents();
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    if (threadIdx.x < kW) cta_cnt[threadIdx.x] = 0;
-    __syncthreads();
-    // Large problems: CTA-contiguous worker ranges (most split row groups stay
-    // inside a CTA).  Small ones: consecutive workers on different SMs.
-    const int64_t worker = P.packed ? static_cast<int64_t>(blockIdx.x) * kW + warp
-                                    : static_cast<int64_t>(warp) * gridDim.x + blockIdx.x;
-    const int64_t cta_w0 = static_cast<int64_t>(blockIdx.x) * kW;
-    const int64_t cta_w1 = cta_w0 + kW - 1;
-    if (worker >= P.nworkers) return;
     const int64_t a0 = worker_begin(P, worker);
     const int64_t a1 = worker_begin(P, worker + 1);
     const int n = static_cast<int>(a1 - a0);
-
-    const uint32_t ring = smem_addr(smem) + static_cast<uint32_t>(warp * kStages * kSB);
-    uint32_t bar[kStages];
-#pragma unroll
-    for (int s = 0; s < kStages; ++s) bar[s] = smem_addr(&bars[warp][s]);
-    if (lane == 0) {
-#pragma unroll
-        for (int s = 0; s < kStages; ++s) mbar_init(bar[s], 1);
-        mbar_fence_init();
-    }
-    __syncwarp();
 
     // Weight bytes do not depend on the prep kernel: start streaming now,
     // activations once the prep grid has completed.
@@ -455,6 +442,80 @@ __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_con
     if (open_t >= 0) {
         AtomCursor o{open_t, open_g, 0};
         flush_group<NC, DUMP>(P, o, acc, worker, a0, a1, lane, cta_w0, cta_w1, cta_cnt);
+    }
+}
+
+// Fused all-gather epilogue: after every CTA of this grid has stored its
+// outputs (locally and into the peers' buffers), the last CTA to finish
+// publishes epoch+1 in each peer's flag word for this rank (release, system
+// scope) and waits, bounded, until every peer has published the same epoch
+// here.  The grid therefore completes only when the full output is in this
+// rank's buffer.  The epoch word persists across calls, so replays of a
+// captured sequence keep counting.
+__device__ __forceinline__ void gather_epilogue(const GemvParams &P) {
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    const uint32_t old = atomicAdd(P.gdone, 1u);
+    if (old != gridDim.x - 1) return;
+    __threadfence_system();
+    const uint32_t e = *reinterpret_cast<volatile uint32_t *>(P.gepoch) + 1u;
+    for (int q = 0; q < P.gworld; ++q)
+        if (q != P.grank) st_release_sys_u32(P.gflags_peer[q] + P.grank, e);
+    const uint32_t *mine = P.gflags_peer[P.grank];
+    const uint64_t t0 = globaltimer_ns();
+    bool ok = true;
+    for (int q = 0; q < P.gworld && ok; ++q) {
+        if (q == P.grank) continue;
+        for (uint32_t it = 0;; ++it) {
+            if (static_cast<int32_t>(ld_acquire_sys_u32(mine + q) - e) >= 0) break;
+            if ((it & 63u) == 0 && globaltimer_ns() - t0 > kPeerWaitLimitNs) {
+                ok = false;
+                break;
+            }
+        }
+    }
+    if (!ok) atomicExch(P.status, kStatusTimeout);
+    *reinterpret_cast<volatile uint32_t *>(P.gepoch) = e;
+}
+
+template <int NC, bool DUMP>
+__global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
+    constexpr int kW = warps_for(NC);
+    constexpr int kSB = Stage<NC>::kBytes;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bars[kW][kStages];
+    __shared__ int cta_cnt[kW];  // arrivals at row groups split between this CTA's warps
+
+    // The next prep launch may start now; it waits for this grid's completion
+    // before it touches the workspace.
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x < kW) cta_cnt[threadIdx.x] = 0;
+    __syncthreads();
+    // Large problems: CTA-contiguous worker ranges (most split row groups stay
+    // inside a CTA).  Small ones: consecutive workers on different SMs.
+    const int64_t worker = P.packed ? static_cast<int64_t>(blockIdx.x) * kW + warp
+                                    : static_cast<int64_t>(warp) * gridDim.x + blockIdx.x;
+    const int64_t cta_w0 = static_cast<int64_t>(blockIdx.x) * kW;
+    const int64_t cta_w1 = cta_w0 + kW - 1;
+    if (worker < P.nworkers) {
+        const uint32_t ring = smem_addr(smem) + static_cast<uint32_t>(warp * kStages * kSB);
+        uint32_t bar[kStages];
+#pragma unroll
+        for (int s = 0; s < kStages; ++s) bar[s] = smem_addr(&bars[warp][s]);
+        if (lane == 0) {
+#pragma unroll
+            for (int s = 0; s < kStages; ++s) mbar_init(bar[s], 1);
+            mbar_fence_init();
+        }
+        __syncwarp();
+        run_worker<NC, DUMP>(P, worker, lane, ring, bar, cta_w0, cta_w1, cta_cnt);
+    }
+    if (!DUMP && P.gworld > 1) {
+        pdl_wait();  // idle warps too: the epilogue touches the workspace
+        gather_epilogue(P);
     }
 }
 

@@ -159,6 +159,45 @@ Q4K_API size_t q4k_batch_workspace_bytes(const q4k_task *tasks, int ntasks, int 
 Q4K_API int q4k_gemv_batch(const q4k_task *tasks, int ntasks, int ncols,
                    void *workspace, size_t workspace_bytes, q4k_stream_t stream);
 
+/* ---- row-sharded multi-GPU: GEMV fused with the output all-gather ------------- */
+
+/* Row-split across GPUs is the reference's multi-GPU mode (mmvq.cu:764-793,
+ * the main device then collects the slices).  Here every rank computes its
+ * rows and, in the same kernel, stores them straight into every rank's full
+ * output buffer over NVLink (peer memory), then exchanges one epoch flag with
+ * each peer: when the launch completes on a rank, that rank's buffer holds
+ * all rows.  Every rank must make the same sequence of calls. */
+#define Q4K_MAX_PEERS 8
+
+typedef struct q4k_gather {
+    int world;                        /* ranks, 1..Q4K_MAX_PEERS */
+    int rank;                         /* this rank */
+    float *out_local;                 /* this rank's full output buffer */
+    float *out_peer[Q4K_MAX_PEERS];   /* each rank's full output buffer, mapped in this process
+                                         (out_peer[rank] == out_local) */
+    uint32_t *flags_peer[Q4K_MAX_PEERS]; /* each rank's flag words (world of them), mapped here */
+    uint32_t *epoch;                  /* this rank's epoch word, zero before the first call */
+} q4k_gather;
+
+/* q4k_gemv_batch over this rank's row shards, gathered into every rank's
+ * buffer.  Each task's dst must point into out_local at this rank's first
+ * row of that matrix (all ranks use the same layout of the full buffer).
+ * A rank stores into its peers' buffers as soon as its launch runs: a region
+ * of the full buffer may be rewritten only once every rank is done reading
+ * it (use different regions for consecutive calls, e.g. one per layer, or
+ * synchronise the ranks before reuse). */
+Q4K_API int q4k_gemv_batch_allgather(const q4k_task *tasks, int ntasks, int ncols, const q4k_gather *gather,
+                                     void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+
+/* Set-up helpers for the buffers above (not on the call path): device memory
+ * that other processes can map (zero-filled), its 64-byte IPC handle, and
+ * mapping / unmapping a peer's buffer from its handle. */
+Q4K_API int q4k_ipc_alloc(size_t bytes, void **ptr);
+Q4K_API int q4k_ipc_free(void *ptr);
+Q4K_API int q4k_ipc_handle(const void *ptr, void *handle64);
+Q4K_API int q4k_ipc_open(const void *handle64, void **ptr);
+Q4K_API int q4k_ipc_close(void *ptr);
+
 /* ---- callers that cannot allocate --------------------------------------------- */
 
 /* q4k_mul_mat_vec without a caller workspace.  No counterpart in the reference.
