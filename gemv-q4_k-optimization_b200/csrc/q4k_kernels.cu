@@ -447,36 +447,40 @@ __device__ __forceinline__ void run_worker(const GemvParams &P, int64_t worker, 
 
 // Fused all-gather epilogue: after every CTA of this grid has stored its
 // outputs (locally and into the peers' buffers), the last CTA to finish
-// publishes epoch+1 in each peer's flag word for this rank (release, system
-// scope) and waits, bounded, until every peer has published the same epoch
-// here.  The grid therefore completes only when the full output is in this
-// rank's buffer.  The epoch word persists across calls, so replays of a
-// captured sequence keep counting.
+// publishes epoch+1 in each peer's flag word for this rank and waits, bounded,
+// until every peer has published the same epoch here.  The grid therefore
+// completes only when the full output is in this rank's buffer.  The epoch
+// word persists across calls, so replays of a captured sequence keep counting.
+// Ordering: each CTA's peer stores -> block barrier -> release fence (system
+// scope) -> arrival count; the last CTA's acquire fence -> per-peer release
+// stores of the flag (one lane per peer, in parallel) -> peers' acquire loads.
 __device__ __forceinline__ void gather_epilogue(const GemvParams &P) {
+    __shared__ int last_cta;
     __syncthreads();
-    if (threadIdx.x != 0) return;
-    __threadfence_system();
-    const uint32_t old = atomicAdd(P.gdone, 1u);
-    if (old != gridDim.x - 1) return;
-    __threadfence_system();
+    if (threadIdx.x == 0) {
+        fence_acq_rel_sys();
+        last_cta = atomicAdd(P.gdone, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last_cta || threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
+    if (lane == 0) fence_acq_rel_sys();
+    __syncwarp();
     const uint32_t e = *reinterpret_cast<volatile uint32_t *>(P.gepoch) + 1u;
-    for (int q = 0; q < P.gworld; ++q)
-        if (q != P.grank) st_release_sys_u32(P.gflags_peer[q] + P.grank, e);
+    const bool peer = lane < P.gworld && lane != P.grank;
+    if (peer) st_release_sys_u32(P.gflags_peer[lane] + P.grank, e);
     const uint32_t *mine = P.gflags_peer[P.grank];
     const uint64_t t0 = globaltimer_ns();
-    bool ok = true;
-    for (int q = 0; q < P.gworld && ok; ++q) {
-        if (q == P.grank) continue;
-        for (uint32_t it = 0;; ++it) {
-            if (static_cast<int32_t>(ld_acquire_sys_u32(mine + q) - e) >= 0) break;
-            if ((it & 63u) == 0 && globaltimer_ns() - t0 > kPeerWaitLimitNs) {
-                ok = false;
-                break;
-            }
+    bool done = !peer;
+    for (uint32_t it = 0;; ++it) {
+        if (!done) done = static_cast<int32_t>(ld_acquire_sys_u32(mine + lane) - e) >= 0;
+        if (__all_sync(0xffffffffu, done)) break;
+        if ((it & 63u) == 0 && globaltimer_ns() - t0 > kPeerWaitLimitNs) {
+            if (lane == 0) atomicExch(P.status, kStatusTimeout);
+            break;
         }
     }
-    if (!ok) atomicExch(P.status, kStatusTimeout);
-    *reinterpret_cast<volatile uint32_t *>(P.gepoch) = e;
+    if (lane == 0) *reinterpret_cast<volatile uint32_t *>(P.gepoch) = e;
 }
 
 template <int NC, bool DUMP>
