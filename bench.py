@@ -1,25 +1,27 @@
 #!/usr/bin/env python
 """Q4_K x q8_1 decode-GEMV benchmark on B200.
 
-Workload ("mistral-7b-decode-gemv-set"): one decode step's
-Q4_K GEMVs of Mistral-7B at batch 1 -- 32 layers x {q 4096x4096, k 1024x4096,
-v 1024x4096, o 4096x4096, gate 14336x4096, up 14336x4096, down 4096x14336}
-plus the 32000x4096 output head, synthetic seeded weights with the BASELINE
-value distributions (d, dmin = fp16(|N(0,1)|*0.01), uniform 6-bit scales/mins,
-uniform nibbles) and x ~ N(0,1) (one activation per matrix group: q/k/v share
-one, gate/up share one).  One prep + persistent GEMV launch pair per layer.
-The 4.0 GB of weights per step exceed the 126 MB L2, so every step streams
-from HBM.
+Default workload ("mistral-7b-decode-gemv-set"): one decode
+step's Q4_K GEMVs of Mistral-7B at batch 1 -- 32 layers x {q 4096x4096, k
+1024x4096, v 1024x4096, o 4096x4096, gate 14336x4096, up 14336x4096, down
+4096x14336} plus the 32000x4096 output head, synthetic seeded weights with
+the BASELINE value distributions (d, dmin = fp16(|N(0,1)|*0.01), uniform 6-bit
+scales/mins, uniform nibbles; generated on the device) and x ~ N(0,1) (q/k/v
+share one activation, gate/up share one).  One prep + persistent GEMV launch
+pair per layer.  The 4.0 GB of weights per step exceed the 126 MB L2, so
+every step streams from HBM.  Other BASELINE configs: --config 1/3/4/5/5t.
 
-Metric: achieved algorithmic HBM bandwidth of the whole job (TB/s, whole
-job over all ranks) with bytes = rows*K*0.5625 + ncols*K*4 per distinct
-activation + ncols*rows*4; also reported as us per GEMV launch.
+Metric: achieved algorithmic HBM bandwidth of the whole job (TB/s, all
+ranks) with bytes = rows*K*0.5625 + ncols*K*4 per distinct activation +
+ncols*rows*4; also us per GEMV launch.
 
-  python bench.py [--gpus N --steps K --warmup W --ncols C]
+  python bench.py [--gpus N --steps K --warmup W --ncols C --config 2]
   python bench.py --impl reference    # the reference's CPU path, timed on the host
 
 N > 1 (torchrun, one rank per GPU): every matrix is row-sharded across the
-ranks and each layer's output slices are all-gathered over NCCL.
+ranks; by default each launch also all-gathers the output rows into every
+rank's buffer over NVLink peer stores (--gather nccl: NCCL all_gather per
+launch instead).
 """
 from __future__ import annotations
 
@@ -39,16 +41,44 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 PKG_DIR = ROOT / "gemv-q4_k-optimization_b200"
 PROFILES = ROOT / "profiles"
-
-LAYERS = 32
-# (name, rows, K, activation group)
-MATS = [("q", 4096, 4096, "attn"), ("k", 1024, 4096, "attn"), ("v", 1024, 4096, "attn"),
-        ("o", 4096, 4096, "o"), ("gate", 14336, 4096, "ffn"), ("up", 14336, 4096, "ffn"),
-        ("down", 4096, 14336, "down")]
-ACT_K = {"attn": 4096, "o": 4096, "ffn": 4096, "down": 14336}
-HEAD = (32000, 4096)
-WORKLOAD = "mistral-7b-decode-gemv-set"
 METRIC = "Q4_K GEMV achieved HBM TB/s (algorithmic bytes), us per GEMV launch"
+
+# A launch group is one q4k_gemv_batch launch: (name, rows, K, activation group).
+MISTRAL_LAYER = [("q", 4096, 4096, "attn"), ("k", 1024, 4096, "attn"), ("v", 1024, 4096, "attn"),
+                 ("o", 4096, 4096, "o"), ("gate", 14336, 4096, "ffn"), ("up", 14336, 4096, "ffn"),
+                 ("down", 4096, 14336, "down")]
+LLAMA70B_LAYER = [("q", 8192, 8192, "attn"), ("k", 1024, 8192, "attn"), ("v", 1024, 8192, "attn"),
+                  ("o", 8192, 8192, "o"), ("gate", 28672, 8192, "ffn"), ("up", 28672, 8192, "ffn"),
+                  ("down", 8192, 28672, "down")]
+# BASELINE config -> (workload name, repeated launch group, default repeats, trailing groups)
+WORKLOADS = {
+    "2": ("mistral-7b-decode-gemv-set", MISTRAL_LAYER, 32, [[("head", 32000, 4096, "head")]]),
+    "1": ("single-4096x4096", [("attn_q", 4096, 4096, "x")], 48, []),
+    "3": ("ffn-up-14336x4096", [("ffn_up", 14336, 4096, "x")], 16, []),
+    "4": ("llama-3-70b-layer-gemvs", LLAMA70B_LAYER, 8, []),
+    "5": ("head-128256x8192", [("head", 128256, 8192, "x")], 6, []),
+    "5t": ("tiny-1024x4096-and-512x4096", [("tiny_1024", 1024, 4096, "x")], 256, []),
+}
+
+
+def build_groups(cfg: str, repeats: int):
+    name, group, _, tail = WORKLOADS[cfg]
+    groups = [list(group) for _ in range(repeats)]
+    if cfg == "5t":  # alternate the two tiny shapes, one launch each
+        groups = [[("tiny_1024", 1024, 4096, "x")] if i % 2 == 0 else [("tiny_512", 512, 4096, "x")]
+                  for i in range(repeats)]
+    return name, groups + [list(t) for t in tail]
+
+
+def group_bytes(group, ncols: int, world: int = 1) -> int:
+    """Algorithmic bytes of one launch group, all ranks (every rank reads the whole x)."""
+    acts = {}
+    for _, r, K, a in group:
+        acts[a] = K
+    w = sum(r * K * 9 // 16 for _, r, K, _ in group)
+    x = sum(ncols * K * 4 for K in acts.values()) * world
+    y = sum(ncols * r * 4 for _, r, _, _ in group)
+    return w + x + y
 
 
 def load_package():
@@ -75,24 +105,6 @@ def measured_peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
-
-
-def shard(rows: int, rank: int, world: int):
-    """Contiguous ceil-split row range [lo, hi) of rank (tails may be short)."""
-    per = (rows + world - 1) // world
-    lo = min(rows, rank * per)
-    return lo, min(rows, lo + per), per
-
-
-def step_bytes(ncols: int, world: int = 1, layers: int = LAYERS) -> dict:
-    """Algorithmic bytes of one decode step, whole job (all ranks)."""
-    w = sum(r * K * 9 // 16 for _, r, K, _ in MATS) * layers + HEAD[0] * HEAD[1] * 9 // 16
-    x_layer = sum(ncols * K * 4 for K in ACT_K.values())
-    y_layer = sum(ncols * r * 4 for _, r, _, _ in MATS)
-    x = (x_layer * layers + ncols * HEAD[1] * 4) * world  # every rank reads the whole x
-    y = y_layer * layers + ncols * HEAD[0] * 4
-    layer = sum(r * K * 9 // 16 for _, r, K, _ in MATS) + x_layer + y_layer
-    return {"total": w + x + y, "weights": w, "per_layer_launch": layer}
 
 
 # ---------------------------------------------------------------------------
@@ -154,24 +166,33 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# reference arm: the reference's own CPU code path (host cores)
+# CPU legs (the oracle and the reference's own dot product; checkers only)
 # ---------------------------------------------------------------------------
+def host_group(q4k, group, ncols, rng):
+    mats = [(q4k.gen_q4k_numpy(rng, r, K), K, a) for _, r, K, a in group]
+    xs = {a: rng.standard_normal((ncols, K)).astype(np.float32) for _, _, K, a in group}
+    return mats, xs
+
+
 def run_reference(args) -> None:
+    """The reference's CPU implementation of the path (its vec_dot_q4_K_q8_1
+    compiled for the host, oracle/_ref), all host threads, one launch group
+    per step (a decoder layer for config 2)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     O = load_oracle()
     q4k = load_package()
     kind = "reference" if O.ref_available() else "port"
-    rng = np.random.default_rng(0)
+    name, groups = build_groups(args.config, 1)
+    group = groups[0]
     ncols = args.ncols
-    mats = [(q4k.gen_q4k_numpy(rng, r, K), K, grp) for _, r, K, grp in MATS]
-    xs = {g: rng.standard_normal((ncols, K)).astype(np.float32) for g, K in ACT_K.items()}
+    mats, xs = host_group(q4k, group, ncols, np.random.default_rng(0))
     threads = O.max_threads() if kind == "port" else O.ref_lib().ref_max_threads()
 
     def one_step():
-        for W, K, grp in mats:
-            yq = O.quantize_q8_1(xs[grp])
+        for W, K, a in mats:
+            yq = O.quantize_q8_1(xs[a])
             if kind == "reference":
                 O.ref_gemv_q8_1(W, K, yq, nthreads=threads)
             else:
@@ -183,54 +204,55 @@ def run_reference(args) -> None:
     for _ in range(args.steps):
         one_step()
     dt = (time.perf_counter() - t0) / args.steps
-    sample_bytes = step_bytes(ncols)["per_layer_launch"]
-    tbs = sample_bytes / dt / 1e12
+    tbs = group_bytes(group, ncols) / dt / 1e12
+    sample = (f"one launch group of {name} per step ({len(group)} Q4_K GEMVs, "
+              f"{group_bytes(group, ncols) / 1e6:.1f} MB algorithmic), q8_1 quantization included; "
+              f"{'the reference vec_dot_q4_K_q8_1 in MMVQ order' if kind == 'reference' else 'the C oracle'}")
     line = {
         "impl": "reference", "metric": METRIC, "value": tbs, "unit": "TB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "ncols": ncols, "sample": "one decoder layer (7 matrices) per step"},
-        "cpu_baseline": {"value": tbs, "unit": "TB/s", "cores": threads, "kind": kind,
-                         "sample": "one Mistral-7B decoder layer's 7 Q4_K GEMVs (122.7 MB of weights) per step, "
-                                   "q8_1 quantization included"},
+        "config": {"workload": name, "ncols": ncols, "sample": "one launch group per step"},
+        "cpu_baseline": {"value": tbs, "unit": "TB/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": tbs, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-# ---------------------------------------------------------------------------
-# our arm
-# ---------------------------------------------------------------------------
-def cpu_baseline(O, layer_mats, ncols, budget_s: float = 12.0) -> dict:
-    """The oracle (all host threads) on layer 0's matrices, repeated for ~budget_s."""
+def cpu_baseline(O, mats, group, ncols, budget_s: float = 12.0) -> dict:
+    """The oracle (all host threads) on the first launch group, repeated for ~budget_s."""
     rng = np.random.default_rng(1)
-    xs = {g: rng.standard_normal((ncols, K)).astype(np.float32) for g, K in ACT_K.items()}
+    xs = {a: rng.standard_normal((ncols, K)).astype(np.float32) for _, _, K, a in group}
     threads = O.max_threads()
-    bytes_one = step_bytes(ncols)["per_layer_launch"]
     n, t0 = 0, time.perf_counter()
     while True:
-        for W, K, grp in layer_mats:
-            O.gemv_f32(W, xs[grp], nthreads=threads)
+        for W, K, a in mats:
+            O.gemv_f32(W, xs[a], nthreads=threads)
         n += 1
         el = time.perf_counter() - t0
         if el > budget_s:
             break
-    return {"value": bytes_one * n / el / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} x one Mistral-7B decoder layer's 7 Q4_K GEMVs (fp32 x, q8_1 quantization "
+    return {"value": group_bytes(group, ncols) * n / el / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} x the first launch group ({len(group)} Q4_K GEMVs, fp32 x, q8_1 quantization "
                       f"included) = {el:.1f} s on the host"}
 
 
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--ncols", type=int, default=1)
+    ap.add_argument("--config", default="2", choices=sorted(WORKLOADS), help="BASELINE config (default 2)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers to build (profiling: fewer)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="repeats of the workload's launch group (default: the workload's; profiling: fewer)")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
-                    help="N > 1: fused peer-store all-gather in the GEMV (default) or NCCL all_gather per layer")
+                    help="N > 1: fused peer-store all-gather in the GEMV (default) or NCCL all_gather per launch")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -256,62 +278,50 @@ def main():
     q4k = load_package()
     q4k.lib()
     ncols = args.ncols
+    reps = args.layers if args.layers is not None else WORKLOADS[args.config][2]
+    wname, groups = build_groups(args.config, reps)
+    full_run = args.layers is None or args.layers == WORKLOADS[args.config][2]
 
-    # ---- weights (sharded rows), activations, outputs -------------------------
+    # ---- weights (row shards), activations, outputs -------------------------
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
-    nlayers = args.layers
     peer = world > 1 and args.gather == "peer"
-    layer_elems = sum(r * ncols for _, r, _, _ in MATS)
-    pg = q4k.PeerGather(nlayers * layer_elems + HEAD[0] * ncols) if peer else None
-    layers = []
-    for li in range(nlayers):
-        xs = {grp: torch.randn((ncols, K), device=dev, generator=g) for grp, K in ACT_K.items()}
+    full_elems = sum(r * ncols for grp in groups for _, r, _, _ in grp)
+    pg = q4k.PeerGather(full_elems) if peer else None
+    L = []
+    base = 0
+    for grp in groups:
+        xs = {a: torch.randn((ncols, K), device=dev, generator=g) for _, _, K, a in grp}
         ents = []
-        for name, rows, K, grp in MATS:
-            lo, hi, per = shard(rows, rank, world)
+        for name, rows, K, a in grp:
+            lo, hi, per = q4k.shard_rows(rows, rank, world)
             W = q4k.gen_q4k_torch(hi - lo, K, generator=g, device=dev)
-            ents.append((name, W, xs[grp], rows, per, hi - lo, lo))
+            ents.append(dict(name=name, W=W, x=xs[a], rows=rows, K=K, lo=lo, n=hi - lo, per=per))
         if peer:
-            # this layer's full outputs live in the shared buffer; the shard
-            # writes its rows there and the kernel stores them into every peer
-            base, outs = li * layer_elems, []
+            # full outputs live in the shared buffer; each rank writes its rows
+            # there and the kernel stores them into every peer's buffer too
+            outs, ybuf0 = [], base
             for e in ents:
-                full = pg.out[base: base + e[3] * ncols].view(ncols, e[3])
-                outs.append(full[:, e[6]: e[6] + e[5]])
-                base += e[3] * ncols
-            ybuf, gath = pg.out[li * layer_elems: (li + 1) * layer_elems], None
+                full = pg.out[base: base + e["rows"] * ncols].view(ncols, e["rows"])
+                outs.append(full[:, e["lo"]: e["lo"] + e["n"]])
+                e["stride"] = e["rows"]
+                base += e["rows"] * ncols
+            ybuf, gath = pg.out[ybuf0: base], None
         else:
-            # local outputs packed so one all-gather covers the layer
-            per_tot = sum(e[4] for e in ents)
+            per_tot = sum(e["per"] for e in ents)
             ybuf = torch.zeros((per_tot * ncols,), device=dev)
             outs, off = [], 0
             for e in ents:
-                outs.append(ybuf[off: off + e[4] * ncols].view(ncols, e[4])[:, : e[5]])
-                off += e[4] * ncols
+                outs.append(ybuf[off: off + e["per"] * ncols].view(ncols, e["per"])[:, : e["n"]])
+                e["stride"] = e["per"]
+                off += e["per"] * ncols
             gath = torch.empty((per_tot * ncols * world,), device=dev) if world > 1 else None
-        tasks = q4k.make_tasks([e[1] for e in ents], [e[2] for e in ents], outs)
+        tasks = q4k.make_tasks([e["W"] for e in ents], [e["x"] for e in ents], outs)
         for i, e in enumerate(ents):
-            tasks[i].stride_col_dst = e[3] if peer else e[4]
-        layers.append(dict(xs=xs, ents=ents, ybuf=ybuf, outs=outs, tasks=tasks, gath=gath))
-    hlo, hhi, hper = shard(HEAD[0], rank, world)
-    head_W = q4k.gen_q4k_torch(hhi - hlo, HEAD[1], generator=g, device=dev)
-    head_x = torch.randn((ncols, HEAD[1]), device=dev, generator=g)
-    if peer:
-        hbase = nlayers * layer_elems
-        head_y = pg.out[hbase: hbase + HEAD[0] * ncols]
-        head_out = head_y.view(ncols, HEAD[0])[:, hlo:hhi]
-        head_gath = None
-    else:
-        head_y = torch.zeros((hper * ncols,), device=dev)
-        head_out = head_y.view(ncols, hper)[:, : hhi - hlo]
-        head_gath = torch.empty((hper * ncols * world,), device=dev) if world > 1 else None
-    head_tasks = q4k.make_tasks([head_W], [head_x], [head_out])
-    head_tasks[0].stride_col_dst = HEAD[0] if peer else hper
+            tasks[i].stride_col_dst = e["stride"]
+        L.append(dict(xs=xs, ents=ents, ybuf=ybuf, tasks=tasks, gath=gath))
 
-    ws_bytes = max([q4k.batch_workspace_bytes(L["tasks"], ncols) for L in layers] +
-                   [q4k.batch_workspace_bytes(head_tasks, ncols)])
-    ws = q4k.Workspace(ws_bytes, dev)
+    ws = q4k.Workspace(max(q4k.batch_workspace_bytes(G["tasks"], ncols) for G in L), dev)
     stream = torch.cuda.Stream(device=dev)
 
     def gemv(tasks):
@@ -321,17 +331,14 @@ def main():
             q4k.gemv_batch(tasks, ncols, ws, stream=stream)
 
     def run_step(ev=None):
-        for li, L in enumerate(layers):
+        for gi, G in enumerate(L):
             if ev is not None:
-                ev[li][0].record(stream)
-            gemv(L["tasks"])
+                ev[gi][0].record(stream)
+            gemv(G["tasks"])
             if ev is not None:
-                ev[li][1].record(stream)
+                ev[gi][1].record(stream)
             if world > 1 and not peer:
-                dist.all_gather_into_tensor(L["gath"], L["ybuf"])
-        gemv(head_tasks)
-        if world > 1 and not peer:
-            dist.all_gather_into_tensor(head_gath, head_y)
+                dist.all_gather_into_tensor(G["gath"], G["ybuf"])
 
     # ---- one untimed step: checks the device status word before timing ------
     with torch.cuda.stream(stream):
@@ -349,7 +356,7 @@ def main():
                 step_graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(step_graph, stream=stream):
                     run_step()
-        except Exception as e:  # capture unsupported (e.g. collectives): time eagerly
+        except Exception as e:  # capture unsupported: time eagerly
             print(f"# graph capture failed ({e!r}); timing eager launches", file=sys.stderr)
             use_graph, step_graph = False, None
 
@@ -369,15 +376,22 @@ def main():
 
     # Clock samples (every 200 ms) need load around the short timed region:
     # the sampler runs from an untimed soak of step replays (~0.8 s) through
-    # the warm-up and the timed steps.
+    # the warm-up and the timed steps.  Every rank replays the same number of
+    # soak steps (rank 0's count).
     if sampler:
         sampler.start()
-    t_soak = time.perf_counter()
-    while time.perf_counter() - t_soak < 0.8:
-        for _ in range(20):
+    nsoak, t_soak = 0, time.perf_counter()
+    while time.perf_counter() - t_soak < 0.8 and nsoak < 4000:
+        for _ in range(10):
             replay()
+        nsoak += 10
         torch.cuda.synchronize(dev)
     if world > 1:
+        t = torch.tensor([nsoak], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        for _ in range(int(t[0]) - nsoak):
+            replay()
+        torch.cuda.synchronize(dev)
         dist.barrier()
     for _ in range(args.warmup):
         replay()
@@ -398,36 +412,39 @@ def main():
     clocks = sampler.stop() if sampler else None
     ms = t_start.elapsed_time(t_end) / args.steps
 
-    # ---- isolated layer launches (events between layers serialize them) ------
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nlayers)]
+    # ---- isolated launches (events between launches serialize them) ---------
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in L]
     with torch.cuda.stream(stream):
         run_step(ev)
     torch.cuda.synchronize(dev)
-    iso_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+    nrep = len(groups) - len(WORKLOADS[args.config][3])  # the repeated group only
+    iso_ms = float(np.mean([a.elapsed_time(b) for a, b in ev[: max(1, nrep)]]))
     if world > 1:
         t = torch.tensor([ms, iso_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, iso_ms = float(t[0]), float(t[1])
 
-    sb = step_bytes(ncols, world, nlayers)
-    value = sb["total"] / (ms * 1e-3) / 1e12
+    step_total = sum(group_bytes(G, ncols, world) for G in groups)
+    value = step_total / (ms * 1e-3) / 1e12
     peak, peak_kind = measured_peaks()
-    nlaunch = nlayers + 1  # GEMV launches per step (each with its overlapped prep launch)
-    # Every launch of the timed step is k_gemv: its average duration in the
-    # chained step is step time / launches, its bytes the step's / launches.
-    per_rank_bytes = sb["total"] / world
+    nlaunch = len(groups)
     launch_us = ms * 1e3 / nlaunch
-    achieved = per_rank_bytes / (ms * 1e-3) / 1e9
-    per_launch_bytes = sb["per_layer_launch"] if world == 1 else None
-    if world > 1:  # this rank's share of one layer
-        per_launch_bytes = sum(e[5] * e[2].shape[1] * 9 // 16 + ncols * e[5] * 4 for e in layers[0]["ents"]) + \
-            sum(ncols * K * 4 for K in ACT_K.values())
+    # Every launch of the timed step is k_gemv (with its programmatic-dependent
+    # prep): its average duration in the chained step is step time / launches;
+    # achieved bandwidth per rank = the rank's step bytes / step time.
+    achieved = step_total / world / (ms * 1e-3) / 1e9
+    g0 = groups[0]
+    if world == 1:
+        launch_bytes = group_bytes(g0, ncols)
+    else:  # this rank's share of the first launch group
+        launch_bytes = (sum(e["n"] * e["K"] * 9 // 16 + ncols * e["n"] * 4 for e in L[0]["ents"]) +
+                        sum(ncols * x.shape[1] * 4 for x in L[0]["xs"].values()))
 
     # ---- e2e: public C-ABI calls with host buffers ------------------------------
     e2e = None
     if not args.no_e2e:
-        xs_all = [L["xs"][grp] for L in layers for grp in ACT_K] + [head_x]
-        ys_all = [pg.out] if peer else [L["ybuf"] for L in layers] + [head_y]
+        xs_all = [x for G in L for x in G["xs"].values()]
+        ys_all = [pg.out] if peer else [G["ybuf"] for G in L]
         h_x = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in xs_all]
         for h, d in zip(h_x, xs_all):
             h.copy_(d)
@@ -460,52 +477,51 @@ def main():
             t = torch.tensor([e_ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e_ms = float(t[0])
-        e2e = {"value": sb["total"] / (e_ms * 1e-3) / 1e12, "unit": "TB/s", "h2d_bytes_per_step": h2d,
+        e2e = {"value": step_total / (e_ms * 1e-3) / 1e12, "unit": "TB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms,
-               "path": "q4k_gemv_batch C-ABI calls (ctypes) per layer, pinned host x -> device, "
+               "path": "q4k_gemv_batch C-ABI calls (ctypes), one per launch group, pinned host x -> device, "
                        "outputs -> pinned host, every step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         O = load_oracle()
-        layer_mats = [(e[1].cpu().numpy(), e[2].shape[1], grp) for e, (_, _, _, grp) in
-                      zip(layers[0]["ents"], MATS)]
-        cpu = cpu_baseline(O, layer_mats, ncols)
+        mats = [(e["W"].cpu().numpy(), e["K"], a) for e, (_, _, _, a) in zip(L[0]["ents"], g0)]
+        cpu = cpu_baseline(O, mats, g0, ncols)
 
     traffic = None
     tf = PROFILES / "gemv_layer_traffic.json"
-    if tf.exists() and world == 1:
+    if tf.exists() and world == 1 and args.config == "2":
         d = json.loads(tf.read_text())
         if d.get("ncols") == ncols:
             traffic = d.get("dram_bytes_per_launch")
 
     if rank == 0:
+        shapes = sorted({f"{r}x{K}" for grp in groups for _, r, K, _ in grp})
         line = {
             "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD if nlayers == LAYERS else f"{WORKLOAD} (profiling subset)",
-                       "layers": nlayers, "matrices_per_layer": len(MATS),
-                       "head": f"{HEAD[0]}x{HEAD[1]}", "ncols": ncols,
-                       "launches": "per layer: prep (q8_1 quantization) + persistent GEMV over 7 matrices (PDL)",
-                       "timing": "one CUDA graph per step (launches chained with programmatic dependencies), "
-                                 "CUDA events on the launch stream around all timed steps",
-                       "l2": "inputs larger than L2 (4.0 GB of weights per step, no flush needed)",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded, generated on the device)",
+            "config": {"workload": wname if full_run else f"{wname} (profiling subset)",
+                       "baseline_config": args.config, "launch_groups": nlaunch, "shapes": shapes,
+                       "ncols": ncols,
+                       "launches": "per group: prep (q8_1 quantization) + persistent GEMV over the group's "
+                                   "matrices, chained with programmatic dependencies",
+                       "timing": "one CUDA graph per step, CUDA events on the launch stream around all timed steps",
+                       "l2": "inputs larger than L2 (weights per step >= 3x the 126 MB L2), no flush needed",
                        "parallelism": "single GPU" if world == 1 else (
                            f"row-shard x{world}, outputs all-gathered inside the GEMV over NVLink peer stores"
-                           if peer else f"row-shard x{world} + NCCL all-gather per layer")},
+                           if peer else f"row-shard x{world} + NCCL all-gather per launch")},
             "us_per_call": launch_us,
-            "us_per_layer_launch_isolated": iso_ms * 1e3,
+            "us_per_launch_isolated": iso_ms * 1e3,
             "pct_hbm_peak": 100.0 * value * 1e3 / world / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
-                         "kernel": "k_gemv: every launch of the step (32 layer launches of 7 matrices + the head), "
-                                   "each with its PDL-overlapped prep launch; achieved = step bytes per rank / "
-                                   "step time",
-                         "algorithmic_bytes_per_layer_launch": per_launch_bytes,
-                         "layer_launch_isolated_gbs": (per_launch_bytes / (iso_ms * 1e-3) / 1e9)},
+                         "kernel": "k_gemv: every launch of the step, each with its programmatic-dependent prep "
+                                   "launch; achieved = step bytes per rank / step time",
+                         "algorithmic_bytes_per_launch": launch_bytes,
+                         "launch_isolated_gbs": launch_bytes / (iso_ms * 1e-3) / 1e9},
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
-            "gpu_launches": args.steps * (nlayers + 1) * 2,
+            "gpu_launches": args.steps * nlaunch * 2,
             "graph": use_graph,
         }
         print(json.dumps(line), flush=True)
