@@ -110,6 +110,8 @@ def lib() -> ctypes.CDLL:
         L.q4k_workspace_status.argtypes = [_P, ctypes.POINTER(_I), _P]
         L.q4k_mul_mat_vec_noalloc.argtypes = [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P]
         L.q4k_gemv_batch_allgather.argtypes = [ctypes.POINTER(Task), _I, _I, ctypes.POINTER(Gather), _P, _SZ, _P]
+        L.q4k_workspace_init.argtypes = [_P, _SZ, _P]
+        L.q4k_gemv_batch_persistent.argtypes = [ctypes.POINTER(Task), _I, _I, ctypes.POINTER(Gather), _P, _SZ, _P]
         L.q4k_ipc_alloc.argtypes = [_SZ, ctypes.POINTER(ctypes.c_void_p)]
         L.q4k_ipc_free.argtypes = [_P]
         L.q4k_ipc_handle.argtypes = [_P, ctypes.c_char_p]
@@ -162,11 +164,19 @@ class Workspace:
         import torch
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=self.device)
+        self.zeroed = False  # control words zero (q4k_workspace_init ran on this buffer)
 
     def ensure(self, nbytes: int) -> "Workspace":
         import torch
         if nbytes > self.buf.numel():
             self.buf = torch.empty(int(nbytes), dtype=torch.uint8, device=self.device)
+            self.zeroed = False
+        return self
+
+    def init(self, stream=None) -> "Workspace":
+        """Zero the whole buffer (q4k_workspace_init), as the single-launch path needs."""
+        _check(lib().q4k_workspace_init(self.ptr, self.nbytes, _stream(stream)))
+        self.zeroed = True
         return self
 
     @property
@@ -320,6 +330,19 @@ def gemv_batch(tasks, ncols: int, ws: Workspace, stream=None) -> None:
     """Every task's GEMV in one prep + one persistent GEMV launch."""
     ws.ensure(batch_workspace_bytes(tasks, ncols))
     _check(lib().q4k_gemv_batch(tasks, len(tasks), ncols, ws.ptr, ws.nbytes, _stream(stream)))
+
+
+def gemv_batch_persistent(tasks, ncols: int, ws: Workspace, stream=None, gather=None) -> None:
+    """q4k_gemv_batch in a single launch (quantization inside the GEMV grid).
+
+    ws is zeroed on first use (and whenever it grows); afterwards every
+    completed call leaves its control words zero.  gather: a PeerGather for
+    the fused all-gather, or None."""
+    ws.ensure(batch_workspace_bytes(tasks, ncols))
+    if not ws.zeroed:
+        ws.init(stream)
+    g = ctypes.byref(gather.desc) if gather is not None else None
+    _check(lib().q4k_gemv_batch_persistent(tasks, len(tasks), ncols, g, ws.ptr, ws.nbytes, _stream(stream)))
 
 
 def debug_subblock_sums(W, yq, K: int, ws: Workspace | None = None, stream=None):

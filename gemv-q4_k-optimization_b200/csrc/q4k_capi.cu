@@ -200,7 +200,13 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         T.apr = static_cast<int32_t>(apr);
         T.rg_base = static_cast<int32_t>(rgs);
         T.ngroups = static_cast<int32_t>(groups);
-        T.pad_ = 0;
+        // The first task of each distinct activation quantizes it on the
+        // single-launch path.
+        T.act_owner = 1;
+        for (int k = 0; k < i; ++k)
+            if (P.act_of_job[k] == P.act_of_job[i]) T.act_owner = 0;
+        T.x = j.kind == kPrepF32 ? static_cast<const float *>(j.src) : nullptr;
+        T.x_col_stride = j.src_col_stride;
         atoms += groups * apr;
         rgs += groups;
     }
@@ -213,6 +219,8 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.gemv.nworkers = static_cast<int32_t>(atoms < max_workers ? atoms : max_workers);
     P.gemv.packed = atoms >= 4 * max_workers ? 1 : 0;
     P.gemv.pad0_ = 0;
+    P.gemv.fused = 0;
+    P.gemv.ncols = ncols;
     if (ws == nullptr) return Q4K_OK;
 
     // pointers into the workspace
@@ -277,8 +285,12 @@ int validate_gather(const q4k_gather *g) {
     return Q4K_OK;
 }
 
+// fused: one launch that quantizes the activations itself (fp32 jobs only;
+// the workspace header and counters must be zero on entry, which every
+// completed call leaves them).
 int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes, cudaStream_t s,
-        int32_t *dump_S = nullptr, int32_t *dump_T = nullptr, const q4k_gather *gather = nullptr) {
+        int32_t *dump_S = nullptr, int32_t *dump_T = nullptr, const q4k_gather *gather = nullptr,
+        bool fused = false) {
     Plan P;
     // Arguments are validated before the device is touched.
     int st = make_plan(jobs, njobs, ncols, nullptr, kFallbackSMs, P);
@@ -313,7 +325,14 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
         P.gemv.gepoch = gather->epoch;
         P.gemv.gdone = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace) + 4);
     }
-    if ((e = launch_prep(P.prep, s)) != cudaSuccess) return cuda_fail(e, "prep launch");
+    if (fused) {
+        uint8_t *w8 = static_cast<uint8_t *>(workspace);
+        P.gemv.fused = 1;
+        // its own line, apart from the status word
+        P.gemv.bar_arrive = reinterpret_cast<unsigned long long *>(w8 + 128);
+    } else if ((e = launch_prep(P.prep, s)) != cudaSuccess) {
+        return cuda_fail(e, "prep launch");
+    }
     if ((e = launch_gemv(P.gemv, ncols, dump_S != nullptr, num_sms, s)) != cudaSuccess)
         return cuda_fail(e, "gemv launch");
     return Q4K_OK;
@@ -485,6 +504,32 @@ int q4k_gemv_batch_allgather(const q4k_task *tasks, int ntasks, int ncols, const
     }
     return run(jobs, ntasks, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr,
                nullptr, gather);
+}
+
+int q4k_workspace_init(void *workspace, size_t workspace_bytes, q4k_stream_t stream) {
+    if (workspace == nullptr || workspace_bytes == 0) return fail(Q4K_EWORKSPACE, "workspace is null or empty");
+    if (!aligned16(workspace)) return fail(Q4K_EWORKSPACE, "workspace is not 16-byte aligned");
+    cudaError_t e = cudaMemsetAsync(workspace, 0, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+    return Q4K_OK;
+}
+
+int q4k_gemv_batch_persistent(const q4k_task *tasks, int ntasks, int ncols, const q4k_gather *gather,
+                              void *workspace, size_t workspace_bytes, q4k_stream_t stream) {
+    if (!tasks || ntasks < 1 || ntasks > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..16", ntasks);
+    if (gather) {
+        int st = validate_gather(gather);
+        if (st != Q4K_OK) return st;
+    }
+    Job jobs[kMaxTasks];
+    for (int i = 0; i < ntasks; ++i) {
+        jobs[i] = {tasks[i].W, tasks[i].x, tasks[i].dst, tasks[i].nrows, tasks[i].K,
+                   tasks[i].stride_row_x, tasks[i].stride_col_x, tasks[i].stride_col_dst, kPrepF32};
+        if (gather && gather->world > 1 && tasks[i].nrows > 0 && tasks[i].K == 0)
+            return fail(Q4K_EINVAL, "task %d: K = 0 is not supported with a fused all-gather", i);
+    }
+    return run(jobs, ntasks, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr,
+               nullptr, gather, /*fused=*/true);
 }
 
 int q4k_ipc_alloc(size_t bytes, void **ptr) {

@@ -75,7 +75,10 @@ struct TaskDesc {
     int32_t apr;             // atoms per row group = ceil(nb / kKS)
     int32_t rg_base;         // global row-group index of row group 0
     int32_t ngroups;         // row groups = ceil(nrows / 32)
-    int32_t pad_;
+    int32_t act_owner;       // single-launch path: 1 if this task quantizes its activation
+    // single-launch path: the fp32 activation this task's q8a records come from
+    const float *x;
+    int64_t x_col_stride;    // floats between activation columns
 };
 
 struct GemvParams {
@@ -101,6 +104,11 @@ struct GemvParams {
     uint32_t *gflags_peer[kMaxPeers];// every rank's flag words (one per sender), mapped here
     uint32_t *gepoch;                // this rank's epoch word (persists across calls)
     uint32_t *gdone;                 // CTAs finished (workspace; zero at kernel start)
+    // Single-launch path (fused quantization + grid barrier): sync words in an
+    // initialised workspace that every launch leaves as it found them.
+    int32_t fused;
+    int32_t ncols;
+    unsigned long long *bar_arrive;  // grid-barrier arrivals, counts up by gridDim.x per launch
 };
 
 enum PrepKind : int32_t { kPrepF32 = 0, kPrepQ81 = 1 };

@@ -28,6 +28,33 @@
 namespace q4k {
 
 // ============================================================================
+// q8_1 quantization of one 32-value block (one warp, lane = value)
+// ============================================================================
+// d = amax/127 (IEEE division), q = amax == 0 ? 0 : roundf(x/d): the semantics
+// of the quantizer the reference calls at kernels/mmvq.cu:734.
+__device__ __forceinline__ void quantize_value(float x, int &q, __half &dh) {
+    const float amax = warp_max_f32(fabsf(x));
+    const float d = amax / 127.0f;  // IEEE division (no fast-math in this build)
+    q = amax == 0.0f ? 0 : static_cast<int>(roundf(x / d));
+    dh = __float2half_rn(d);
+}
+
+// Write block b's quants and metadata into its q8a record (column base act_col).
+__device__ __forceinline__ void write_q8a(uint8_t *act_col, int b, int lane, int q, __half dh, int32_t *dump_T) {
+    const int T = warp_sum_i32(q);
+    uint8_t *rec = act_col + static_cast<int64_t>(b >> 3) * kActSBBytes;
+    const int s = b & 7;
+    rec[s * 32 + lane] = static_cast<uint8_t>(static_cast<int8_t>(q));
+    if (lane == 0) {
+        const float d8 = __half2float(dh);
+        float *meta = reinterpret_cast<float *>(rec + kActMetaOff + 16 * (s >> 1));
+        meta[s & 1] = (s & 1) ? d8 * 0.0625f : d8;
+        meta[2 + (s & 1)] = d8 * static_cast<float>(T);
+        if (dump_T != nullptr) *dump_T = T;
+    }
+}
+
+// ============================================================================
 // prep: quantize / repack activations, clear counters
 // ============================================================================
 __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams P) {
@@ -58,10 +85,7 @@ __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams
         if (J.kind == kPrepF32) {
             const float *xc = static_cast<const float *>(J.src) + col * J.src_col_stride;
             const float x = pos < J.K ? xc[pos] : 0.0f;
-            const float amax = warp_max_f32(fabsf(x));
-            const float d = amax / 127.0f;  // IEEE division (no fast-math in this build)
-            q = amax == 0.0f ? 0 : static_cast<int>(roundf(x / d));
-            dh = __float2half_rn(d);
+            quantize_value(x, q, dh);
             if (J.q81_out != nullptr) {
                 const float sum = warp_sum_f32(x);
                 uint8_t *blk = J.q81_out + (col * J.q81_col_stride + b) * kQ81Bytes;
@@ -78,17 +102,8 @@ __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams
         }
 
         if (J.act != nullptr && b * 32 < J.K) {
-            const int T = warp_sum_i32(q);
-            uint8_t *rec = J.act + col * J.act_col_stride + static_cast<int64_t>(b >> 3) * kActSBBytes;
-            const int s = b & 7;
-            rec[s * 32 + lane] = static_cast<uint8_t>(static_cast<int8_t>(q));
-            if (lane == 0) {
-                const float d8 = __half2float(dh);
-                float *meta = reinterpret_cast<float *>(rec + kActMetaOff + 16 * (s >> 1));
-                meta[s & 1] = (s & 1) ? d8 * 0.0625f : d8;
-                meta[2 + (s & 1)] = d8 * static_cast<float>(T);
-                if (J.dump_T != nullptr) J.dump_T[static_cast<int64_t>(col) * (J.K / 32) + b] = T;
-            }
+            int32_t *dT = J.dump_T != nullptr ? J.dump_T + static_cast<int64_t>(col) * (J.K / 32) + b : nullptr;
+            write_q8a(J.act + col * J.act_col_stride, b, lane, q, dh, dT);
         }
     }
 }
@@ -372,39 +387,51 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
     }
 }
 
-// One worker's whole range: stream its atoms through the warp's ring and
-// flush its row groups.  Returns (never exits the kernel) so that a fused
-// all-gather can still run its CTA-wide epilogue.
-template <int NC, bool DUMP>
-__device__ __forceinline__ void run_worker(const GemvParams &P, int64_t worker, int lane, uint32_t ring,
-                                           const uint32_t (&bar)[kStages], int64_t cta_w0, int64_t cta_w1,
-                                           int *cta_cnt) {
-    constexpr int kSB = Stage<NC>::kBytes;
-    const int64_t a0 = worker_begin(P, worker);
-    const int64_t a1 = worker_begin(P, worker + 1);
-    const int n = static_cast<int>(a1 - a0);
+// Per-warp pipeline state of one worker.
+struct WorkerPipe {
+    int64_t a0, a1;
+    int n;
+    uint32_t ring;
+    AtomCursor icur;            // next atom to issue
+    AtomCursor pro[kStages];    // the prologue atoms
+};
 
-    // Weight bytes do not depend on the prep kernel: start streaming now,
-    // activations once the prep grid has completed.
-    AtomCursor icur = locate_atom(P, a0);
-    AtomCursor pro[kStages];
+// Issue the weight copies of the first kStages atoms (they do not depend on
+// any earlier grid: the weights are read-only).
+template <int NC>
+__device__ __forceinline__ void worker_prologue(const GemvParams &P, WorkerPipe &W, int lane,
+                                                const uint32_t (&bar)[kStages]) {
+    constexpr int kSB = Stage<NC>::kBytes;
+    W.icur = locate_atom(P, W.a0);
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
-        pro[s] = icur;
-        if (s < n) {
-            issue_weights<NC>(P, icur, ring + s * kSB, bar[s], lane);
-            advance(P, icur);
+        W.pro[s] = W.icur;
+        if (s < W.n) {
+            issue_weights<NC>(P, W.icur, W.ring + s * kSB, bar[s], lane);
+            advance(P, W.icur);
         }
     }
-    pdl_wait();
+}
+
+// The rest of one worker's range, once the activations are ready: stream its
+// atoms through the warp's ring and flush its row groups.  Returns (never
+// exits the kernel) so that the CTA-wide epilogues can still run.
+template <int NC, bool DUMP>
+__device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, int64_t worker, int lane,
+                                            const uint32_t (&bar)[kStages], int64_t cta_w0, int64_t cta_w1,
+                                            int *cta_cnt) {
+    constexpr int kSB = Stage<NC>::kBytes;
+    const int n = W.n;
+    const uint32_t ring = W.ring;
+    AtomCursor icur = W.icur;
 #pragma unroll
     for (int s = 0; s < kStages; ++s)
-        if (s < n) issue_acts<NC>(P, pro[s], ring + s * kSB, bar[s], lane);
+        if (s < n) issue_acts<NC>(P, W.pro[s], ring + s * kSB, bar[s], lane);
 
     uint64_t acc[NC];
 #pragma unroll
     for (int j = 0; j < NC; ++j) acc[j] = 0ull;
-    AtomCursor cur = pro[0];
+    AtomCursor cur = W.pro[0];
     int open_t = -1, open_g = -1;
 
     for (int i = 0; i < n; ++i) {
@@ -413,7 +440,7 @@ __device__ __forceinline__ void run_worker(const GemvParams &P, int64_t worker, 
         if (cur.t != open_t || cur.g != open_g) {
             if (open_t >= 0) {
                 AtomCursor o{open_t, open_g, 0};
-                flush_group<NC, DUMP>(P, o, acc, worker, a0, a1, lane, cta_w0, cta_w1, cta_cnt);
+                flush_group<NC, DUMP>(P, o, acc, worker, W.a0, W.a1, lane, cta_w0, cta_w1, cta_cnt);
             }
             open_t = cur.t;
             open_g = cur.g;
@@ -441,8 +468,68 @@ __device__ __forceinline__ void run_worker(const GemvParams &P, int64_t worker, 
     }
     if (open_t >= 0) {
         AtomCursor o{open_t, open_g, 0};
-        flush_group<NC, DUMP>(P, o, acc, worker, a0, a1, lane, cta_w0, cta_w1, cta_cnt);
+        flush_group<NC, DUMP>(P, o, acc, worker, W.a0, W.a1, lane, cta_w0, cta_w1, cta_cnt);
     }
+}
+
+// Single-launch path, before the main loop: every warp of the grid quantizes
+// a share of the activation blocks of the tasks that own an activation (the
+// same arithmetic as k_prep); a grid barrier then makes the q8a records of
+// all CTAs visible before any activation copy is issued.
+__device__ __forceinline__ void fused_quantize(const GemvParams &P) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    const int64_t wid = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int64_t base = 0;
+    for (int t = 0; t < P.ntasks; ++t) {
+        const TaskDesc &T = P.task[t];
+        if (!T.act_owner) continue;
+        const int nblk = T.nb * 8;
+        const int64_t items = static_cast<int64_t>(P.ncols) * nblk;
+        // warp wid takes items wid - base, wid - base + nw, ... of this task
+        int64_t first = wid - base;
+        if (first < 0) first += ((-first + nw - 1) / nw) * nw;
+        for (int64_t it = first; it < items; it += nw) {
+            const int col = static_cast<int>(it / nblk);
+            const int b = static_cast<int>(it - static_cast<int64_t>(col) * nblk);
+            int q;
+            __half dh;
+            quantize_value(T.x[col * T.x_col_stride + b * 32 + lane], q, dh);
+            write_q8a(const_cast<uint8_t *>(T.act) + col * T.act_col_stride, b, lane, q, dh, nullptr);
+        }
+        base += items;
+    }
+}
+
+// Grid-wide barrier over all CTAs of this launch (one CTA per SM, all
+// resident).  The arrival counter only counts up, by gridDim.x per launch, so
+// it needs no reset: a CTA reads it after griddepcontrol.wait (the previous
+// launch's arrivals are complete, this launch's are fewer than gridDim.x),
+// which fixes this launch's target, the next multiple of gridDim.x.  The
+// arrival is a release reduction by one thread after bar.sync (publishing the
+// CTA's stores) and the waiters acquire the counter; the wait is bounded.
+__device__ __forceinline__ unsigned long long barrier_target(const GemvParams &P) {
+    const unsigned long long v0 = ld_relaxed_gpu_u64(P.bar_arrive);
+    return v0 - v0 % gridDim.x + gridDim.x;
+}
+
+__device__ __forceinline__ void grid_barrier_arrive(const GemvParams &P) {
+    __syncthreads();
+    if (threadIdx.x == 0) red_add_release_gpu_u64(P.bar_arrive, 1ull);
+}
+
+__device__ __forceinline__ void grid_barrier_wait(const GemvParams &P, unsigned long long target) {
+    if (threadIdx.x == 0) {
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t it = 0;; ++it) {
+            if (ld_acquire_gpu_u64(P.bar_arrive) >= target) break;
+            if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+                atomicExch(P.status, kStatusTimeout);
+                break;
+            }
+        }
+    }
+    __syncthreads();
 }
 
 // Fused all-gather epilogue: after every CTA of this grid has stored its
@@ -454,6 +541,7 @@ __device__ __forceinline__ void run_worker(const GemvParams &P, int64_t worker, 
 // Ordering: each CTA's peer stores -> block barrier -> release fence (system
 // scope) -> arrival count; the last CTA's acquire fence -> per-peer release
 // stores of the flag (one lane per peer, in parallel) -> peers' acquire loads.
+// The last CTA also returns the arrival count to 0 for the next launch.
 __device__ __forceinline__ void gather_epilogue(const GemvParams &P) {
     __shared__ int last_cta;
     __syncthreads();
@@ -480,7 +568,10 @@ __device__ __forceinline__ void gather_epilogue(const GemvParams &P) {
             break;
         }
     }
-    if (lane == 0) *reinterpret_cast<volatile uint32_t *>(P.gepoch) = e;
+    if (lane == 0) {
+        *reinterpret_cast<volatile uint32_t *>(P.gepoch) = e;
+        *reinterpret_cast<volatile uint32_t *>(P.gdone) = 0u;  // ready for the next launch
+    }
 }
 
 template <int NC, bool DUMP>
@@ -491,8 +582,8 @@ __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_con
     __shared__ __align__(8) uint64_t bars[kW][kStages];
     __shared__ int cta_cnt[kW];  // arrivals at row groups split between this CTA's warps
 
-    // The next prep launch may start now; it waits for this grid's completion
-    // before it touches the workspace.
+    // The next launch on the stream may start now; it waits for this grid's
+    // completion before it touches the workspace.
     pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -504,9 +595,14 @@ __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_con
                                     : static_cast<int64_t>(warp) * gridDim.x + blockIdx.x;
     const int64_t cta_w0 = static_cast<int64_t>(blockIdx.x) * kW;
     const int64_t cta_w1 = cta_w0 + kW - 1;
-    if (worker < P.nworkers) {
-        const uint32_t ring = smem_addr(smem) + static_cast<uint32_t>(warp * kStages * kSB);
-        uint32_t bar[kStages];
+    const bool active = worker < P.nworkers;
+    uint32_t bar[kStages];
+    WorkerPipe W;
+    if (active) {
+        W.a0 = worker_begin(P, worker);
+        W.a1 = worker_begin(P, worker + 1);
+        W.n = static_cast<int>(W.a1 - W.a0);
+        W.ring = smem_addr(smem) + static_cast<uint32_t>(warp * kStages * kSB);
 #pragma unroll
         for (int s = 0; s < kStages; ++s) bar[s] = smem_addr(&bars[warp][s]);
         if (lane == 0) {
@@ -515,12 +611,30 @@ __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_con
             mbar_fence_init();
         }
         __syncwarp();
-        run_worker<NC, DUMP>(P, worker, lane, ring, bar, cta_w0, cta_w1, cta_cnt);
     }
-    if (!DUMP && P.gworld > 1) {
-        pdl_wait();  // idle warps too: the epilogue touches the workspace
-        gather_epilogue(P);
+    // Weights stream while the previous grid on the stream (the prep launch,
+    // or the previous single-launch GEMV) finishes; griddepcontrol.wait
+    // returns once it has completed.
+    if (active) worker_prologue<NC>(P, W, lane, bar);
+    pdl_wait();
+    if (P.fused) {
+        // Single launch: quantize this CTA's share of the activations, then a
+        // grid barrier before any activation copy.  (Issuing the weights after
+        // the arrival instead measured slower: the copies no longer overlap
+        // the previous grid's tail.)
+        unsigned long long target = 0;
+        if (threadIdx.x == 0) {
+            target = barrier_target(P);
+            if (blockIdx.x == 0) *P.status = kStatusOk;
+        }
+        fused_quantize(P);
+        fence_proxy_async_global();  // this thread's q8a stores, before other CTAs' bulk copies
+        grid_barrier_arrive(P);
+        grid_barrier_wait(P, target);
+        fence_proxy_async_global();  // the q8a records are read by bulk copies next
     }
+    if (active) worker_main<NC, DUMP>(P, W, worker, lane, bar, cta_w0, cta_w1, cta_cnt);
+    if (!DUMP && P.gworld > 1) gather_epilogue(P);
 }
 
 // ============================================================================

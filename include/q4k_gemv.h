@@ -189,6 +189,29 @@ typedef struct q4k_gather {
 Q4K_API int q4k_gemv_batch_allgather(const q4k_task *tasks, int ntasks, int ncols, const q4k_gather *gather,
                                      void *workspace, size_t workspace_bytes, q4k_stream_t stream);
 
+/* ---- single-launch path (no reference counterpart) --------------------------- */
+
+/* The calls above issue two launches (activation quantization, then the
+ * GEMV) and accept a workspace with arbitrary contents, as ggml's pool hands
+ * it out.  A caller that keeps one workspace per stream can save the first
+ * launch: q4k_gemv_batch_persistent quantizes the activations inside the GEMV
+ * launch (all warps of the grid, then a grid-wide barrier) and needs the same
+ * workspace size (q4k_batch_workspace_bytes).  It requires the workspace's
+ * control words to be in a known state on entry: zero the workspace once with
+ * q4k_workspace_init before the first call; every call that completes leaves
+ * them valid again (the two-launch calls may use the same workspace in
+ * between).  After a call reports Q4K_ETIMEOUT (q4k_workspace_status) call
+ * q4k_workspace_init again.  gather may be NULL (no all-gather) or a
+ * descriptor as for q4k_gemv_batch_allgather.  Results are identical to
+ * q4k_gemv_batch.  All CTAs of the launch (one per SM) must be resident at
+ * once; a GPU shared with other work can delay that, in which case the
+ * barrier's bounded wait ends with Q4K_ETIMEOUT.  On B200, chained inside a
+ * CUDA graph, it measured slightly slower than the two-launch calls, whose
+ * quantization launch overlaps the previous GEMV's tail. */
+Q4K_API int q4k_workspace_init(void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+Q4K_API int q4k_gemv_batch_persistent(const q4k_task *tasks, int ntasks, int ncols, const q4k_gather *gather,
+                                      void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+
 /* Set-up helpers for the buffers above (not on the call path): device memory
  * that other processes can map (zero-filled), its 64-byte IPC handle, and
  * mapping / unmapping a peer's buffer from its handle. */

@@ -84,3 +84,19 @@ def test_op_mul_mat_vec_q_rejects_bad_rows(q4k):
     assert L.q4k_op_mul_mat_vec_q(256, 4096, 512, 1024, 10, 5, 1, 4096, 16, None, 0, None) == EINVAL
     assert L.q4k_op_mul_mat_vec_q(256, 4096, 512, 1024, 0, 32, 1, 4096, 16, None, 0, None) == EINVAL
     assert L.q4k_op_mul_mat_vec_q(256, 4096, 512, 1024, 0, 8, 1, 4000, 16, None, 0, None) == EINVAL
+
+
+def test_persistent_path_argument_checks(q4k):
+    L = q4k.lib()
+    tasks = (q4k.Task * 17)()
+    assert L.q4k_gemv_batch_persistent(tasks, 17, 1, None, None, 0, None) == EINVAL
+    assert L.q4k_gemv_batch_persistent(None, 1, 1, None, None, 0, None) == EINVAL
+    t = (q4k.Task * 1)()
+    t[0].W, t[0].x, t[0].dst, t[0].nrows, t[0].K, t[0].stride_row_x = 256, 512, 1024, 32, 300, 2
+    assert L.q4k_gemv_batch_persistent(t, 1, 1, None, None, 0, None) == EINVAL  # K % 256
+    g = q4k.Gather()
+    g.world = 9
+    t[0].K = 256
+    assert L.q4k_gemv_batch_persistent(t, 1, 1, ctypes.byref(g), None, 0, None) == EINVAL
+    assert L.q4k_workspace_init(None, 256, None) == EWORKSPACE
+    assert L.q4k_workspace_init(4097, 256, None) == EWORKSPACE  # not 16-byte aligned
