@@ -55,12 +55,11 @@ struct Layout {
     size_t counters_off = 0, partials_off = 0, act_off = 0, total = 0;
 };
 
-Layout make_layout(int64_t n_rowgroups, int ncols, size_t act_bytes, int num_sms) {
+Layout make_layout(int64_t n_rowgroups, int ncols, size_t act_bytes, int64_t partial_slots) {
     Layout L;
     L.counters_off = kAlign;
     L.partials_off = L.counters_off + round_up(static_cast<size_t>(n_rowgroups) * 4, kAlign);
-    const size_t workers = static_cast<size_t>(num_sms) * kMaxWarps;
-    L.act_off = L.partials_off + round_up(workers * 2 * ncols * 32 * sizeof(float), kAlign);
+    L.act_off = L.partials_off + round_up(static_cast<size_t>(partial_slots) * ncols * 32 * sizeof(float), kAlign);
     L.total = L.act_off + round_up(act_bytes, kAlign);
     return L;
 }
@@ -211,14 +210,15 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         rgs += groups;
     }
     P.n_rowgroups = rgs;
-    P.layout = make_layout(rgs, ncols, P.act_bytes, num_sms);
     P.any_work = atoms > 0;
     P.gemv.ntasks = nt;
     P.gemv.natoms = atoms;
-    const int64_t max_workers = static_cast<int64_t>(num_sms) * warps_for(ncols);
-    P.gemv.nworkers = static_cast<int32_t>(atoms < max_workers ? atoms : max_workers);
+    const int64_t max_workers = static_cast<int64_t>(num_sms) * rings_for(ncols);
+    const int64_t nw = atoms < max_workers ? atoms : max_workers;
+    P.gemv.nworkers = static_cast<int32_t>(nw);
     P.gemv.packed = atoms >= 4 * max_workers ? 1 : 0;
     P.gemv.pad0_ = 0;
+    P.layout = make_layout(rgs, ncols, P.act_bytes, 2 * nw);
     P.gemv.fused = 0;
     P.gemv.ncols = ncols;
     if (ws == nullptr) return Q4K_OK;

@@ -46,13 +46,25 @@ constexpr int kSmemLimit = 227 * 1024;
 
 // One ring stage: weights (32 rows) then the activation records of ncols columns.
 __host__ __device__ constexpr int stage_bytes(int ncols) { return kWStageBytes + ncols * kKS * 320; }
-// Warps per CTA for ncols columns: as many private rings as fit (one CTA per SM).
-__host__ __device__ constexpr int warps_for(int ncols) {
+// Warps that share one ring, each computing a share of the columns: from
+// Q4K_SPLIT_MIN columns on, two.  The split doubles the warps per SM without
+// more shared memory, but repeats the per-row work in both warps; on B200 it
+// measured no faster at 8 columns and slower at 3-5 (the dp4a/f32x2 pipe and
+// the shared-memory wavefronts, not latency, bound those), so the default
+// (9) leaves it off.
+#ifndef Q4K_SPLIT_MIN
+#define Q4K_SPLIT_MIN 9
+#endif
+__host__ __device__ constexpr int split_for(int ncols) { return ncols >= Q4K_SPLIT_MIN ? 2 : 1; }
+// Rings (= workers) per CTA for ncols columns: as many as fit (one CTA per SM).
+__host__ __device__ constexpr int rings_for(int ncols) {
     return kSmemLimit / (kStages * stage_bytes(ncols)) < kMaxWarps ? kSmemLimit / (kStages * stage_bytes(ncols))
                                                                    : kMaxWarps;
 }
-__host__ __device__ constexpr int smem_bytes(int ncols) { return warps_for(ncols) * kStages * stage_bytes(ncols); }
-static_assert(warps_for(8) >= 4, "ring too large for 8 columns");
+__host__ __device__ constexpr int warps_for(int ncols) { return rings_for(ncols) * split_for(ncols); }
+__host__ __device__ constexpr int smem_bytes(int ncols) { return rings_for(ncols) * kStages * stage_bytes(ncols); }
+static_assert(rings_for(8) >= 4, "ring too large for 8 columns");
+static_assert(warps_for(8) * 32 <= 1024, "block too large");
 
 // Device status codes (match q4k_status).
 constexpr int kStatusOk = 0;
@@ -85,9 +97,9 @@ struct GemvParams {
     CUtensorMap tmap[kMaxTasks];  // per task: uint32 view {nb*36, nrows}, box {36, 32}
     TaskDesc task[kMaxTasks];
     int32_t ntasks;
-    int32_t nworkers;        // active workers (<= gridDim.x * warps_for(ncols), <= natoms)
-    int32_t packed;          // 1: worker = cta * warps + warp (CTA-contiguous ranges);
-                             // 0: worker = warp * gridDim.x + cta (small problems spread over SMs)
+    int32_t nworkers;        // active workers (<= gridDim.x * rings_for(ncols), <= natoms)
+    int32_t packed;          // 1: worker = cta * rings + ring (CTA-contiguous ranges);
+                             // 0: worker = ring * gridDim.x + cta (small problems spread over SMs)
     int32_t pad0_;
     int64_t natoms;
     int32_t *counters;       // one per global row group, zero at kernel start

@@ -282,15 +282,40 @@ __device__ __forceinline__ void sb_dot(uint32_t p, uint32_t act, uint64_t (&acc)
     }
 }
 
-template <int NC, bool DUMP>
+// Columns [j0, j0 + NCW) of one atom (all NC columns unless two warps split
+// them) against its ring stage.
+// A row's running sums, one per column.  Each super-block is summed in fp32
+// from zero (16 products per column) and added here with Kahan compensation:
+// the running sum of a row can grow far beyond its final value, and plain
+// fp32 accumulation across super-blocks loses ~1e-4 absolute on rows that
+// cancel (outside the 1e-4 + 1e-5 relative bar for K >= 14336).
+template <int NCW>
+struct RowAcc {
+    float sum[NCW];
+    float comp[NCW];  // low-order part lost by sum, negated
+    __device__ __forceinline__ void clear() {
+#pragma unroll
+        for (int j = 0; j < NCW; ++j) sum[j] = comp[j] = 0.0f;
+    }
+    __device__ __forceinline__ void add(int j, float v) {
+        const float y = v - comp[j];
+        const float t = sum[j] + y;
+        comp[j] = (t - sum[j]) - y;
+        sum[j] = t;
+    }
+    __device__ __forceinline__ float value(int j) const { return sum[j] - comp[j]; }
+};
+
+template <int NCW, int NC, bool DUMP>
 __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCursor &c, uint32_t stage, int lane,
-                                             uint64_t (&acc)[NC]) {
+                                             int j0, RowAcc<NCW> &acc) {
     const TaskDesc &T = P.task[c.t];
     const int rows = min(32, T.nrows - c.g * 32);
     const int kb0 = c.kp * kKS;
     const int nsb = min(kKS, T.nb - kb0);
     if (lane >= rows) return;
     const int row = c.g * 32 + lane;
+    const uint32_t act = stage + Stage<NC>::kActOff + j0 * (kKS * kActSBBytes);
 #pragma unroll
     for (int i = 0; i < kKS; ++i) {
         if (i < nsb) {
@@ -298,10 +323,17 @@ __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCurs
             int64_t dcs = 0;
             if constexpr (DUMP) {
                 dcs = static_cast<int64_t>(T.nrows) * T.nb * 8;
-                dS = P.dump_S + static_cast<int64_t>(row) * T.nb * 8 + (kb0 + i) * 8;
+                dS = P.dump_S + j0 * dcs + static_cast<int64_t>(row) * T.nb * 8 + (kb0 + i) * 8;
             }
-            sb_dot<NC, DUMP>(stage + i * kBoxBytes + lane * kPitch, stage + Stage<NC>::kActOff + i * kActSBBytes,
-                             acc, dS, dcs);
+            uint64_t sb[NCW];
+#pragma unroll
+            for (int j = 0; j < NCW; ++j) sb[j] = 0ull;
+            sb_dot<NCW, DUMP>(stage + i * kBoxBytes + lane * kPitch, act + i * kActSBBytes, sb, dS, dcs);
+#pragma unroll
+            for (int j = 0; j < NCW; ++j) {
+                const float2 v = f2_unpack(sb[j]);
+                acc.add(j, v.x + v.y);
+            }
         }
     }
 }
@@ -318,22 +350,24 @@ __device__ __forceinline__ void store_out(const GemvParams &P, const TaskDesc &T
     }
 }
 
-// Finish a row group this warp worked on: write it out directly if the warp
-// covered all of its atoms, otherwise deposit the partial sums and let the
-// last of the contributing warps add them up (always in worker order, so the
-// result is deterministic) and write.  Contributors that all belong to this
-// CTA count arrivals in shared memory under block-scope ordering; otherwise a
-// device-scope acquire-release counter in the workspace is used.
-template <int NC, bool DUMP>
-__device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCursor &cur, uint64_t (&acc)[NC],
-                                            int64_t worker, int64_t a0, int64_t a1, int lane, int64_t cta_w0,
-                                            int64_t cta_w1, int *cta_cnt) {
+// Finish a row group this warp worked on: write it out directly if the
+// worker covered all of its atoms, otherwise deposit the partial sums and let
+// the last of the contributing warps add them up (always in worker order, so
+// the result is deterministic) and write.  With a column split both warps of
+// a worker deposit their columns and count as arrivals.  Contributors that all
+// belong to this CTA count arrivals in shared memory under block-scope
+// ordering; otherwise a device-scope acquire-release counter in the workspace
+// is used.
+template <int NCW, int NC, bool DUMP>
+__device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCursor &cur, const RowAcc<NCW> &acc,
+                                            int64_t worker, int64_t a0, int64_t a1, int lane, int j0,
+                                            int64_t cta_w0, int64_t cta_w1, int *cta_cnt) {
+    constexpr int kSplit = split_for(NC);
     const TaskDesc &T = P.task[cur.t];
-    float v[NC];
+    float v[NCW];
 #pragma unroll
-    for (int j = 0; j < NC; ++j) {
-        const float2 p = f2_unpack(acc[j]);
-        v[j] = p.x + p.y;
+    for (int j = 0; j < NCW; ++j) {
+        v[j] = acc.value(j);
     }
     const int64_t sg = T.atom_base + static_cast<int64_t>(cur.g) * T.apr;
     const int64_t eg = sg + T.apr;
@@ -342,15 +376,16 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
     if (sg >= a0 && eg <= a1) {
         if (!DUMP && valid) {
 #pragma unroll
-            for (int j = 0; j < NC; ++j) store_out(P, T, j, row, v[j]);
+            for (int j = 0; j < NCW; ++j) store_out(P, T, j0 + j, row, v[j]);
         }
         return;
     }
     const int slot = (a0 > sg) ? 0 : 1;  // 0: group began before this worker, 1: it covers the start
-    float *mine = P.partials + ((worker * 2 + slot) * NC) * 32;
+    float *mine = P.partials + ((worker * 2 + slot) * NC + j0) * 32;
 #pragma unroll
-    for (int j = 0; j < NC; ++j) mine[j * 32 + lane] = v[j];
+    for (int j = 0; j < NCW; ++j) mine[j * 32 + lane] = v[j];
     const int64_t w1 = worker_of(P, sg), w2 = worker_of(P, eg - 1);
+    const int last = kSplit * static_cast<int>(w2 - w1 + 1) - 1;
     const bool local = P.packed && w1 >= cta_w0 && w2 <= cta_w1;
     int old = 0;
     if (local) {
@@ -358,13 +393,13 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
         __syncwarp();
         if (lane == 0) old = atomicAdd(&cta_cnt[w1 - cta_w0], 1);
         old = __shfl_sync(0xffffffffu, old, 0);
-        if (old != static_cast<int>(w2 - w1)) return;  // not the last contributor
+        if (old != last) return;  // not the last contributor
         __threadfence_block();
     } else {
         __syncwarp();
         if (lane == 0) old = atom_add_acqrel_gpu(&P.counters[T.rg_base + cur.g], 1);
         old = __shfl_sync(0xffffffffu, old, 0);
-        if (old != static_cast<int>(w2 - w1)) return;
+        if (old != last) return;
         __syncwarp();
     }
     float tot[NC];
@@ -398,39 +433,46 @@ struct WorkerPipe {
 
 // Issue the weight copies of the first kStages atoms (they do not depend on
 // any earlier grid: the weights are read-only).
+// (A column-split partner only follows the cursors: issue == false.)
 template <int NC>
 __device__ __forceinline__ void worker_prologue(const GemvParams &P, WorkerPipe &W, int lane,
-                                                const uint32_t (&bar)[kStages]) {
+                                                const uint32_t (&bar)[kStages], bool issue) {
     constexpr int kSB = Stage<NC>::kBytes;
     W.icur = locate_atom(P, W.a0);
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
         W.pro[s] = W.icur;
         if (s < W.n) {
-            issue_weights<NC>(P, W.icur, W.ring + s * kSB, bar[s], lane);
+            if (issue) issue_weights<NC>(P, W.icur, W.ring + s * kSB, bar[s], lane);
             advance(P, W.icur);
         }
     }
 }
 
 // The rest of one worker's range, once the activations are ready: stream its
-// atoms through the warp's ring and flush its row groups.  Returns (never
-// exits the kernel) so that the CTA-wide epilogues can still run.
-template <int NC, bool DUMP>
-__device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, int64_t worker, int lane,
-                                            const uint32_t (&bar)[kStages], int64_t cta_w0, int64_t cta_w1,
+// atoms through the ring and flush its row groups.  The issuer warp (the only
+// one unless the columns are split) owns the copies; with a split it refills
+// a stage only after both warps have released it (empty barrier, two
+// arrivals).  Returns (never exits the kernel) so that the CTA-wide epilogues
+// can still run.
+template <int NC, int NCW, bool DUMP>
+__device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, int64_t worker, int lane, int j0,
+                                            bool issuer, const uint32_t (&full)[kStages],
+                                            const uint32_t (&empty)[kStages], int64_t cta_w0, int64_t cta_w1,
                                             int *cta_cnt) {
     constexpr int kSB = Stage<NC>::kBytes;
+    constexpr bool kShared = split_for(NC) > 1;
     const int n = W.n;
     const uint32_t ring = W.ring;
     AtomCursor icur = W.icur;
+    if (issuer) {
 #pragma unroll
-    for (int s = 0; s < kStages; ++s)
-        if (s < n) issue_acts<NC>(P, W.pro[s], ring + s * kSB, bar[s], lane);
+        for (int s = 0; s < kStages; ++s)
+            if (s < n) issue_acts<NC>(P, W.pro[s], ring + s * kSB, full[s], lane);
+    }
 
-    uint64_t acc[NC];
-#pragma unroll
-    for (int j = 0; j < NC; ++j) acc[j] = 0ull;
+    RowAcc<NCW> acc;
+    acc.clear();
     AtomCursor cur = W.pro[0];
     int open_t = -1, open_g = -1;
 
@@ -440,35 +482,46 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
         if (cur.t != open_t || cur.g != open_g) {
             if (open_t >= 0) {
                 AtomCursor o{open_t, open_g, 0};
-                flush_group<NC, DUMP>(P, o, acc, worker, W.a0, W.a1, lane, cta_w0, cta_w1, cta_cnt);
+                flush_group<NCW, NC, DUMP>(P, o, acc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1, cta_cnt);
             }
             open_t = cur.t;
             open_g = cur.g;
-#pragma unroll
-            for (int j = 0; j < NC; ++j) acc[j] = 0ull;
+            acc.clear();
         }
-        if (!wait_phase(bar[s], parity, kWaitLimitNs)) {
+        bool ok = wait_phase(full[s], parity, kWaitLimitNs);
+        if (ok) {
+            compute_atom<NCW, NC, DUMP>(P, cur, ring + s * kSB, lane, j0, acc);
+            __syncwarp();
+            if constexpr (kShared) {
+                if (lane == 0) mbar_arrive(empty[s]);
+            }
+            if (issuer && i + kStages < n) {
+                if constexpr (kShared) ok = wait_phase(empty[s], parity, kWaitLimitNs);
+                if (ok) {
+                    fence_proxy_async_smem();
+                    issue_weights<NC>(P, icur, ring + s * kSB, full[s], lane);
+                    issue_acts<NC>(P, icur, ring + s * kSB, full[s], lane);
+                    advance(P, icur);
+                }
+            }
+        }
+        if (!ok) {
             if (lane == 0) atomicExch(P.status, kStatusTimeout);
-            // Let this warp's other copies in flight land (bounded) before leaving.
-            for (int k = 1; k < kStages; ++k) {
-                const int ii = i + k;
-                if (ii < n) wait_phase(bar[ii % kStages], static_cast<uint32_t>((ii / kStages) & 1), kDrainLimitNs);
+            // The issuer lets its other copies in flight land (bounded) before leaving.
+            if (issuer) {
+                for (int k = 1; k < kStages; ++k) {
+                    const int ii = i + k;
+                    if (ii < n)
+                        wait_phase(full[ii % kStages], static_cast<uint32_t>((ii / kStages) & 1), kDrainLimitNs);
+                }
             }
             return;
-        }
-        compute_atom<NC, DUMP>(P, cur, ring + s * kSB, lane, acc);
-        __syncwarp();
-        if (i + kStages < n) {
-            fence_proxy_async_smem();
-            issue_weights<NC>(P, icur, ring + s * kSB, bar[s], lane);
-            issue_acts<NC>(P, icur, ring + s * kSB, bar[s], lane);
-            advance(P, icur);
         }
         advance(P, cur);
     }
     if (open_t >= 0) {
         AtomCursor o{open_t, open_g, 0};
-        flush_group<NC, DUMP>(P, o, acc, worker, W.a0, W.a1, lane, cta_w0, cta_w1, cta_cnt);
+        flush_group<NCW, NC, DUMP>(P, o, acc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1, cta_cnt);
     }
 }
 
@@ -576,46 +629,57 @@ __device__ __forceinline__ void gather_epilogue(const GemvParams &P) {
 
 template <int NC, bool DUMP>
 __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
-    constexpr int kW = warps_for(NC);
+    constexpr int kR = rings_for(NC);
+    constexpr int kSplit = split_for(NC);
+    constexpr int kNC0 = (NC + kSplit - 1) / kSplit;  // columns of the issuer warp
     constexpr int kSB = Stage<NC>::kBytes;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bars[kW][kStages];
-    __shared__ int cta_cnt[kW];  // arrivals at row groups split between this CTA's warps
+    __shared__ __align__(8) uint64_t full_bars[kR][kStages];
+    __shared__ __align__(8) uint64_t empty_bars[kR][kStages];
+    __shared__ int cta_cnt[kR];  // arrivals at row groups split between this CTA's workers
 
     // The next launch on the stream may start now; it waits for this grid's
     // completion before it touches the workspace.
     pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    if (threadIdx.x < kW) cta_cnt[threadIdx.x] = 0;
+    const int rid = warp / kSplit;           // ring = worker slot in this CTA
+    const int half = warp - rid * kSplit;    // 0: issuer, columns [0, kNC0); 1: columns [kNC0, NC)
+    if (threadIdx.x < kR) {
+        cta_cnt[threadIdx.x] = 0;
+#pragma unroll
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_addr(&full_bars[threadIdx.x][s]), 1);
+            mbar_init(smem_addr(&empty_bars[threadIdx.x][s]), kSplit);
+        }
+        mbar_fence_init();
+    }
     __syncthreads();
     // Large problems: CTA-contiguous worker ranges (most split row groups stay
     // inside a CTA).  Small ones: consecutive workers on different SMs.
-    const int64_t worker = P.packed ? static_cast<int64_t>(blockIdx.x) * kW + warp
-                                    : static_cast<int64_t>(warp) * gridDim.x + blockIdx.x;
-    const int64_t cta_w0 = static_cast<int64_t>(blockIdx.x) * kW;
-    const int64_t cta_w1 = cta_w0 + kW - 1;
+    const int64_t worker = P.packed ? static_cast<int64_t>(blockIdx.x) * kR + rid
+                                    : static_cast<int64_t>(rid) * gridDim.x + blockIdx.x;
+    const int64_t cta_w0 = static_cast<int64_t>(blockIdx.x) * kR;
+    const int64_t cta_w1 = cta_w0 + kR - 1;
     const bool active = worker < P.nworkers;
-    uint32_t bar[kStages];
+    const bool issuer = half == 0;
+    uint32_t full[kStages], empty[kStages];
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+        full[s] = smem_addr(&full_bars[rid][s]);
+        empty[s] = smem_addr(&empty_bars[rid][s]);
+    }
     WorkerPipe W;
     if (active) {
         W.a0 = worker_begin(P, worker);
         W.a1 = worker_begin(P, worker + 1);
         W.n = static_cast<int>(W.a1 - W.a0);
-        W.ring = smem_addr(smem) + static_cast<uint32_t>(warp * kStages * kSB);
-#pragma unroll
-        for (int s = 0; s < kStages; ++s) bar[s] = smem_addr(&bars[warp][s]);
-        if (lane == 0) {
-#pragma unroll
-            for (int s = 0; s < kStages; ++s) mbar_init(bar[s], 1);
-            mbar_fence_init();
-        }
-        __syncwarp();
+        W.ring = smem_addr(smem) + static_cast<uint32_t>(rid * kStages * kSB);
     }
     // Weights stream while the previous grid on the stream (the prep launch,
     // or the previous single-launch GEMV) finishes; griddepcontrol.wait
     // returns once it has completed.
-    if (active) worker_prologue<NC>(P, W, lane, bar);
+    if (active) worker_prologue<NC>(P, W, lane, full, issuer);
     pdl_wait();
     if (P.fused) {
         // Single launch: quantize this CTA's share of the activations, then a
@@ -633,7 +697,14 @@ __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_con
         grid_barrier_wait(P, target);
         fence_proxy_async_global();  // the q8a records are read by bulk copies next
     }
-    if (active) worker_main<NC, DUMP>(P, W, worker, lane, bar, cta_w0, cta_w1, cta_cnt);
+    if (active) {
+        if (issuer) {
+            worker_main<NC, kNC0, DUMP>(P, W, worker, lane, 0, true, full, empty, cta_w0, cta_w1, cta_cnt);
+        } else if constexpr (kSplit > 1) {
+            worker_main<NC, NC - kNC0, DUMP>(P, W, worker, lane, kNC0, false, full, empty, cta_w0, cta_w1,
+                                             cta_cnt);
+        }
+    }
     if (!DUMP && P.gworld > 1) gather_epilogue(P);
 }
 
