@@ -43,13 +43,17 @@ PKG_DIR = ROOT / "gemv-q4_k-optimization_b200"
 PROFILES = ROOT / "profiles"
 METRIC = "Q4_K GEMV achieved HBM TB/s (algorithmic bytes), us per GEMV launch"
 
-# A launch group is one q4k_gemv_batch launch: (name, rows, K, activation group).
+# A launch group is one q4k_gemv_batch launch: (name, rows, K, activation group
+# [, glu op]).  An entry with a glu op is a gate/up pair fused in one task
+# (two matrices of rows x K, one output: op(up.x, gate.x)).
 MISTRAL_LAYER = [("q", 4096, 4096, "attn"), ("k", 1024, 4096, "attn"), ("v", 1024, 4096, "attn"),
                  ("o", 4096, 4096, "o"), ("gate", 14336, 4096, "ffn"), ("up", 14336, 4096, "ffn"),
                  ("down", 4096, 14336, "down")]
 LLAMA70B_LAYER = [("q", 8192, 8192, "attn"), ("k", 1024, 8192, "attn"), ("v", 1024, 8192, "attn"),
                   ("o", 8192, 8192, "o"), ("gate", 28672, 8192, "ffn"), ("up", 28672, 8192, "ffn"),
                   ("down", 8192, 28672, "down")]
+MISTRAL_LAYER_FUSED = [e for e in MISTRAL_LAYER if e[0] not in ("gate", "up")]
+MISTRAL_LAYER_FUSED.insert(4, ("gate_up", 14336, 4096, "ffn", "swiglu"))
 # BASELINE config -> (workload name, repeated launch group, default repeats, trailing groups)
 WORKLOADS = {
     "2": ("mistral-7b-decode-gemv-set", MISTRAL_LAYER, 32, [[("head", 32000, 4096, "head")]]),
@@ -58,7 +62,16 @@ WORKLOADS = {
     "4": ("llama-3-70b-layer-gemvs", LLAMA70B_LAYER, 8, []),
     "5": ("head-128256x8192", [("head", 128256, 8192, "x")], 6, []),
     "5t": ("tiny-1024x4096-and-512x4096", [("tiny_1024", 1024, 4096, "x")], 256, []),
+    # next-row workloads: the fused gate+up+SwiGLU epilogue
+    "2f": ("mistral-7b-decode-gemv-set-ffn-gate-up-swiglu-fused", MISTRAL_LAYER_FUSED, 32,
+           [[("head", 32000, 4096, "head")]]),
+    "ffn": ("ffn-gate-up-swiglu-2x14336x4096", [("gate_up", 14336, 4096, "x", "swiglu")], 16, []),
 }
+
+
+def ent(e):
+    """(name, rows, K, activation group, glu op or None) of a group entry."""
+    return (e[0], e[1], e[2], e[3], e[4] if len(e) > 4 else None)
 
 
 def build_groups(cfg: str, repeats: int):
@@ -73,11 +86,11 @@ def build_groups(cfg: str, repeats: int):
 def group_bytes(group, ncols: int, world: int = 1) -> int:
     """Algorithmic bytes of one launch group, all ranks (every rank reads the whole x)."""
     acts = {}
-    for _, r, K, a in group:
+    for _, r, K, a, _ in map(ent, group):
         acts[a] = K
-    w = sum(r * K * 9 // 16 for _, r, K, _ in group)
+    w = sum(r * K * 9 // 16 * (2 if glu else 1) for _, r, K, _, glu in map(ent, group))
     x = sum(ncols * K * 4 for K in acts.values()) * world
-    y = sum(ncols * r * 4 for _, r, _, _ in group)
+    y = sum(ncols * r * 4 for _, r, _, _, _ in map(ent, group))
     return w + x + y
 
 
@@ -169,8 +182,9 @@ class ClockSampler:
 # CPU legs (the oracle and the reference's own dot product; checkers only)
 # ---------------------------------------------------------------------------
 def host_group(q4k, group, ncols, rng):
-    mats = [(q4k.gen_q4k_numpy(rng, r, K), K, a) for _, r, K, a in group]
-    xs = {a: rng.standard_normal((ncols, K)).astype(np.float32) for _, _, K, a in group}
+    mats = [(q4k.gen_q4k_numpy(rng, r, K), K, a) for _, r, K, a, glu in map(ent, group)
+            for _ in range(2 if glu else 1)]
+    xs = {a: rng.standard_normal((ncols, K)).astype(np.float32) for _, _, K, a, _ in map(ent, group)}
     return mats, xs
 
 
@@ -222,7 +236,7 @@ def run_reference(args) -> None:
 def cpu_baseline(O, mats, group, ncols, budget_s: float = 12.0) -> dict:
     """The oracle (all host threads) on the first launch group, repeated for ~budget_s."""
     rng = np.random.default_rng(1)
-    xs = {a: rng.standard_normal((ncols, K)).astype(np.float32) for _, _, K, a in group}
+    xs = {a: rng.standard_normal((ncols, K)).astype(np.float32) for _, _, K, a, _ in map(ent, group)}
     threads = O.max_threads()
     n, t0 = 0, time.perf_counter()
     while True:
@@ -286,17 +300,22 @@ def main():
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
     peer = world > 1 and args.gather == "peer"
-    full_elems = sum(r * ncols for grp in groups for _, r, _, _ in grp)
+    full_elems = sum(r * ncols for grp in groups for _, r, _, _, _ in map(ent, grp))
+    fused = any(glu for grp in groups for *_, glu in map(ent, grp))
+    if fused and world > 1:
+        raise SystemExit(f"config {args.config} (fused gate/up epilogue) runs on one GPU")
     pg = q4k.PeerGather(full_elems) if peer else None
     L = []
     base = 0
     for grp in groups:
-        xs = {a: torch.randn((ncols, K), device=dev, generator=g) for _, _, K, a in grp}
+        xs = {a: torch.randn((ncols, K), device=dev, generator=g) for _, _, K, a, _ in map(ent, grp)}
         ents = []
-        for name, rows, K, a in grp:
+        for name, rows, K, a, glu in map(ent, grp):
             lo, hi, per = q4k.shard_rows(rows, rank, world)
             W = q4k.gen_q4k_torch(hi - lo, K, generator=g, device=dev)
-            ents.append(dict(name=name, W=W, x=xs[a], rows=rows, K=K, lo=lo, n=hi - lo, per=per))
+            Wg = q4k.gen_q4k_torch(hi - lo, K, generator=g, device=dev) if glu else None
+            ents.append(dict(name=name, W=W, W_gate=Wg, glu=glu, x=xs[a], rows=rows, K=K, lo=lo, n=hi - lo,
+                             per=per))
         if peer:
             # full outputs live in the shared buffer; each rank writes its rows
             # there and the kernel stores them into every peer's buffer too
@@ -316,17 +335,26 @@ def main():
                 e["stride"] = e["per"]
                 off += e["per"] * ncols
             gath = torch.empty((per_tot * ncols * world,), device=dev) if world > 1 else None
-        tasks = q4k.make_tasks([e["W"] for e in ents], [e["x"] for e in ents], outs)
-        for i, e in enumerate(ents):
-            tasks[i].stride_col_dst = e["stride"]
+        if fused:
+            tasks = q4k.make_tasks_ex([dict(W=e["W"], W_gate=e["W_gate"], x=e["x"], out=o,
+                                            glu=e["glu"] or "none") for e, o in zip(ents, outs)])
+            for i, e in enumerate(ents):
+                tasks[i].t.stride_col_dst = e["stride"]
+        else:
+            tasks = q4k.make_tasks([e["W"] for e in ents], [e["x"] for e in ents], outs)
+            for i, e in enumerate(ents):
+                tasks[i].stride_col_dst = e["stride"]
         L.append(dict(xs=xs, ents=ents, ybuf=ybuf, tasks=tasks, gath=gath))
 
-    ws = q4k.Workspace(max(q4k.batch_workspace_bytes(G["tasks"], ncols) for G in L), dev)
+    wsb = q4k.batch_ex_workspace_bytes if fused else q4k.batch_workspace_bytes
+    ws = q4k.Workspace(max(wsb(G["tasks"], ncols) for G in L), dev)
     stream = torch.cuda.Stream(device=dev)
 
     def gemv(tasks):
         if peer:
             q4k.gemv_batch_allgather(tasks, ncols, pg, ws, stream=stream)
+        elif fused:
+            q4k.gemv_batch_ex(tasks, ncols, ws, stream=stream)
         else:
             q4k.gemv_batch(tasks, ncols, ws, stream=stream)
 
@@ -437,7 +465,8 @@ def main():
     if world == 1:
         launch_bytes = group_bytes(g0, ncols)
     else:  # this rank's share of the first launch group
-        launch_bytes = (sum(e["n"] * e["K"] * 9 // 16 + ncols * e["n"] * 4 for e in L[0]["ents"]) +
+        launch_bytes = (sum(e["n"] * e["K"] * 9 // 16 * (2 if e["glu"] else 1) + ncols * e["n"] * 4
+                            for e in L[0]["ents"]) +
                         sum(ncols * x.shape[1] * 4 for x in L[0]["xs"].values()))
 
     # ---- e2e: public C-ABI calls with host buffers ------------------------------
@@ -485,7 +514,8 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         O = load_oracle()
-        mats = [(e["W"].cpu().numpy(), e["K"], a) for e, (_, _, _, a) in zip(L[0]["ents"], g0)]
+        mats = [(M.cpu().numpy(), e["K"], a) for e, (_, _, _, a, _) in zip(L[0]["ents"], map(ent, g0))
+                for M in (e["W"], e["W_gate"]) if M is not None]
         cpu = cpu_baseline(O, mats, g0, ncols)
 
     traffic = None
@@ -496,7 +526,7 @@ def main():
             traffic = d.get("dram_bytes_per_launch")
 
     if rank == 0:
-        shapes = sorted({f"{r}x{K}" for grp in groups for _, r, K, _ in grp})
+        shapes = sorted({f"{r}x{K}" for grp in groups for _, r, K, _, _ in map(ent, grp)})
         line = {
             "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -505,7 +535,8 @@ def main():
                        "baseline_config": args.config, "launch_groups": nlaunch, "shapes": shapes,
                        "ncols": ncols,
                        "launches": "per group: prep (q8_1 quantization) + persistent GEMV over the group's "
-                                   "matrices, chained with programmatic dependencies",
+                                   "matrices, chained with programmatic dependencies" + (
+                                       "; ffn gate+up as one task with the SwiGLU epilogue" if fused else ""),
                        "timing": "one CUDA graph per step, CUDA events on the launch stream around all timed steps",
                        "l2": "inputs larger than L2 (weights per step >= 3x the 126 MB L2), no flush needed",
                        "parallelism": "single GPU" if world == 1 else (

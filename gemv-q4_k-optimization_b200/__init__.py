@@ -66,6 +66,17 @@ class Task(ctypes.Structure):
                 ("stride_col_x", ctypes.c_int64), ("stride_col_dst", ctypes.c_int64)]
 
 
+class TaskEx(ctypes.Structure):
+    """struct q4k_task_ex (include/q4k_gemv.h): a task with an optional fused epilogue."""
+    _fields_ = [("t", Task), ("W_gate", ctypes.c_void_p), ("x_bias", ctypes.c_void_p),
+                ("gate_bias", ctypes.c_void_p), ("stride_col_bias", ctypes.c_int64), ("glu_op", ctypes.c_int)]
+
+
+# Q4K_GLU_* (include/q4k_gemv.h)
+GLU_NONE, GLU_SWIGLU, GLU_GEGLU, GLU_SWIGLU_OAI, GLU_MUL = 0, 1, 2, 3, 4
+GLU_OPS = {"none": GLU_NONE, "swiglu": GLU_SWIGLU, "geglu": GLU_GEGLU, "swiglu_oai": GLU_SWIGLU_OAI,
+           "mul": GLU_MUL}
+
 _lib = None
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -87,37 +98,49 @@ def lib() -> ctypes.CDLL:
             raise RuntimeError(f"{LIB_PATH} is missing: build the CUDA library first "
                                f"(make -C {HERE})")
         L = ctypes.CDLL(str(LIB_PATH))
-        L.q4k_status_string.restype = ctypes.c_char_p
-        L.q4k_status_string.argtypes = [_I]
-        L.q4k_last_error.restype = ctypes.c_char_p
-        L.q4k_version.restype = _I
-        L.q4k_device_supported.restype = _I
-        L.q4k_row_bytes.restype = _SZ
-        L.q4k_row_bytes.argtypes = [_I64]
-        L.q4k_q8_1_bytes.restype = _SZ
-        L.q4k_q8_1_bytes.argtypes = [_I64, _I]
-        L.q4k_gemv_workspace_bytes.restype = _SZ
-        L.q4k_gemv_workspace_bytes.argtypes = [_I64, _I64, _I]
-        L.q4k_batch_workspace_bytes.restype = _SZ
-        L.q4k_batch_workspace_bytes.argtypes = [ctypes.POINTER(Task), _I, _I]
-        L.q4k_quantize_q8_1.argtypes = [_P, _I64, _I64, _I64, _I, _P, _P]
-        L.q4k_mul_mat_vec_q8_1.argtypes = [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _SZ, _P]
-        L.q4k_mul_mat_vec.argtypes = [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _SZ, _P]
-        L.q4k_op_mul_mat_vec_q.argtypes = [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P]
-        L.q4k_custom_q4k_gemv.argtypes = [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]
-        L.q4k_gemv_batch.argtypes = [ctypes.POINTER(Task), _I, _I, _P, _SZ, _P]
-        L.q4k_debug_subblock_sums.argtypes = [_P, _P, _I64, _I64, _I, _I64, _I64, _P, _P, _P, _SZ, _P]
-        L.q4k_workspace_status.argtypes = [_P, ctypes.POINTER(_I), _P]
-        L.q4k_mul_mat_vec_noalloc.argtypes = [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P]
-        L.q4k_gemv_batch_allgather.argtypes = [ctypes.POINTER(Task), _I, _I, ctypes.POINTER(Gather), _P, _SZ, _P]
-        L.q4k_workspace_init.argtypes = [_P, _SZ, _P]
-        L.q4k_gemv_batch_persistent.argtypes = [ctypes.POINTER(Task), _I, _I, ctypes.POINTER(Gather), _P, _SZ, _P]
-        L.q4k_ipc_alloc.argtypes = [_SZ, ctypes.POINTER(ctypes.c_void_p)]
-        L.q4k_ipc_free.argtypes = [_P]
-        L.q4k_ipc_handle.argtypes = [_P, ctypes.c_char_p]
-        L.q4k_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
-        L.q4k_ipc_close.argtypes = [_P]
-        L.q4k_noalloc_scratch_bytes.restype = _SZ
+        TP, GP, TXP = ctypes.POINTER(Task), ctypes.POINTER(Gather), ctypes.POINTER(TaskEx)
+        sigs = {  # name: (restype, argtypes); restype None = int status
+            "q4k_status_string": (ctypes.c_char_p, [_I]),
+            "q4k_last_error": (ctypes.c_char_p, []),
+            "q4k_version": (_I, []),
+            "q4k_device_supported": (_I, []),
+            "q4k_row_bytes": (_SZ, [_I64]),
+            "q4k_q8_1_bytes": (_SZ, [_I64, _I]),
+            "q4k_gemv_workspace_bytes": (_SZ, [_I64, _I64, _I]),
+            "q4k_batch_workspace_bytes": (_SZ, [TP, _I, _I]),
+            "q4k_quantize_q8_1": (None, [_P, _I64, _I64, _I64, _I, _P, _P]),
+            "q4k_mul_mat_vec_q8_1": (None, [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _SZ, _P]),
+            "q4k_mul_mat_vec": (None, [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _SZ, _P]),
+            "q4k_op_mul_mat_vec_q": (None, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
+            "q4k_custom_q4k_gemv": (None, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
+            "q4k_gemv_batch": (None, [TP, _I, _I, _P, _SZ, _P]),
+            "q4k_debug_subblock_sums": (None, [_P, _P, _I64, _I64, _I, _I64, _I64, _P, _P, _P, _SZ, _P]),
+            "q4k_workspace_status": (None, [_P, ctypes.POINTER(_I), _P]),
+            "q4k_mul_mat_vec_noalloc": (None, [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P]),
+            "q4k_noalloc_scratch_bytes": (_SZ, []),
+            "q4k_gemv_batch_allgather": (None, [TP, _I, _I, GP, _P, _SZ, _P]),
+            "q4k_workspace_init": (None, [_P, _SZ, _P]),
+            "q4k_gemv_batch_persistent": (None, [TP, _I, _I, GP, _P, _SZ, _P]),
+            "q4k_batch_ex_workspace_bytes": (_SZ, [TXP, _I, _I]),
+            "q4k_gemv_batch_ex": (None, [TXP, _I, _I, _P, _SZ, _P]),
+            "q4k_gemv_fused_workspace_bytes": (_SZ, [_I64, _I64, _I]),
+            "q4k_mul_mat_vec_q8_1_fused": (None, [_P, _P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _P, _I,
+                                                  _P, _SZ, _P]),
+            "q4k_mul_mat_vec_fused": (None, [_P, _P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _P, _I,
+                                             _P, _SZ, _P]),
+            "q4k_ipc_alloc": (None, [_SZ, ctypes.POINTER(ctypes.c_void_p)]),
+            "q4k_ipc_free": (None, [_P]),
+            "q4k_ipc_handle": (None, [_P, ctypes.c_char_p]),
+            "q4k_ipc_open": (None, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+            "q4k_ipc_close": (None, [_P]),
+        }
+        overridden = "Q4K_LIB" in os.environ
+        for name, (res, args) in sigs.items():
+            fn = getattr(L, name, None) if overridden else getattr(L, name)  # the in-tree build must have all
+            if fn is None:
+                continue
+            fn.restype = res if res is not None else _I
+            fn.argtypes = args
         _lib = L
     return _lib
 
@@ -330,6 +353,75 @@ def gemv_batch(tasks, ncols: int, ws: Workspace, stream=None) -> None:
     """Every task's GEMV in one prep + one persistent GEMV launch."""
     ws.ensure(batch_workspace_bytes(tasks, ncols))
     _check(lib().q4k_gemv_batch(tasks, len(tasks), ncols, ws.ptr, ws.nbytes, _stream(stream)))
+
+
+def _ptr_or_none(t):
+    return None if t is None else t.data_ptr()
+
+
+def make_tasks_ex(items):
+    """ctypes q4k_task_ex array from dicts with keys W, x, out and optionally
+    W_gate, x_bias, gate_bias (tensors; biases (ncols, nrows) or (nrows,)) and
+    glu ("swiglu", "geglu", "swiglu_oai", "mul" or "none")."""
+    arr = (TaskEx * len(items))()
+    for i, it in enumerate(items):
+        base = make_tasks([it["W"]], [it["x"]], [it["out"]])[0]
+        arr[i].t = base
+        arr[i].W_gate = _ptr_or_none(it.get("W_gate"))
+        xb, gb = it.get("x_bias"), it.get("gate_bias")
+        arr[i].x_bias = _ptr_or_none(xb)
+        arr[i].gate_bias = _ptr_or_none(gb)
+        b = xb if xb is not None else gb
+        arr[i].stride_col_bias = b.stride(0) if (b is not None and b.dim() > 1) else 0
+        arr[i].glu_op = GLU_OPS[it.get("glu", "swiglu" if it.get("W_gate") is not None else "none")]
+    return arr
+
+
+def batch_ex_workspace_bytes(tasks, ncols: int) -> int:
+    return int(lib().q4k_batch_ex_workspace_bytes(tasks, len(tasks), ncols))
+
+
+def gemv_batch_ex(tasks, ncols: int, ws: Workspace, stream=None) -> None:
+    """Batched launch of tasks with optional fused bias/gate epilogues."""
+    ws.ensure(batch_ex_workspace_bytes(tasks, ncols))
+    _check(lib().q4k_gemv_batch_ex(tasks, len(tasks), ncols, ws.ptr, ws.nbytes, _stream(stream)))
+
+
+def mul_mat_vec_fused(W, W_gate, x, glu: str = "swiglu", x_bias=None, gate_bias=None, out=None,
+                      ws: Workspace | None = None, stream=None):
+    """glu(W.x + x_bias, W_gate.x + gate_bias) through q4k_mul_mat_vec_fused.
+    x: (ncols, K) fp32; biases: (ncols, nrows) with the output's column stride, or None."""
+    import torch
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    ncols, K = x.shape
+    nrows = W.shape[0]
+    if out is None:
+        out = torch.empty((ncols, nrows), dtype=torch.float32, device=x.device)
+    for b in (x_bias, gate_bias):
+        if b is not None and ncols > 1:
+            assert b.stride(0) == out.stride(0), "bias column stride must equal the output's"
+    w = _ws_for(int(lib().q4k_gemv_fused_workspace_bytes(nrows, K, ncols)), ws, x.device)
+    _check(lib().q4k_mul_mat_vec_fused(W.data_ptr(), _ptr_or_none(W_gate), x.data_ptr(), out.data_ptr(), K, nrows,
+                                       ncols, W.stride(0) // BLOCK_BYTES, x.stride(0), out.stride(0),
+                                       _ptr_or_none(x_bias), _ptr_or_none(gate_bias), GLU_OPS[glu],
+                                       w.ptr, w.nbytes, _stream(stream)))
+    return out
+
+
+def mul_mat_vec_q8_1_fused(W, W_gate, yq, K: int, glu: str = "swiglu", x_bias=None, gate_bias=None, out=None,
+                           ws: Workspace | None = None, stream=None):
+    """The q8_1-input fused entry (q4k_mul_mat_vec_q8_1_fused).  yq: (ncols, Kpad/32*36) uint8."""
+    import torch
+    ncols, nrows = yq.shape[0], W.shape[0]
+    if out is None:
+        out = torch.empty((ncols, nrows), dtype=torch.float32, device=yq.device)
+    w = _ws_for(int(lib().q4k_gemv_fused_workspace_bytes(nrows, K, ncols)), ws, yq.device)
+    _check(lib().q4k_mul_mat_vec_q8_1_fused(W.data_ptr(), _ptr_or_none(W_gate), yq.data_ptr(), out.data_ptr(), K,
+                                            nrows, ncols, W.stride(0) // BLOCK_BYTES, yq.stride(0) // Q8_1_BYTES,
+                                            out.stride(0), _ptr_or_none(x_bias), _ptr_or_none(gate_bias),
+                                            GLU_OPS[glu], w.ptr, w.nbytes, _stream(stream)))
+    return out
 
 
 def gemv_batch_persistent(tasks, ncols: int, ws: Workspace, stream=None, gather=None) -> None:

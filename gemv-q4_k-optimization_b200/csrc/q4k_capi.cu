@@ -71,6 +71,12 @@ struct Job {
     float *dst;
     int64_t nrows, K, stride_row_x, src_col_stride, stride_col_dst;
     int kind;  // kPrepF32 / kPrepQ81
+    // fused epilogue (kernels/mmvq.cu:182-227, :309-338)
+    const void *gate = nullptr;      // gate matrix: same shape and row stride as W
+    const float *x_bias = nullptr;
+    const float *gate_bias = nullptr;
+    int64_t bias_col_stride = 0;
+    int glu_op = Q4K_GLU_NONE;
 };
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -123,6 +129,18 @@ int validate_job(const Job &j, int ncols, int idx) {
     if (!j.dst) return fail(Q4K_EINVAL, "task %d: null dst", idx);
     if (ncols > 1 && j.stride_col_dst < j.nrows)
         return fail(Q4K_EINVAL, "task %d: stride_col_dst=%lld < nrows", idx, (long long)j.stride_col_dst);
+    const bool fused = j.gate || j.x_bias || j.gate_bias || j.glu_op != Q4K_GLU_NONE;
+    if (fused) {
+        if (j.gate ? (j.glu_op < Q4K_GLU_SWIGLU || j.glu_op > Q4K_GLU_MUL) : j.glu_op != Q4K_GLU_NONE)
+            return fail(Q4K_EINVAL, "task %d: glu_op=%d does not match the gate (%s)", idx, j.glu_op,
+                        j.gate ? "given" : "absent");
+        if (j.gate_bias && !j.gate) return fail(Q4K_EINVAL, "task %d: gate_bias without a gate", idx);
+        if (j.gate && !aligned16(j.gate)) return fail(Q4K_EINVAL, "task %d: gate is not 16-byte aligned", idx);
+        if (ncols > 1 && (j.x_bias || j.gate_bias) && j.bias_col_stride != 0 && j.bias_col_stride < j.nrows)
+            return fail(Q4K_EINVAL, "task %d: stride_col_bias=%lld < nrows", idx, (long long)j.bias_col_stride);
+        if (j.bias_col_stride < 0) return fail(Q4K_EINVAL, "task %d: stride_col_bias < 0", idx);
+        if (j.K == 0) return fail(Q4K_EINVAL, "task %d: a fused epilogue needs K > 0", idx);
+    }
     if (j.K == 0) return Q4K_OK;  // empty sums: dst is zeroed
     if (!j.W || !j.src) return fail(Q4K_EINVAL, "task %d: null pointer", idx);
     if (!aligned16(j.W)) return fail(Q4K_EINVAL, "task %d: W is not 16-byte aligned", idx);
@@ -147,6 +165,7 @@ struct Plan {
     int act_of_job[kMaxTasks] = {};
     int n_act = 0;
     bool any_work = false;
+    bool any_fused = false;  // a task with a gate or a bias: the epilogue kernel variant
 };
 
 // Build the schedule (no device memory touched).  ws may be null (sizing).
@@ -181,12 +200,16 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     // row groups and atoms
     int64_t atoms = 0, rgs = 0;
     int nt = 0;
+    int ngated = 0;
+    P.any_fused = false;
     for (int i = 0; i < njobs; ++i) {
         const Job &j = jobs[i];
         if (P.act_of_job[i] < 0) continue;
         const int64_t groups = (j.nrows + 31) / 32;
         const int64_t nb = j.K / Q4K_QK_K;
-        const int64_t apr = (nb + kKS - 1) / kKS;
+        // a gated atom is one super-block position of both matrices
+        const int64_t apr = j.gate ? nb : (nb + kKS - 1) / kKS;
+        if (j.gate || j.x_bias) P.any_fused = true;
         TaskDesc &T = P.gemv.task[nt++];
         T.W = static_cast<const uint8_t *>(j.W);
         T.dst = j.dst;
@@ -206,6 +229,15 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
             if (P.act_of_job[k] == P.act_of_job[i]) T.act_owner = 0;
         T.x = j.kind == kPrepF32 ? static_cast<const float *>(j.src) : nullptr;
         T.x_col_stride = j.src_col_stride;
+        T.has_gate = j.gate ? 1 : 0;
+        T.gate_map = j.gate ? ngated : -1;
+        T.pad2_ = 0;
+        if (j.gate && ++ngated > kMaxGated)
+            return fail(Q4K_EINVAL, "more than %d tasks with a fused gate in one launch", kMaxGated);
+        T.glu_op = j.glu_op;
+        T.x_bias = j.x_bias;
+        T.gate_bias = j.gate_bias;
+        T.bias_col_stride = j.bias_col_stride;
         atoms += groups * apr;
         rgs += groups;
     }
@@ -218,7 +250,10 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.gemv.nworkers = static_cast<int32_t>(nw);
     P.gemv.packed = atoms >= 4 * max_workers ? 1 : 0;
     P.gemv.pad0_ = 0;
-    P.layout = make_layout(rgs, ncols, P.act_bytes, 2 * nw);
+    // the epilogue kernel variant (any gate or bias) keeps gate partials too
+    P.gemv.pcols = P.any_fused ? 2 * ncols : ncols;
+    P.gemv.pad1_ = 0;
+    P.layout = make_layout(rgs, P.gemv.pcols, P.act_bytes, 2 * nw);
     P.gemv.fused = 0;
     P.gemv.ncols = ncols;
     if (ws == nullptr) return Q4K_OK;
@@ -234,6 +269,12 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         const Job &j = jobs[i];
         int st = encode_weight_map(&P.gemv.tmap[nt], j.W, j.nrows, j.K / Q4K_QK_K, j.stride_row_x * Q4K_BLOCK_BYTES);
         if (st != Q4K_OK) return st;
+        if (j.gate) {
+            const int gm = P.gemv.task[nt].gate_map;
+            st = encode_weight_map(&P.gemv.tmap_gate[gm], j.gate, j.nrows, j.K / Q4K_QK_K,
+                                   j.stride_row_x * Q4K_BLOCK_BYTES);
+            if (st != Q4K_OK) return st;
+        }
         P.gemv.task[nt++].act = ws + P.layout.act_off + acts[P.act_of_job[i]].off;
     }
     // prep jobs: one per distinct activation
@@ -333,9 +374,20 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     } else if ((e = launch_prep(P.prep, s)) != cudaSuccess) {
         return cuda_fail(e, "prep launch");
     }
-    if ((e = launch_gemv(P.gemv, ncols, dump_S != nullptr, num_sms, s)) != cudaSuccess)
+    const int mode = dump_S != nullptr ? kModeDump : P.any_fused ? kModeGated : kModePlain;
+    if ((e = launch_gemv(P.gemv, ncols, mode, num_sms, s)) != cudaSuccess)
         return cuda_fail(e, "gemv launch");
     return Q4K_OK;
+}
+
+Job job_of(const q4k_task_ex &t) {
+    Job j{t.t.W, t.t.x, t.t.dst, t.t.nrows, t.t.K, t.t.stride_row_x, t.t.stride_col_x, t.t.stride_col_dst, kPrepF32};
+    j.gate = t.W_gate;
+    j.x_bias = t.x_bias;
+    j.gate_bias = t.gate_bias;
+    j.bias_col_stride = t.stride_col_bias;
+    j.glu_op = t.glu_op;
+    return j;
 }
 
 size_t plan_bytes(const Job *jobs, int njobs, int ncols) {
@@ -488,6 +540,57 @@ int q4k_gemv_batch(const q4k_task *tasks, int ntasks, int ncols, void *workspace
         jobs[i] = {tasks[i].W, tasks[i].x, tasks[i].dst, tasks[i].nrows, tasks[i].K,
                    tasks[i].stride_row_x, tasks[i].stride_col_x, tasks[i].stride_col_dst, kPrepF32};
     return run(jobs, ntasks, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t q4k_batch_ex_workspace_bytes(const q4k_task_ex *tasks, int ntasks, int ncols) {
+    if (!tasks || ntasks < 1 || ntasks > kMaxTasks) return 0;
+    Job jobs[kMaxTasks];
+    for (int i = 0; i < ntasks; ++i) jobs[i] = job_of(tasks[i]);
+    return plan_bytes(jobs, ntasks, ncols);
+}
+
+int q4k_gemv_batch_ex(const q4k_task_ex *tasks, int ntasks, int ncols, void *workspace, size_t workspace_bytes,
+                      q4k_stream_t stream) {
+    if (!tasks || ntasks < 1 || ntasks > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..16", ntasks);
+    Job jobs[kMaxTasks];
+    for (int i = 0; i < ntasks; ++i) jobs[i] = job_of(tasks[i]);
+    return run(jobs, ntasks, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t q4k_gemv_fused_workspace_bytes(int64_t nrows, int64_t K, int ncols) {
+    static const float dummy = 0.0f;
+    static float dummy_out = 0.0f;
+    Job j{reinterpret_cast<const void *>(uintptr_t(256)), &dummy, &dummy_out, nrows, K, K / Q4K_QK_K,
+          K, nrows, kPrepF32};
+    j.gate = reinterpret_cast<const void *>(uintptr_t(256));
+    j.glu_op = Q4K_GLU_SWIGLU;
+    return plan_bytes(&j, 1, ncols);
+}
+
+int q4k_mul_mat_vec_q8_1_fused(const void *W, const void *W_gate, const void *y_q8_1, float *dst, int64_t K,
+                               int64_t nrows, int ncols, int64_t stride_row_x, int64_t stride_col_y,
+                               int64_t stride_col_dst, const float *x_bias, const float *gate_bias, int glu_op,
+                               void *workspace, size_t workspace_bytes, q4k_stream_t stream) {
+    Job j{W, y_q8_1, dst, nrows, K, stride_row_x, stride_col_y, stride_col_dst, kPrepQ81};
+    j.gate = W_gate;
+    j.x_bias = x_bias;
+    j.gate_bias = gate_bias;
+    j.bias_col_stride = stride_col_dst;  // x_bias[j*stride_col_dst + row], kernels/mmvq.cu:211
+    j.glu_op = glu_op;
+    return run(&j, 1, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int q4k_mul_mat_vec_fused(const void *W, const void *W_gate, const float *x, float *dst, int64_t K, int64_t nrows,
+                          int ncols, int64_t stride_row_x, int64_t stride_col_x, int64_t stride_col_dst,
+                          const float *x_bias, const float *gate_bias, int glu_op, void *workspace,
+                          size_t workspace_bytes, q4k_stream_t stream) {
+    Job j{W, x, dst, nrows, K, stride_row_x, stride_col_x, stride_col_dst, kPrepF32};
+    j.gate = W_gate;
+    j.x_bias = x_bias;
+    j.gate_bias = gate_bias;
+    j.bias_col_stride = stride_col_dst;
+    j.glu_op = glu_op;
+    return run(&j, 1, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int q4k_gemv_batch_allgather(const q4k_task *tasks, int ntasks, int ncols, const q4k_gather *gather,

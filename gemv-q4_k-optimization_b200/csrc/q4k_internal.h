@@ -15,6 +15,7 @@ constexpr int kActSBBytes = 320;  // q8a bytes per super-block and column
 constexpr int kActMetaOff = 256;  // q8a: offset of the per-pair float4 metadata
 constexpr int kMaxCols = 8;
 constexpr int kMaxTasks = 16;
+constexpr int kMaxGated = 4;  // tasks with a fused gate per launch (their tensor maps are kernel parameters)
 constexpr int kMaxJobs = 16;
 constexpr int kMaxPeers = 8;
 
@@ -91,10 +92,24 @@ struct TaskDesc {
     // single-launch path: the fp32 activation this task's q8a records come from
     const float *x;
     int64_t x_col_stride;    // floats between activation columns
+    // Fused epilogue (kernels/mmvq.cu:182-227, :309-338): with a gate matrix
+    // (tensor map tmap_gate[gate_map]) an atom holds one super-block of each
+    // matrix (apr = nb) and the output is glu(W.x + x_bias, Wg.x + gate_bias).
+    int32_t has_gate;
+    int32_t glu_op;          // GluOp
+    int32_t gate_map;
+    int32_t pad2_;
+    const float *x_bias;     // per output row, or nullptr
+    const float *gate_bias;  // per output row, or nullptr (only with a gate)
+    int64_t bias_col_stride; // floats between bias columns (0: one column for all)
 };
 
+// Epilogue ops (values of q4k_gemv.h's Q4K_GLU_*).
+enum GluOp : int32_t { kGluNone = 0, kGluSwiglu = 1, kGluGeglu = 2, kGluSwigluOai = 3, kGluMul = 4 };
+
 struct GemvParams {
-    CUtensorMap tmap[kMaxTasks];  // per task: uint32 view {nb*36, nrows}, box {36, 32}
+    CUtensorMap tmap[kMaxTasks];        // per task: uint32 view {nb*36, nrows}, box {36, 32}
+    CUtensorMap tmap_gate[kMaxGated];   // gate matrices of the tasks with a fused gate
     TaskDesc task[kMaxTasks];
     int32_t ntasks;
     int32_t nworkers;        // active workers (<= gridDim.x * rings_for(ncols), <= natoms)
@@ -103,7 +118,9 @@ struct GemvParams {
     int32_t pad0_;
     int64_t natoms;
     int32_t *counters;       // one per global row group, zero at kernel start
-    float *partials;         // [nworkers][2][ncols][32]
+    float *partials;         // [nworkers][2][pcols][32]
+    int32_t pcols;           // columns per partial slot: ncols, or 2*ncols when a task has a gate
+    int32_t pad1_;
     int32_t *status;
     int32_t *dump_S;         // debug: sub-block sums (nullptr in the product path)
     // Fused all-gather over peer memory (gworld > 1): every output value is
@@ -150,7 +167,9 @@ struct PrepParams {
 
 // Launchers (q4k_kernels.cu).  Return cudaSuccess or the launch error.
 cudaError_t launch_prep(const PrepParams &p, cudaStream_t s);
-cudaError_t launch_gemv(const GemvParams &p, int ncols, bool dump, int grid, cudaStream_t s);
+// Kernel variants: plain, debug dump of the sub-block sums, fused epilogues.
+enum GemvMode : int { kModePlain = 0, kModeDump = 1, kModeGated = 2 };
+cudaError_t launch_gemv(const GemvParams &p, int ncols, int mode, int grid, cudaStream_t s);
 // Per-device setup (SM count, shared-memory opt-in); thread-safe, idempotent.
 cudaError_t device_setup(int *num_sms);
 

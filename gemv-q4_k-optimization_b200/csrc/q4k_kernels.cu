@@ -159,34 +159,43 @@ struct Stage {
     // region starts on a multiple of 128 bytes from the ring base
     static_assert(kBoxBytes % 128 == 0 && kActOff % 128 == 0 && kBytes % 128 == 0, "stage alignment");
 };
-static_assert(sizeof(GemvParams) <= 4096, "kernel parameters exceed 4 KB");
+static_assert(sizeof(GemvParams) <= 32764, "kernel parameters exceed the 32 KB launch limit");
 
 // Announce the atom's bytes and copy its weights: one tensor-map box (32 rows
 // x 144 bytes) per super-block, issued by lane 0.  Rows past the matrix end
 // are zero-filled by the copy and still counted in its byte total.
-template <int NC>
+template <int NC, bool GATED>
 __device__ __forceinline__ void issue_weights(const GemvParams &P, const AtomCursor &c, uint32_t stage,
                                               uint32_t bar, int lane) {
     const TaskDesc &T = P.task[c.t];
-    const int kb0 = c.kp * kKS;
-    const int nsb = min(kKS, T.nb - kb0);
     if (lane == 0) {
-        mbar_expect_tx(bar, static_cast<uint32_t>(nsb * (kBoxBytes + NC * kActSBBytes)));
+        if (GATED && T.has_gate) {
+            // one super-block position of both matrices: box 0 main, box 1 gate
+            static_assert(kKS >= 2, "a gated atom needs two boxes per stage");
+            mbar_expect_tx(bar, static_cast<uint32_t>(2 * kBoxBytes + NC * kActSBBytes));
+            tma_load_2d(stage, &P.tmap[c.t], c.kp * 36, c.g * 32, bar);
+            tma_load_2d(stage + kBoxBytes, &P.tmap_gate[T.gate_map], c.kp * 36, c.g * 32, bar);
+        } else {
+            const int kb0 = c.kp * kKS;
+            const int nsb = min(kKS, T.nb - kb0);
+            mbar_expect_tx(bar, static_cast<uint32_t>(nsb * (kBoxBytes + NC * kActSBBytes)));
 #pragma unroll
-        for (int i = 0; i < kKS; ++i)
-            if (i < nsb) tma_load_2d(stage + i * kBoxBytes, &P.tmap[c.t], (kb0 + i) * 36, c.g * 32, bar);
+            for (int i = 0; i < kKS; ++i)
+                if (i < nsb) tma_load_2d(stage + i * kBoxBytes, &P.tmap[c.t], (kb0 + i) * 36, c.g * 32, bar);
+        }
     }
     __syncwarp();
 }
 
 // Copy the atom's activation records (one copy per column, lanes 0..NC-1).
 // Only after griddepcontrol.wait: the prep kernel writes them.
-template <int NC>
+template <int NC, bool GATED>
 __device__ __forceinline__ void issue_acts(const GemvParams &P, const AtomCursor &c, uint32_t stage,
                                            uint32_t bar, int lane) {
     const TaskDesc &T = P.task[c.t];
-    const int kb0 = c.kp * kKS;
-    const int nsb = min(kKS, T.nb - kb0);
+    const bool gated = GATED && T.has_gate;
+    const int kb0 = gated ? c.kp : c.kp * kKS;
+    const int nsb = gated ? 1 : min(kKS, T.nb - kb0);
     if (lane < NC) {
         const uint8_t *src = T.act + lane * T.act_col_stride + static_cast<int64_t>(kb0) * kActSBBytes;
         bulk_g2s(stage + Stage<NC>::kActOff + lane * (kKS * kActSBBytes), src,
@@ -306,16 +315,40 @@ struct RowAcc {
     __device__ __forceinline__ float value(int j) const { return sum[j] - comp[j]; }
 };
 
-template <int NCW, int NC, bool DUMP>
+template <int NCW>
+__device__ __forceinline__ void add_sb(RowAcc<NCW> &acc, const uint64_t (&sb)[NCW]) {
+#pragma unroll
+    for (int j = 0; j < NCW; ++j) {
+        const float2 v = f2_unpack(sb[j]);
+        acc.add(j, v.x + v.y);
+    }
+}
+
+template <int NCW, int NC, int MODE>
 __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCursor &c, uint32_t stage, int lane,
-                                             int j0, RowAcc<NCW> &acc) {
+                                             int j0, RowAcc<NCW> &acc, RowAcc<NCW> &gacc) {
     const TaskDesc &T = P.task[c.t];
     const int rows = min(32, T.nrows - c.g * 32);
+    if (lane >= rows) return;
+    constexpr bool DUMP = MODE == kModeDump;
+    const uint32_t act = stage + Stage<NC>::kActOff + j0 * (kKS * kActSBBytes);
+    if constexpr (MODE == kModeGated) {
+        if (T.has_gate) {
+            uint64_t sb[NCW];
+#pragma unroll
+            for (int j = 0; j < NCW; ++j) sb[j] = 0ull;
+            sb_dot<NCW, false>(stage + lane * kPitch, act, sb, nullptr, 0);
+            add_sb(acc, sb);
+#pragma unroll
+            for (int j = 0; j < NCW; ++j) sb[j] = 0ull;
+            sb_dot<NCW, false>(stage + kBoxBytes + lane * kPitch, act, sb, nullptr, 0);
+            add_sb(gacc, sb);
+            return;
+        }
+    }
     const int kb0 = c.kp * kKS;
     const int nsb = min(kKS, T.nb - kb0);
-    if (lane >= rows) return;
     const int row = c.g * 32 + lane;
-    const uint32_t act = stage + Stage<NC>::kActOff + j0 * (kKS * kActSBBytes);
 #pragma unroll
     for (int i = 0; i < kKS; ++i) {
         if (i < nsb) {
@@ -329,11 +362,7 @@ __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCurs
 #pragma unroll
             for (int j = 0; j < NCW; ++j) sb[j] = 0ull;
             sb_dot<NCW, DUMP>(stage + i * kBoxBytes + lane * kPitch, act + i * kActSBBytes, sb, dS, dcs);
-#pragma unroll
-            for (int j = 0; j < NCW; ++j) {
-                const float2 v = f2_unpack(sb[j]);
-                acc.add(j, v.x + v.y);
-            }
+            add_sb(acc, sb);
         }
     }
 }
@@ -350,6 +379,46 @@ __device__ __forceinline__ void store_out(const GemvParams &P, const TaskDesc &T
     }
 }
 
+// Output of a fused row (kernels/mmvq.cu:309-338): the main result plus its
+// bias, combined with the gate result plus its bias.  SWIGLU: times
+// silu(g) = g / (1 + e^-g); GEGLU: times the tanh approximation of gelu(g);
+// SWIGLU_OAI: the clamped variant (alpha 1.702, limit 7) with the roles of
+// the reference's call (gate first); MUL: times g.
+__device__ __forceinline__ float glu_out(int op, float v, float g) {
+    switch (op) {
+        case kGluSwiglu:
+            return v * (g / (1.0f + expf(-g)));
+        case kGluGeglu:
+            return v * (0.5f * g * (1.0f + tanhf(0.79788456080286535588f * g * (1.0f + 0.044715f * g * g))));
+        case kGluSwigluOai: {
+            const float a = fminf(g, 7.0f);
+            const float b = fmaxf(fminf(v, 7.0f), -7.0f);
+            return a / (1.0f + expf(-a * 1.702f)) * (1.0f + b);
+        }
+        case kGluMul:
+            return v * g;
+        default:
+            return v;
+    }
+}
+
+// Final value of output (row, column j): biases and the gate epilogue applied
+// (launches with a fused task only; the plain kernel stores v as it is).
+template <bool GATED>
+__device__ __forceinline__ void store_final(const GemvParams &P, const TaskDesc &T, int j, int row, float v,
+                                            float g) {
+    if constexpr (!GATED) {
+        store_out(P, T, j, row, v);
+        return;
+    }
+    if (T.x_bias != nullptr) v += T.x_bias[j * T.bias_col_stride + row];
+    if (T.has_gate) {
+        if (T.gate_bias != nullptr) g += T.gate_bias[j * T.bias_col_stride + row];
+        v = glu_out(T.glu_op, v, g);
+    }
+    store_out(P, T, j, row, v);
+}
+
 // Finish a row group this warp worked on: write it out directly if the
 // worker covered all of its atoms, otherwise deposit the partial sums and let
 // the last of the contributing warps add them up (always in worker order, so
@@ -358,16 +427,20 @@ __device__ __forceinline__ void store_out(const GemvParams &P, const TaskDesc &T
 // belong to this CTA count arrivals in shared memory under block-scope
 // ordering; otherwise a device-scope acquire-release counter in the workspace
 // is used.
-template <int NCW, int NC, bool DUMP>
+template <int NCW, int NC, int MODE>
 __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCursor &cur, const RowAcc<NCW> &acc,
-                                            int64_t worker, int64_t a0, int64_t a1, int lane, int j0,
-                                            int64_t cta_w0, int64_t cta_w1, int *cta_cnt) {
+                                            const RowAcc<NCW> &gacc, int64_t worker, int64_t a0, int64_t a1,
+                                            int lane, int j0, int64_t cta_w0, int64_t cta_w1, int *cta_cnt) {
     constexpr int kSplit = split_for(NC);
+    constexpr bool DUMP = MODE == kModeDump;
+    constexpr bool GATED = MODE == kModeGated;
     const TaskDesc &T = P.task[cur.t];
-    float v[NCW];
+    const bool gated = GATED && T.has_gate;
+    float v[NCW], gv[NCW];
 #pragma unroll
     for (int j = 0; j < NCW; ++j) {
         v[j] = acc.value(j);
+        gv[j] = GATED ? gacc.value(j) : 0.0f;
     }
     const int64_t sg = T.atom_base + static_cast<int64_t>(cur.g) * T.apr;
     const int64_t eg = sg + T.apr;
@@ -376,14 +449,21 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
     if (sg >= a0 && eg <= a1) {
         if (!DUMP && valid) {
 #pragma unroll
-            for (int j = 0; j < NCW; ++j) store_out(P, T, j0 + j, row, v[j]);
+            for (int j = 0; j < NCW; ++j) store_final<GATED>(P, T, j0 + j, row, v[j], gv[j]);
         }
         return;
     }
+    // Partial slot: [pcols][32] floats, the main sums of the NC columns and,
+    // for a gated task, the gate sums after them.
     const int slot = (a0 > sg) ? 0 : 1;  // 0: group began before this worker, 1: it covers the start
-    float *mine = P.partials + ((worker * 2 + slot) * NC + j0) * 32;
+    constexpr int kPC = GATED ? 2 * NC : NC;  // floats per partial slot and lane (the host sizes pcols alike)
+    float *mine = P.partials + ((worker * 2 + slot) * kPC + j0) * 32;
 #pragma unroll
     for (int j = 0; j < NCW; ++j) mine[j * 32 + lane] = v[j];
+    if (gated) {
+#pragma unroll
+        for (int j = 0; j < NCW; ++j) mine[(NC + j) * 32 + lane] = gv[j];
+    }
     const int64_t w1 = worker_of(P, sg), w2 = worker_of(P, eg - 1);
     const int last = kSplit * static_cast<int>(w2 - w1 + 1) - 1;
     const bool local = P.packed && w1 >= cta_w0 && w2 <= cta_w1;
@@ -402,17 +482,21 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
         if (old != last) return;
         __syncwarp();
     }
-    float tot[NC];
+    float tot[NC], gtot[NC];
 #pragma unroll
-    for (int j = 0; j < NC; ++j) tot[j] = 0.0f;
+    for (int j = 0; j < NC; ++j) tot[j] = gtot[j] = 0.0f;
     for (int64_t w = w1; w <= w2; ++w) {
-        const float *src = P.partials + ((w * 2 + (w == w1 ? 1 : 0)) * NC) * 32;
+        const float *src = P.partials + ((w * 2 + (w == w1 ? 1 : 0)) * kPC) * 32;
 #pragma unroll
         for (int j = 0; j < NC; ++j) tot[j] += ldcg_f32(src + j * 32 + lane);
+        if (gated) {
+#pragma unroll
+            for (int j = 0; j < NC; ++j) gtot[j] += ldcg_f32(src + (NC + j) * 32 + lane);
+        }
     }
     if (!DUMP && valid) {
 #pragma unroll
-        for (int j = 0; j < NC; ++j) store_out(P, T, j, row, tot[j]);
+        for (int j = 0; j < NC; ++j) store_final<GATED>(P, T, j, row, tot[j], gtot[j]);
     }
     if (lane == 0) {
         if (local)
@@ -434,7 +518,7 @@ struct WorkerPipe {
 // Issue the weight copies of the first kStages atoms (they do not depend on
 // any earlier grid: the weights are read-only).
 // (A column-split partner only follows the cursors: issue == false.)
-template <int NC>
+template <int NC, bool GATED>
 __device__ __forceinline__ void worker_prologue(const GemvParams &P, WorkerPipe &W, int lane,
                                                 const uint32_t (&bar)[kStages], bool issue) {
     constexpr int kSB = Stage<NC>::kBytes;
@@ -443,7 +527,7 @@ __device__ __forceinline__ void worker_prologue(const GemvParams &P, WorkerPipe 
     for (int s = 0; s < kStages; ++s) {
         W.pro[s] = W.icur;
         if (s < W.n) {
-            if (issue) issue_weights<NC>(P, W.icur, W.ring + s * kSB, bar[s], lane);
+            if (issue) issue_weights<NC, GATED>(P, W.icur, W.ring + s * kSB, bar[s], lane);
             advance(P, W.icur);
         }
     }
@@ -455,7 +539,7 @@ __device__ __forceinline__ void worker_prologue(const GemvParams &P, WorkerPipe 
 // a stage only after both warps have released it (empty barrier, two
 // arrivals).  Returns (never exits the kernel) so that the CTA-wide epilogues
 // can still run.
-template <int NC, int NCW, bool DUMP>
+template <int NC, int NCW, int MODE>
 __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, int64_t worker, int lane, int j0,
                                             bool issuer, const uint32_t (&full)[kStages],
                                             const uint32_t (&empty)[kStages], int64_t cta_w0, int64_t cta_w1,
@@ -468,11 +552,12 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
     if (issuer) {
 #pragma unroll
         for (int s = 0; s < kStages; ++s)
-            if (s < n) issue_acts<NC>(P, W.pro[s], ring + s * kSB, full[s], lane);
+            if (s < n) issue_acts<NC, MODE == kModeGated>(P, W.pro[s], ring + s * kSB, full[s], lane);
     }
 
-    RowAcc<NCW> acc;
+    RowAcc<NCW> acc, gacc;  // main and (gated launches) gate sums of the open row group
     acc.clear();
+    if constexpr (MODE == kModeGated) gacc.clear();
     AtomCursor cur = W.pro[0];
     int open_t = -1, open_g = -1;
 
@@ -482,15 +567,17 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
         if (cur.t != open_t || cur.g != open_g) {
             if (open_t >= 0) {
                 AtomCursor o{open_t, open_g, 0};
-                flush_group<NCW, NC, DUMP>(P, o, acc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1, cta_cnt);
+                flush_group<NCW, NC, MODE>(P, o, acc, gacc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1,
+                                           cta_cnt);
             }
             open_t = cur.t;
             open_g = cur.g;
             acc.clear();
+            if constexpr (MODE == kModeGated) gacc.clear();
         }
         bool ok = wait_phase(full[s], parity, kWaitLimitNs);
         if (ok) {
-            compute_atom<NCW, NC, DUMP>(P, cur, ring + s * kSB, lane, j0, acc);
+            compute_atom<NCW, NC, MODE>(P, cur, ring + s * kSB, lane, j0, acc, gacc);
             __syncwarp();
             if constexpr (kShared) {
                 if (lane == 0) mbar_arrive(empty[s]);
@@ -499,8 +586,8 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
                 if constexpr (kShared) ok = wait_phase(empty[s], parity, kWaitLimitNs);
                 if (ok) {
                     fence_proxy_async_smem();
-                    issue_weights<NC>(P, icur, ring + s * kSB, full[s], lane);
-                    issue_acts<NC>(P, icur, ring + s * kSB, full[s], lane);
+                    issue_weights<NC, MODE == kModeGated>(P, icur, ring + s * kSB, full[s], lane);
+                    issue_acts<NC, MODE == kModeGated>(P, icur, ring + s * kSB, full[s], lane);
                     advance(P, icur);
                 }
             }
@@ -521,7 +608,8 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
     }
     if (open_t >= 0) {
         AtomCursor o{open_t, open_g, 0};
-        flush_group<NCW, NC, DUMP>(P, o, acc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1, cta_cnt);
+        flush_group<NCW, NC, MODE>(P, o, acc, gacc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1,
+                                   cta_cnt);
     }
 }
 
@@ -627,8 +715,9 @@ __device__ __forceinline__ void gather_epilogue(const GemvParams &P) {
     }
 }
 
-template <int NC, bool DUMP>
+template <int NC, int MODE>
 __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
+    constexpr bool DUMP = MODE == kModeDump;
     constexpr int kR = rings_for(NC);
     constexpr int kSplit = split_for(NC);
     constexpr int kNC0 = (NC + kSplit - 1) / kSplit;  // columns of the issuer warp
@@ -679,7 +768,7 @@ __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_con
     // Weights stream while the previous grid on the stream (the prep launch,
     // or the previous single-launch GEMV) finishes; griddepcontrol.wait
     // returns once it has completed.
-    if (active) worker_prologue<NC>(P, W, lane, full, issuer);
+    if (active) worker_prologue<NC, MODE == kModeGated>(P, W, lane, full, issuer);
     pdl_wait();
     if (P.fused) {
         // Single launch: quantize this CTA's share of the activations, then a
@@ -699,9 +788,9 @@ __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_con
     }
     if (active) {
         if (issuer) {
-            worker_main<NC, kNC0, DUMP>(P, W, worker, lane, 0, true, full, empty, cta_w0, cta_w1, cta_cnt);
+            worker_main<NC, kNC0, MODE>(P, W, worker, lane, 0, true, full, empty, cta_w0, cta_w1, cta_cnt);
         } else if constexpr (kSplit > 1) {
-            worker_main<NC, NC - kNC0, DUMP>(P, W, worker, lane, kNC0, false, full, empty, cta_w0, cta_w1,
+            worker_main<NC, NC - kNC0, MODE>(P, W, worker, lane, kNC0, false, full, empty, cta_w0, cta_w1,
                                              cta_cnt);
         }
     }
@@ -719,35 +808,35 @@ struct DevState {
 };
 DevState g_dev[64];
 
-template <int NC, bool DUMP>
+template <int NC, int MODE>
 cudaError_t set_attrs() {
-    return cudaFuncSetAttribute(k_gemv<NC, DUMP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(NC));
+    return cudaFuncSetAttribute(k_gemv<NC, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(NC));
 }
 
-template <bool DUMP>
+template <int MODE>
 cudaError_t set_attrs_all() {
     cudaError_t e;
-    if ((e = set_attrs<1, DUMP>()) != cudaSuccess) return e;
-    if ((e = set_attrs<2, DUMP>()) != cudaSuccess) return e;
-    if ((e = set_attrs<3, DUMP>()) != cudaSuccess) return e;
-    if ((e = set_attrs<4, DUMP>()) != cudaSuccess) return e;
-    if ((e = set_attrs<5, DUMP>()) != cudaSuccess) return e;
-    if ((e = set_attrs<6, DUMP>()) != cudaSuccess) return e;
-    if ((e = set_attrs<7, DUMP>()) != cudaSuccess) return e;
-    return set_attrs<8, DUMP>();
+    if ((e = set_attrs<1, MODE>()) != cudaSuccess) return e;
+    if ((e = set_attrs<2, MODE>()) != cudaSuccess) return e;
+    if ((e = set_attrs<3, MODE>()) != cudaSuccess) return e;
+    if ((e = set_attrs<4, MODE>()) != cudaSuccess) return e;
+    if ((e = set_attrs<5, MODE>()) != cudaSuccess) return e;
+    if ((e = set_attrs<6, MODE>()) != cudaSuccess) return e;
+    if ((e = set_attrs<7, MODE>()) != cudaSuccess) return e;
+    return set_attrs<8, MODE>();
 }
 
-template <bool DUMP>
+template <int MODE>
 void *gemv_fn(int ncols) {
     switch (ncols) {
-        case 1: return reinterpret_cast<void *>(k_gemv<1, DUMP>);
-        case 2: return reinterpret_cast<void *>(k_gemv<2, DUMP>);
-        case 3: return reinterpret_cast<void *>(k_gemv<3, DUMP>);
-        case 4: return reinterpret_cast<void *>(k_gemv<4, DUMP>);
-        case 5: return reinterpret_cast<void *>(k_gemv<5, DUMP>);
-        case 6: return reinterpret_cast<void *>(k_gemv<6, DUMP>);
-        case 7: return reinterpret_cast<void *>(k_gemv<7, DUMP>);
-        case 8: return reinterpret_cast<void *>(k_gemv<8, DUMP>);
+        case 1: return reinterpret_cast<void *>(k_gemv<1, MODE>);
+        case 2: return reinterpret_cast<void *>(k_gemv<2, MODE>);
+        case 3: return reinterpret_cast<void *>(k_gemv<3, MODE>);
+        case 4: return reinterpret_cast<void *>(k_gemv<4, MODE>);
+        case 5: return reinterpret_cast<void *>(k_gemv<5, MODE>);
+        case 6: return reinterpret_cast<void *>(k_gemv<6, MODE>);
+        case 7: return reinterpret_cast<void *>(k_gemv<7, MODE>);
+        case 8: return reinterpret_cast<void *>(k_gemv<8, MODE>);
         default: return nullptr;
     }
 }
@@ -762,8 +851,9 @@ cudaError_t device_setup(int *num_sms) {
     DevState &st = g_dev[dev];
     if (!st.ready) {
         if ((e = cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-        if ((e = set_attrs_all<false>()) != cudaSuccess) return e;
-        if ((e = set_attrs_all<true>()) != cudaSuccess) return e;
+        if ((e = set_attrs_all<kModePlain>()) != cudaSuccess) return e;
+        if ((e = set_attrs_all<kModeDump>()) != cudaSuccess) return e;
+        if ((e = set_attrs_all<kModeGated>()) != cudaSuccess) return e;
         st.ready = true;
     }
     *num_sms = st.num_sms;
@@ -791,8 +881,10 @@ cudaError_t launch_prep(const PrepParams &p, cudaStream_t s) {
     return cudaLaunchKernelEx(&cfg, k_prep, p);
 }
 
-cudaError_t launch_gemv(const GemvParams &p, int ncols, bool dump, int grid, cudaStream_t s) {
-    void *fn = dump ? gemv_fn<true>(ncols) : gemv_fn<false>(ncols);
+cudaError_t launch_gemv(const GemvParams &p, int ncols, int mode, int grid, cudaStream_t s) {
+    void *fn = mode == kModeDump    ? gemv_fn<kModeDump>(ncols)
+               : mode == kModeGated ? gemv_fn<kModeGated>(ncols)
+                                    : gemv_fn<kModePlain>(ncols);
     if (fn == nullptr) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));

@@ -159,6 +159,58 @@ Q4K_API size_t q4k_batch_workspace_bytes(const q4k_task *tasks, int ntasks, int 
 Q4K_API int q4k_gemv_batch(const q4k_task *tasks, int ntasks, int ncols,
                    void *workspace, size_t workspace_bytes, q4k_stream_t stream);
 
+/* ---- fused epilogue: bias and gated linear unit (kernels/mmvq.cu:182-227, :309-338) */
+
+/* The reference's fused MMVQ (ggml_cuda_mul_mat_vec_q with fusion args,
+ * mmvq.cu:666-762; device part mmvq.cu:182-227 and :309-338) computes, per
+ * output, r = W.x (+ x_bias) and, with a gate matrix, g = Wg.x (+ gate_bias),
+ * and stores op(r, g).  Here both matrices stream in the same launch: an
+ * atom holds one super-block of each for 32 rows, and the epilogue runs on
+ * the final sums.  Ops (the reference's switch at mmvq.cu:318-333):
+ *   SWIGLU      r * g / (1 + exp(-g))
+ *   GEGLU       r * 0.5 g (1 + tanh(sqrt(2/pi) g (1 + 0.044715 g^2)))
+ *   SWIGLU_OAI  a / (1 + exp(-1.702 a)) * (1 + b), a = min(g, 7), b = clamp(r, -7, 7)
+ *   MUL         r * g (the reference's default branch)
+ * Bias element (row, column j) is x_bias[j*stride_col_bias + row]. */
+#define Q4K_GLU_NONE 0       /* no gate (a bias alone is allowed) */
+#define Q4K_GLU_SWIGLU 1
+#define Q4K_GLU_GEGLU 2
+#define Q4K_GLU_SWIGLU_OAI 3
+#define Q4K_GLU_MUL 4
+
+typedef struct q4k_task_ex {
+    q4k_task t;               /* t.W: the main matrix (the reference's vx, the "up" projection) */
+    const void *W_gate;       /* gate matrix (fusion.gate): same shape and row stride as t.W, or NULL */
+    const float *x_bias;      /* added to the main result (fusion.x_bias), or NULL */
+    const float *gate_bias;   /* added to the gate result (fusion.gate_bias), or NULL; needs W_gate */
+    int64_t stride_col_bias;  /* floats between bias columns (0: one column for all) */
+    int glu_op;               /* Q4K_GLU_*: SWIGLU..MUL with W_gate, NONE without */
+} q4k_task_ex;
+
+/* Workspace bytes / batched launch for tasks with optional fused epilogues
+ * (q4k_gemv_batch otherwise).  K = 0 is rejected for a fused task; at most
+ * Q4K_MAX_GATED tasks of one launch may have a gate. */
+#define Q4K_MAX_GATED 4
+Q4K_API size_t q4k_batch_ex_workspace_bytes(const q4k_task_ex *tasks, int ntasks, int ncols);
+Q4K_API int q4k_gemv_batch_ex(const q4k_task_ex *tasks, int ntasks, int ncols, void *workspace,
+                              size_t workspace_bytes, q4k_stream_t stream);
+
+/* One fused GEMV: the reference's fused Q4_K call with q8_1 input
+ * (mul_mat_vec_q_switch_type with fusion, mmvq.cu:479-593) and its fp32-input
+ * form (ggml_cuda_mul_mat_vec_q with fusion, mmvq.cu:666-762).  The bias
+ * column stride is stride_col_dst, as in the reference (mmvq.cu:211).
+ * Workspace: q4k_gemv_fused_workspace_bytes. */
+Q4K_API size_t q4k_gemv_fused_workspace_bytes(int64_t nrows, int64_t K, int ncols);
+Q4K_API int q4k_mul_mat_vec_q8_1_fused(const void *W, const void *W_gate, const void *y_q8_1, float *dst,
+                                       int64_t K, int64_t nrows, int ncols, int64_t stride_row_x,
+                                       int64_t stride_col_y, int64_t stride_col_dst, const float *x_bias,
+                                       const float *gate_bias, int glu_op, void *workspace,
+                                       size_t workspace_bytes, q4k_stream_t stream);
+Q4K_API int q4k_mul_mat_vec_fused(const void *W, const void *W_gate, const float *x, float *dst, int64_t K,
+                                  int64_t nrows, int ncols, int64_t stride_row_x, int64_t stride_col_x,
+                                  int64_t stride_col_dst, const float *x_bias, const float *gate_bias, int glu_op,
+                                  void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+
 /* ---- row-sharded multi-GPU: GEMV fused with the output all-gather ------------- */
 
 /* Row-split across GPUs is the reference's multi-GPU mode (mmvq.cu:764-793,

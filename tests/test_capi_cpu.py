@@ -100,3 +100,22 @@ def test_persistent_path_argument_checks(q4k):
     assert L.q4k_gemv_batch_persistent(t, 1, 1, ctypes.byref(g), None, 0, None) == EINVAL
     assert L.q4k_workspace_init(None, 256, None) == EWORKSPACE
     assert L.q4k_workspace_init(4097, 256, None) == EWORKSPACE  # not 16-byte aligned
+
+
+def test_fused_epilogue_argument_checks(q4k):
+    L = q4k.lib()
+    # glu op without a gate, gate without an op, gate_bias without a gate, bad op: all rejected before the GPU
+    assert L.q4k_mul_mat_vec_fused(256, None, 512, 1024, 256, 32, 1, 1, 256, 32, None, None, 1, None, 0,
+                                   None) == EINVAL
+    assert L.q4k_mul_mat_vec_fused(256, 768, 512, 1024, 256, 32, 1, 1, 256, 32, None, None, 0, None, 0,
+                                   None) == EINVAL
+    assert L.q4k_mul_mat_vec_fused(256, None, 512, 1024, 256, 32, 1, 1, 256, 32, None, 2048, 0, None, 0,
+                                   None) == EINVAL
+    assert L.q4k_mul_mat_vec_fused(256, 768, 512, 1024, 256, 32, 1, 1, 256, 32, None, None, 9, None, 0,
+                                   None) == EINVAL
+    assert L.q4k_mul_mat_vec_fused(256, 776, 512, 1024, 256, 32, 1, 1, 256, 32, None, None, 1, None, 0,
+                                   None) == EINVAL  # gate not 16-byte aligned
+    assert L.q4k_mul_mat_vec_fused(256, 768, 512, 1024, 0, 32, 1, 0, 0, 32, None, None, 1, None, 0,
+                                   None) == EINVAL  # K = 0 with a fused epilogue
+    assert "glu_op" in L.q4k_last_error().decode() or "K > 0" in L.q4k_last_error().decode()
+    assert q4k.lib().q4k_gemv_fused_workspace_bytes(14336, 4096, 1) > q4k.gemv_workspace_bytes(14336, 4096, 1)
