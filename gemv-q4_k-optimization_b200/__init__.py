@@ -69,7 +69,8 @@ class Task(ctypes.Structure):
 class TaskEx(ctypes.Structure):
     """struct q4k_task_ex (include/q4k_gemv.h): a task with an optional fused epilogue."""
     _fields_ = [("t", Task), ("W_gate", ctypes.c_void_p), ("x_bias", ctypes.c_void_p),
-                ("gate_bias", ctypes.c_void_p), ("stride_col_bias", ctypes.c_int64), ("glu_op", ctypes.c_int)]
+                ("gate_bias", ctypes.c_void_p), ("stride_col_bias", ctypes.c_int64), ("glu_op", ctypes.c_int),
+                ("rms_norm", ctypes.c_int), ("norm_eps", ctypes.c_float), ("norm_weight", ctypes.c_void_p)]
 
 
 # Q4K_GLU_* (include/q4k_gemv.h)
@@ -128,6 +129,7 @@ def lib() -> ctypes.CDLL:
                                                   _P, _SZ, _P]),
             "q4k_mul_mat_vec_fused": (None, [_P, _P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _P, _I,
                                              _P, _SZ, _P]),
+            "q4k_rms_norm_quantize_q8_1": (None, [_P, _I64, _I64, _I64, _I, _P, ctypes.c_float, _P, _P]),
             "q4k_ipc_alloc": (None, [_SZ, ctypes.POINTER(ctypes.c_void_p)]),
             "q4k_ipc_free": (None, [_P]),
             "q4k_ipc_handle": (None, [_P, ctypes.c_char_p]),
@@ -362,7 +364,8 @@ def _ptr_or_none(t):
 def make_tasks_ex(items):
     """ctypes q4k_task_ex array from dicts with keys W, x, out and optionally
     W_gate, x_bias, gate_bias (tensors; biases (ncols, nrows) or (nrows,)) and
-    glu ("swiglu", "geglu", "swiglu_oai", "mul" or "none")."""
+    glu ("swiglu", "geglu", "swiglu_oai", "mul" or "none"), and rms_norm (bool), norm_eps,
+    norm_weight (K fp32) for RMSNorm of x inside the quantization launch."""
     arr = (TaskEx * len(items))()
     for i, it in enumerate(items):
         base = make_tasks([it["W"]], [it["x"]], [it["out"]])[0]
@@ -374,7 +377,24 @@ def make_tasks_ex(items):
         b = xb if xb is not None else gb
         arr[i].stride_col_bias = b.stride(0) if (b is not None and b.dim() > 1) else 0
         arr[i].glu_op = GLU_OPS[it.get("glu", "swiglu" if it.get("W_gate") is not None else "none")]
+        if it.get("rms_norm"):
+            arr[i].rms_norm = 1
+            arr[i].norm_eps = float(it.get("norm_eps", 1e-5))
+            arr[i].norm_weight = _ptr_or_none(it.get("norm_weight"))
     return arr
+
+
+def rms_norm_quantize_q8_1(x, norm_weight=None, eps: float = 1e-5, Kpad: int | None = None, stream=None):
+    """ggml q8_1 blocks of RMSNorm(x) * norm_weight: (ncols, Kpad/32*36) uint8 (one launch)."""
+    import torch
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    ncols, K = x.shape
+    Kp = kpad(K) if Kpad is None else Kpad
+    y = torch.zeros((ncols, Kp // QK8_1 * Q8_1_BYTES), dtype=torch.uint8, device=x.device)
+    _check(lib().q4k_rms_norm_quantize_q8_1(x.data_ptr(), K, x.stride(0), Kp, ncols, _ptr_or_none(norm_weight),
+                                            eps, y.data_ptr(), _stream(stream)))
+    return y
 
 
 def batch_ex_workspace_bytes(tasks, ncols: int) -> int:

@@ -77,6 +77,10 @@ struct Job {
     const float *gate_bias = nullptr;
     int64_t bias_col_stride = 0;
     int glu_op = Q4K_GLU_NONE;
+    // RMSNorm of x ahead of the quantizer (fp32 jobs)
+    int norm = 0;
+    float norm_eps = 0.0f;
+    const float *norm_w = nullptr;
 };
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -141,6 +145,11 @@ int validate_job(const Job &j, int ncols, int idx) {
         if (j.bias_col_stride < 0) return fail(Q4K_EINVAL, "task %d: stride_col_bias < 0", idx);
         if (j.K == 0) return fail(Q4K_EINVAL, "task %d: a fused epilogue needs K > 0", idx);
     }
+    if (j.norm) {
+        if (j.kind != kPrepF32) return fail(Q4K_EINVAL, "task %d: RMSNorm needs fp32 activations", idx);
+        if (!(j.norm_eps >= 0.0f) || j.norm_eps > 1.0f)
+            return fail(Q4K_EINVAL, "task %d: norm_eps=%g outside [0, 1]", idx, static_cast<double>(j.norm_eps));
+    }
     if (j.K == 0) return Q4K_OK;  // empty sums: dst is zeroed
     if (!j.W || !j.src) return fail(Q4K_EINVAL, "task %d: null pointer", idx);
     if (!aligned16(j.W)) return fail(Q4K_EINVAL, "task %d: W is not 16-byte aligned", idx);
@@ -177,7 +186,15 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         if (st != Q4K_OK) return st;
     }
     // distinct activations
-    struct Act { const void *src; int64_t K, stride; int kind; size_t off; };
+    struct Act {
+        const void *src;
+        int64_t K, stride;
+        int kind;
+        size_t off;
+        int norm;
+        float eps;
+        const float *w;
+    };
     Act acts[kMaxTasks];
     P.n_act = 0;
     P.act_bytes = 0;
@@ -188,11 +205,12 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         int found = -1;
         for (int a = 0; a < P.n_act; ++a)
             if (acts[a].src == j.src && acts[a].K == j.K && acts[a].stride == j.src_col_stride &&
-                acts[a].kind == j.kind)
+                acts[a].kind == j.kind && acts[a].norm == j.norm &&
+                (!j.norm || (acts[a].eps == j.norm_eps && acts[a].w == j.norm_w)))
                 found = a;
         if (found < 0) {
             found = P.n_act++;
-            acts[found] = {j.src, j.K, j.src_col_stride, j.kind, P.act_bytes};
+            acts[found] = {j.src, j.K, j.src_col_stride, j.kind, P.act_bytes, j.norm, j.norm_eps, j.norm_w};
             P.act_bytes += round_up(static_cast<size_t>(ncols) * (j.K / Q4K_QK_K) * kActSBBytes, kAlign);
         }
         P.act_of_job[i] = found;
@@ -279,6 +297,7 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     }
     // prep jobs: one per distinct activation
     int64_t items = 0;
+    int32_t norm_ctas = 0;
     for (int a = 0; a < P.n_act; ++a) {
         PrepJob &J = P.prep.job[a];
         J.src = acts[a].src;
@@ -293,10 +312,22 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         J.nblk = static_cast<int32_t>(acts[a].K / Q4K_QK8_1);
         J.ncols = ncols;
         J.kind = acts[a].kind;
-        items += static_cast<int64_t>(ncols) * J.nblk;
+        J.norm = acts[a].norm;
+        J.norm_eps = acts[a].eps;
+        J.norm_w = acts[a].w;
+        J.pad_ = 0;
+        if (J.norm) {
+            J.cta_base = norm_ctas;  // one CTA per column; no warp items
+            norm_ctas += ncols;
+        } else {
+            J.cta_base = 0;
+            items += static_cast<int64_t>(ncols) * J.nblk;
+        }
     }
     P.prep.njobs = P.n_act;
     P.prep.nitems = items;
+    P.prep.norm_ctas = norm_ctas;
+    P.prep.pad_ = 0;
     P.prep.zero_ptr = reinterpret_cast<int32_t *>(ws);
     P.prep.zero_count = static_cast<int32_t>((P.layout.counters_off + rgs * 4) / 4);
     return Q4K_OK;
@@ -387,6 +418,9 @@ Job job_of(const q4k_task_ex &t) {
     j.gate_bias = t.gate_bias;
     j.bias_col_stride = t.stride_col_bias;
     j.glu_op = t.glu_op;
+    j.norm = t.rms_norm;
+    j.norm_eps = t.norm_eps;
+    j.norm_w = t.norm_weight;
     return j;
 }
 
@@ -490,6 +524,45 @@ int q4k_quantize_q8_1(const float *x, int64_t K, int64_t stride_col_x, int64_t K
     p.zero_count = 0;
     if ((e = launch_prep(p, reinterpret_cast<cudaStream_t>(stream))) != cudaSuccess)
         return cuda_fail(e, "quantize launch");
+    return Q4K_OK;
+}
+
+int q4k_rms_norm_quantize_q8_1(const float *x, int64_t K, int64_t stride_col_x, int64_t Kpad, int ncols,
+                               const float *norm_weight, float eps, void *y_q8_1, q4k_stream_t stream) {
+    if (ncols < 1 || ncols > Q4K_MAX_NCOLS) return fail(Q4K_EINVAL, "ncols=%d outside 1..8", ncols);
+    if (K < 1 || Kpad < K || Kpad % Q4K_QK8_1 || Kpad > (int64_t(1) << 30))
+        return fail(Q4K_EINVAL, "need 0 < K <= Kpad, Kpad %% 32 == 0 (K=%lld Kpad=%lld)", (long long)K,
+                    (long long)Kpad);
+    if (!x || !y_q8_1) return fail(Q4K_EINVAL, "null pointer");
+    if (ncols > 1 && stride_col_x < K) return fail(Q4K_EINVAL, "stride_col_x < K");
+    if (!(eps >= 0.0f) || eps > 1.0f) return fail(Q4K_EINVAL, "eps=%g outside [0, 1]", static_cast<double>(eps));
+    int num_sms = 0;
+    cudaError_t e = device_setup(&num_sms);
+    if (e != cudaSuccess) return cuda_fail(e, "device setup");
+    PrepParams p{};
+    PrepJob &J = p.job[0];
+    J.src = x;
+    J.act = nullptr;
+    J.q81_out = static_cast<uint8_t *>(y_q8_1);
+    J.dump_T = nullptr;
+    J.src_col_stride = stride_col_x;
+    J.q81_col_stride = Kpad / Q4K_QK8_1;
+    J.item_base = 0;
+    J.K = static_cast<int32_t>(K);
+    J.nblk = static_cast<int32_t>(Kpad / Q4K_QK8_1);
+    J.ncols = ncols;
+    J.kind = kPrepF32;
+    J.norm = 1;
+    J.norm_eps = eps;
+    J.norm_w = norm_weight;
+    J.cta_base = 0;
+    p.njobs = 1;
+    p.nitems = 0;
+    p.norm_ctas = ncols;
+    p.zero_ptr = nullptr;
+    p.zero_count = 0;
+    if ((e = launch_prep(p, reinterpret_cast<cudaStream_t>(stream))) != cudaSuccess)
+        return cuda_fail(e, "rms-norm quantize launch");
     return Q4K_OK;
 }
 

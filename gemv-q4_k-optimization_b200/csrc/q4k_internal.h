@@ -155,6 +155,13 @@ struct PrepJob {
     int32_t nblk;            // q8 blocks per column to produce
     int32_t ncols;
     int32_t kind;
+    // RMSNorm ahead of the quantizer (fp32 jobs): one CTA per column, CTAs
+    // [cta_base, cta_base + ncols) of the launch; the job has no warp items.
+    int32_t norm;
+    float norm_eps;
+    const float *norm_w;     // per-element weight, or nullptr
+    int32_t cta_base;
+    int32_t pad_;
 };
 
 struct PrepParams {
@@ -163,6 +170,8 @@ struct PrepParams {
     int32_t zero_count;      // int32 words to clear at zero_ptr (counters, status)
     int64_t nitems;
     int32_t *zero_ptr;
+    int32_t norm_ctas;       // leading CTAs that normalize whole columns (RMSNorm jobs)
+    int32_t pad_;
 };
 
 // Launchers (q4k_kernels.cu).  Return cudaSuccess or the launch error.

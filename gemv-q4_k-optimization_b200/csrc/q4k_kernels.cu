@@ -57,6 +57,50 @@ __device__ __forceinline__ void write_q8a(uint8_t *act_col, int b, int lane, int
 // ============================================================================
 // prep: quantize / repack activations, clear counters
 // ============================================================================
+// RMSNorm of one column, then its q8a / q8_1 blocks (a whole CTA of 256
+// threads).  y = x / sqrt(mean(x^2) + eps) (* w): the step the reference's
+// decode trace runs before quantize_q8_1 (rms_norm_f32, upstream ggml).  The
+// sum of squares has a fixed order (per-thread fma over i = tid, tid+256, ...;
+// xor butterflies inside and across the 8 warps) and the scale is
+// 1 / sqrtf(mean + eps) with IEEE division and square root, so the CPU
+// checker reproduces it bit for bit (upstream uses rsqrtf).
+__device__ __forceinline__ void prep_norm_column(const PrepJob &J, int col) {
+    __shared__ float red[8];
+    __shared__ float scale_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float *xc = static_cast<const float *>(J.src) + col * J.src_col_stride;
+    float s = 0.0f;
+    for (int i = tid; i < J.K; i += 256) s = fmaf(xc[i], xc[i], s);
+    s = warp_sum_f32(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (warp == 0) {
+        float t = lane < 8 ? red[lane] : 0.0f;
+        t = warp_sum_f32(t);
+        if (lane == 0) scale_s = 1.0f / sqrtf(t / static_cast<float>(J.K) + J.norm_eps);
+    }
+    __syncthreads();
+    const float scale = scale_s;
+    for (int b = warp; b < J.nblk; b += 8) {
+        const int pos = b * 32 + lane;
+        float y = 0.0f;
+        if (pos < J.K) {
+            y = xc[pos] * scale;
+            if (J.norm_w != nullptr) y = y * J.norm_w[pos];
+        }
+        int q;
+        __half dh;
+        quantize_value(y, q, dh);
+        if (J.q81_out != nullptr) {
+            const float sum = warp_sum_f32(y);
+            uint8_t *blk = J.q81_out + (col * J.q81_col_stride + b) * kQ81Bytes;
+            blk[4 + lane] = static_cast<uint8_t>(static_cast<int8_t>(q));
+            if (lane == 0) *reinterpret_cast<__half2 *>(blk) = __halves2half2(dh, __float2half_rn(sum));
+        }
+        if (J.act != nullptr && b * 32 < J.K) write_q8a(J.act + col * J.act_col_stride, b, lane, q, dh, nullptr);
+    }
+}
+
 __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams P) {
     // Let the dependent GEMV grid launch now: it only issues weight copies
     // before its griddepcontrol.wait, which returns after this grid completes.
@@ -69,9 +113,18 @@ __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams
     const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t i = tid; i < P.zero_count; i += nthr) P.zero_ptr[i] = 0;
 
+    if (static_cast<int>(blockIdx.x) < P.norm_ctas) {
+        int j = 0;
+        while (!(P.job[j].norm && static_cast<int>(blockIdx.x) < P.job[j].cta_base + P.job[j].ncols)) ++j;
+        prep_norm_column(P.job[j], static_cast<int>(blockIdx.x) - P.job[j].cta_base);
+        return;
+    }
     const int lane = threadIdx.x & 31;
-    const int64_t wid = tid >> 5, nw = nthr >> 5;
+    // warp items of the other jobs, over the CTAs after the normalizing ones
+    const int64_t ftid = tid - static_cast<int64_t>(P.norm_ctas) * blockDim.x;
+    const int64_t wid = ftid >> 5, nw = (nthr - static_cast<int64_t>(P.norm_ctas) * blockDim.x) >> 5;
     for (int64_t item = wid; item < P.nitems; item += nw) {
+        // (a normalizing job owns no items: its item_base equals the next job's)
         int j = 0;
         while (j + 1 < P.njobs && item >= P.job[j + 1].item_base) ++j;
         const PrepJob &J = P.job[j];
@@ -866,6 +919,7 @@ cudaError_t launch_prep(const PrepParams &p, cudaStream_t s) {
     if (zb > blocks) blocks = zb;
     if (blocks < 1) blocks = 1;
     if (blocks > 4096) blocks = 4096;
+    blocks += p.norm_ctas;  // the normalizing CTAs come first
     // Programmatic dependent of whatever precedes it on the stream: it can be
     // resident before the previous GEMV ends and waits for it on the device.
     cudaLaunchConfig_t cfg = {};

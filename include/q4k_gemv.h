@@ -185,7 +185,21 @@ typedef struct q4k_task_ex {
     const float *gate_bias;   /* added to the gate result (fusion.gate_bias), or NULL; needs W_gate */
     int64_t stride_col_bias;  /* floats between bias columns (0: one column for all) */
     int glu_op;               /* Q4K_GLU_*: SWIGLU..MUL with W_gate, NONE without */
+    int rms_norm;             /* 1: quantize RMSNorm(x) * norm_weight instead of x (see below) */
+    float norm_eps;           /* RMSNorm epsilon */
+    const float *norm_weight; /* K per-element weights, or NULL (no multiply) */
 } q4k_task_ex;
+
+/* ---- RMSNorm fused into the quantization launch ---------------------------------
+ * The reference's decode trace runs rms_norm_f32 -> quantize_q8_1 ->
+ * mul_mat_vec_q (upstream ggml; no source in the reference).  With
+ * rms_norm = 1 the quantization launch normalizes each column first:
+ * y = x / sqrt(mean(x^2) + eps) * w, one CTA per column, the sum of squares
+ * in a fixed order (per-thread fma over a stride of 256, xor butterflies) and
+ * scale = 1 / sqrtf(mean + eps) (upstream: rsqrtf, within 2 ulp).  Tasks that
+ * name the same x with the same norm share one normalized quantization. */
+Q4K_API int q4k_rms_norm_quantize_q8_1(const float *x, int64_t K, int64_t stride_col_x, int64_t Kpad, int ncols,
+                                       const float *norm_weight, float eps, void *y_q8_1, q4k_stream_t stream);
 
 /* Workspace bytes / batched launch for tasks with optional fused epilogues
  * (q4k_gemv_batch otherwise).  K = 0 is rejected for a fused task; at most

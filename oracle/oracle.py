@@ -57,6 +57,9 @@ def lib() -> ctypes.CDLL:
         L.or_f2h.argtypes = [ctypes.c_float]
         L.or_f2h.restype = ctypes.c_uint16
         L.or_quantize_q8_1.argtypes = [_c_p, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p]
+        L.or_rmsnorm.argtypes = [_c_p, _c_i64, _c_i64, ctypes.c_int, _c_p, ctypes.c_float, _c_p]
+        L.or_rmsnorm_scale.argtypes = [_c_p, _c_i64, ctypes.c_float]
+        L.or_rmsnorm_scale.restype = ctypes.c_float
         L.or_subblock_sums_sb.argtypes = [_c_p, _c_p, _c_p, _c_p]
         L.or_gemv_q4k_q8_1.argtypes = [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, ctypes.c_int,
                                        _c_p, _c_i64, ctypes.c_int]
@@ -109,6 +112,18 @@ def quantize_q8_1(x: np.ndarray, Kpad: int | None = None) -> np.ndarray:
     out = np.zeros((ncols, Kp // QK8_1 * Q81_BYTES), dtype=np.uint8)
     lib().or_quantize_q8_1(_ptr(x), K, K, Kp, ncols, _ptr(out))
     return out
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray | None = None, eps: float = 1e-5) -> np.ndarray:
+    """(ncols, K) float32 -> RMSNorm(x) * w in the library's reduction order (bit-exact)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if x.ndim == 1:
+        x = x[None, :]
+    ncols, K = x.shape
+    y = np.empty_like(x)
+    wa = None if w is None else np.ascontiguousarray(w, dtype=np.float32)
+    lib().or_rmsnorm(_ptr(x), K, K, ncols, None if wa is None else _ptr(wa), eps, _ptr(y))
+    return y
 
 
 def gemv_q8_1(W: np.ndarray, K: int, yq: np.ndarray, nthreads: int = 0) -> np.ndarray:

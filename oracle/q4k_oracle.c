@@ -137,6 +137,62 @@ void or_quantize_q8_1(const float *x, int64_t K, int64_t stride_col_x,
 }
 
 /* ------------------------------------------------------------------------ */
+/* RMSNorm ahead of the quantizer                                            */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * y = x / sqrt(mean(x^2) + eps) (* w), the step before quantize_q8_1 in the
+ * reference's decode trace (rms_norm_f32 -> quantize_q8_1 -> mul_mat_vec_q;
+ * upstream ggml, not vendored: restated from the published definition).
+ * The sum of squares is formed in the library's fixed order so the scale is
+ * bit-identical: 256 partial sums s_t = fma(x_i, x_i, s_t) over
+ * i = t, t+256, ... (ascending), an xor-butterfly sum (offsets 16..1) inside
+ * each group of 32, then the same butterfly over the 8 group sums (lanes 8..31
+ * adding zeros).  scale = 1 / sqrtf(sum / K + eps) (IEEE division and square
+ * root), y_i = (x_i * scale) * w_i.
+ */
+static void butterfly32(float *v) {
+    for (int off = 16; off > 0; off >>= 1) {
+        float n[32];
+        for (int l = 0; l < 32; ++l) n[l] = v[l] + v[l ^ off];
+        memcpy(v, n, sizeof(n));
+    }
+}
+
+float or_rmsnorm_scale(const float *x, int64_t K, float eps) {
+    float part[256];
+    for (int t = 0; t < 256; ++t) {
+        float s = 0.0f;
+        for (int64_t i = t; i < K; i += 256) s = fmaf(x[i], x[i], s);
+        part[t] = s;
+    }
+    float lanes[32];
+    float warp_tot[8];
+    for (int w = 0; w < 8; ++w) {
+        memcpy(lanes, part + 32 * w, sizeof(lanes));
+        butterfly32(lanes);
+        warp_tot[w] = lanes[0];
+    }
+    for (int l = 0; l < 32; ++l) lanes[l] = l < 8 ? warp_tot[l] : 0.0f;
+    butterfly32(lanes);
+    const float mean = lanes[0] / (float)K;
+    return 1.0f / sqrtf(mean + eps);
+}
+
+void or_rmsnorm(const float *x, int64_t K, int64_t stride_col_x, int ncols, const float *w, float eps,
+                float *y) {
+    for (int j = 0; j < ncols; ++j) {
+        const float *xc = x + (int64_t)j * stride_col_x;
+        float *yc = y + (int64_t)j * K;
+        const float scale = or_rmsnorm_scale(xc, K, eps);
+        for (int64_t i = 0; i < K; ++i) {
+            const float v = xc[i] * scale;
+            yc[i] = w ? v * w[i] : v;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Q4_K super-block decode and integer sub-block sums                        */
 /* ------------------------------------------------------------------------ */
 

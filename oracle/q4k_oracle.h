@@ -71,6 +71,11 @@ void or_subblock_sums(const uint8_t *W, int64_t nrows, int64_t K,
 /* Number of OpenMP threads the oracle would use with nthreads <= 0. */
 int or_max_threads(void);
 
+/* RMSNorm in the library's reduction order: y (ncols x K, dense) from x. */
+float or_rmsnorm_scale(const float *x, int64_t K, float eps);
+void or_rmsnorm(const float *x, int64_t K, int64_t stride_col_x, int ncols, const float *w, float eps,
+                float *y);
+
 #ifdef __cplusplus
 }
 #endif

@@ -119,3 +119,12 @@ def test_fused_epilogue_argument_checks(q4k):
                                    None) == EINVAL  # K = 0 with a fused epilogue
     assert "glu_op" in L.q4k_last_error().decode() or "K > 0" in L.q4k_last_error().decode()
     assert q4k.lib().q4k_gemv_fused_workspace_bytes(14336, 4096, 1) > q4k.gemv_workspace_bytes(14336, 4096, 1)
+
+
+def test_rms_norm_quantize_argument_checks(q4k):
+    L = q4k.lib()
+    assert L.q4k_rms_norm_quantize_q8_1(256, 0, 0, 32, 1, None, 1e-5, 512, None) == EINVAL       # K = 0
+    assert L.q4k_rms_norm_quantize_q8_1(256, 100, 100, 96, 1, None, 1e-5, 512, None) == EINVAL   # Kpad < K
+    assert L.q4k_rms_norm_quantize_q8_1(256, 64, 64, 64, 9, None, 1e-5, 512, None) == EINVAL     # ncols
+    assert L.q4k_rms_norm_quantize_q8_1(256, 64, 64, 64, 1, None, -1.0, 512, None) == EINVAL     # eps
+    assert L.q4k_rms_norm_quantize_q8_1(None, 64, 64, 64, 1, None, 1e-5, 512, None) == EINVAL    # null x
