@@ -175,11 +175,12 @@ struct Plan {
     int n_act = 0;
     bool any_work = false;
     bool any_fused = false;  // a task with a gate or a bias: the epilogue kernel variant
+    bool r2 = false;         // the two-rows-per-lane variant (64-row groups)
 };
 
 // Build the schedule (no device memory touched).  ws may be null (sizing).
 int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, Plan &P,
-              int32_t *dump_T = nullptr) {
+              int32_t *dump_T = nullptr, bool dump = false) {
     if (njobs < 1 || njobs > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..%d", njobs, kMaxTasks);
     for (int i = 0; i < njobs; ++i) {
         int st = validate_job(jobs[i], ncols, i);
@@ -215,19 +216,25 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         }
         P.act_of_job[i] = found;
     }
+    // kernel variant: the epilogue one for a gate or bias; else, from kR2Min
+    // columns on, 64-row groups with two rows per lane
+    P.any_fused = false;
+    for (int i = 0; i < njobs; ++i)
+        if (P.act_of_job[i] >= 0 && (jobs[i].gate || jobs[i].x_bias)) P.any_fused = true;
+    P.r2 = !dump && !P.any_fused && ncols >= kR2Min && split_for(ncols) == 1;
+    const int64_t group_rows = P.r2 ? 64 : 32;
     // row groups and atoms
     int64_t atoms = 0, rgs = 0;
     int nt = 0;
     int ngated = 0;
-    P.any_fused = false;
     for (int i = 0; i < njobs; ++i) {
         const Job &j = jobs[i];
         if (P.act_of_job[i] < 0) continue;
-        const int64_t groups = (j.nrows + 31) / 32;
+        const int64_t groups = (j.nrows + group_rows - 1) / group_rows;
         const int64_t nb = j.K / Q4K_QK_K;
-        // a gated atom is one super-block position of both matrices
-        const int64_t apr = j.gate ? nb : (nb + kKS - 1) / kKS;
-        if (j.gate || j.x_bias) P.any_fused = true;
+        // a gated or two-row atom is one super-block position (of both
+        // matrices / of 64 rows); a plain one kKS super-blocks of 32 rows
+        const int64_t apr = (j.gate || P.r2) ? nb : (nb + kKS - 1) / kKS;
         TaskDesc &T = P.gemv.task[nt++];
         T.W = static_cast<const uint8_t *>(j.W);
         T.dst = j.dst;
@@ -268,8 +275,8 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.gemv.nworkers = static_cast<int32_t>(nw);
     P.gemv.packed = atoms >= 4 * max_workers ? 1 : 0;
     P.gemv.pad0_ = 0;
-    // the epilogue kernel variant (any gate or bias) keeps gate partials too
-    P.gemv.pcols = P.any_fused ? 2 * ncols : ncols;
+    // the epilogue variant keeps gate partials, the two-row one the second row's
+    P.gemv.pcols = (P.any_fused || P.r2) ? 2 * ncols : ncols;
     P.gemv.pad1_ = 0;
     P.layout = make_layout(rgs, P.gemv.pcols, P.act_bytes, 2 * nw);
     P.gemv.fused = 0;
@@ -365,12 +372,13 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
         bool fused = false) {
     Plan P;
     // Arguments are validated before the device is touched.
-    int st = make_plan(jobs, njobs, ncols, nullptr, kFallbackSMs, P);
+    const bool dump = dump_S != nullptr;
+    int st = make_plan(jobs, njobs, ncols, nullptr, kFallbackSMs, P, nullptr, dump);
     if (st != Q4K_OK) return st;
     int num_sms = 0;
     cudaError_t e = device_setup(&num_sms);
     if (e != cudaSuccess) return cuda_fail(e, "device setup");
-    st = make_plan(jobs, njobs, ncols, nullptr, num_sms, P);
+    st = make_plan(jobs, njobs, ncols, nullptr, num_sms, P, nullptr, dump);
     if (st != Q4K_OK) return st;
     st = zero_outputs(jobs, njobs, ncols, s);
     if (st != Q4K_OK) return st;
@@ -382,7 +390,7 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     if (!aligned16(workspace)) return fail(Q4K_EWORKSPACE, "workspace is not 16-byte aligned");
     if (ws_bytes < P.layout.total)
         return fail(Q4K_EWORKSPACE, "workspace of %zu bytes < %zu required", ws_bytes, P.layout.total);
-    st = make_plan(jobs, njobs, ncols, static_cast<uint8_t *>(workspace), num_sms, P, dump_T);
+    st = make_plan(jobs, njobs, ncols, static_cast<uint8_t *>(workspace), num_sms, P, dump_T, dump);
     if (st != Q4K_OK) return st;
     P.gemv.dump_S = dump_S;
     P.gemv.gworld = 1;
@@ -405,7 +413,7 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     } else if ((e = launch_prep(P.prep, s)) != cudaSuccess) {
         return cuda_fail(e, "prep launch");
     }
-    const int mode = dump_S != nullptr ? kModeDump : P.any_fused ? kModeGated : kModePlain;
+    const int mode = dump ? kModeDump : P.any_fused ? kModeGated : P.r2 ? kModeR2 : kModePlain;
     if ((e = launch_gemv(P.gemv, ncols, mode, num_sms, s)) != cudaSuccess)
         return cuda_fail(e, "gemv launch");
     return Q4K_OK;

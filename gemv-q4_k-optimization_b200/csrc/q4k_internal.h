@@ -177,7 +177,13 @@ struct PrepParams {
 // Launchers (q4k_kernels.cu).  Return cudaSuccess or the launch error.
 cudaError_t launch_prep(const PrepParams &p, cudaStream_t s);
 // Kernel variants: plain, debug dump of the sub-block sums, fused epilogues.
-enum GemvMode : int { kModePlain = 0, kModeDump = 1, kModeGated = 2 };
+// kModeR2: plain tasks at ncols >= kR2Min, 64-row groups with two rows per
+// lane (one activation load serves both rows).
+enum GemvMode : int { kModePlain = 0, kModeDump = 1, kModeGated = 2, kModeR2 = 3 };
+#ifndef Q4K_R2_MIN
+#define Q4K_R2_MIN 3
+#endif
+constexpr int kR2Min = Q4K_R2_MIN;
 cudaError_t launch_gemv(const GemvParams &p, int ncols, int mode, int grid, cudaStream_t s);
 // Per-device setup (SM count, shared-memory opt-in); thread-safe, idempotent.
 cudaError_t device_setup(int *num_sms);

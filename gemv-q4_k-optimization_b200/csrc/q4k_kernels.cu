@@ -105,12 +105,39 @@ __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams
     // Let the dependent GEMV grid launch now: it only issues weight copies
     // before its griddepcontrol.wait, which returns after this grid completes.
     pdl_launch_dependents();
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    // While the previous grid runs, ask L2 for this CTA's activation lines.  A
+    // prefetch binds no value: if the previous grid writes x, the reads after
+    // the wait still see its stores (L2 is the point of coherence).
+    if (static_cast<int>(blockIdx.x) < P.norm_ctas) {
+        int j = 0;
+        while (!(P.job[j].norm && static_cast<int>(blockIdx.x) < P.job[j].cta_base + P.job[j].ncols)) ++j;
+        const PrepJob &J = P.job[j];
+        const float *xc = static_cast<const float *>(J.src) +
+                          (static_cast<int>(blockIdx.x) - J.cta_base) * J.src_col_stride;
+        for (int i = static_cast<int>(threadIdx.x) * 32; i < J.K; i += 256 * 32) prefetch_l2(xc + i);
+    } else if ((threadIdx.x & 31) == 0) {
+        const int64_t w0 = (tid - static_cast<int64_t>(P.norm_ctas) * blockDim.x) >> 5;
+        const int64_t nw0 = (nthr - static_cast<int64_t>(P.norm_ctas) * blockDim.x) >> 5;
+        for (int64_t item = w0; item < P.nitems; item += nw0) {
+            int j = 0;
+            while (j + 1 < P.njobs && item >= P.job[j + 1].item_base) ++j;
+            const PrepJob &J = P.job[j];
+            const int64_t local = item - J.item_base;
+            const int col = static_cast<int>(local / J.nblk);
+            const int b = static_cast<int>(local - static_cast<int64_t>(col) * J.nblk);
+            if (J.kind == kPrepF32) {
+                if (b * 32 < J.K) prefetch_l2(static_cast<const float *>(J.src) + col * J.src_col_stride + b * 32);
+            } else {
+                prefetch_l2(static_cast<const uint8_t *>(J.src) + (col * J.src_col_stride + b) * kQ81Bytes);
+            }
+        }
+    }
     // This grid may itself be a programmatic dependent of the previous GEMV
     // launch (which shares the workspace): wait for it before writing.
     pdl_wait();
 
-    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t i = tid; i < P.zero_count; i += nthr) P.zero_ptr[i] = 0;
 
     if (static_cast<int>(blockIdx.x) < P.norm_ctas) {
@@ -217,12 +244,18 @@ static_assert(sizeof(GemvParams) <= 32764, "kernel parameters exceed the 32 KB l
 // Announce the atom's bytes and copy its weights: one tensor-map box (32 rows
 // x 144 bytes) per super-block, issued by lane 0.  Rows past the matrix end
 // are zero-filled by the copy and still counted in its byte total.
-template <int NC, bool GATED>
+template <int NC, int MODE>
 __device__ __forceinline__ void issue_weights(const GemvParams &P, const AtomCursor &c, uint32_t stage,
                                               uint32_t bar, int lane) {
+    constexpr bool GATED = MODE == kModeGated;
     const TaskDesc &T = P.task[c.t];
     if (lane == 0) {
-        if (GATED && T.has_gate) {
+        if (MODE == kModeR2) {
+            // one super-block of 64 rows: two boxes of 32 rows
+            mbar_expect_tx(bar, static_cast<uint32_t>(2 * kBoxBytes + NC * kActSBBytes));
+            tma_load_2d(stage, &P.tmap[c.t], c.kp * 36, c.g * 64, bar);
+            tma_load_2d(stage + kBoxBytes, &P.tmap[c.t], c.kp * 36, c.g * 64 + 32, bar);
+        } else if (GATED && T.has_gate) {
             // one super-block position of both matrices: box 0 main, box 1 gate
             static_assert(kKS >= 2, "a gated atom needs two boxes per stage");
             mbar_expect_tx(bar, static_cast<uint32_t>(2 * kBoxBytes + NC * kActSBBytes));
@@ -242,11 +275,11 @@ __device__ __forceinline__ void issue_weights(const GemvParams &P, const AtomCur
 
 // Copy the atom's activation records (one copy per column, lanes 0..NC-1).
 // Only after griddepcontrol.wait: the prep kernel writes them.
-template <int NC, bool GATED>
+template <int NC, int MODE>
 __device__ __forceinline__ void issue_acts(const GemvParams &P, const AtomCursor &c, uint32_t stage,
                                            uint32_t bar, int lane) {
     const TaskDesc &T = P.task[c.t];
-    const bool gated = GATED && T.has_gate;
+    const bool gated = MODE == kModeR2 || (MODE == kModeGated && T.has_gate);  // one record per atom
     const int kb0 = gated ? c.kp : c.kp * kKS;
     const int nsb = gated ? 1 : min(kKS, T.nb - kb0);
     if (lane < NC) {
@@ -368,6 +401,97 @@ struct RowAcc {
     __device__ __forceinline__ float value(int j) const { return sum[j] - comp[j]; }
 };
 
+// Per-row constants of one super-block: d, dmin and the 6-bit scales/mins.
+struct SbHead {
+    float d, dmin, nd23, pm23;
+    uint32_t sc03, m03, sc47, m47;
+};
+__device__ __forceinline__ SbHead sb_head(uint32_t p) {
+    const uint4 h = lds128(p);
+    const float2 dm = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
+    SbHead H;
+    H.d = dm.x;
+    H.dmin = dm.y;
+    H.sc03 = h.y & 0x3F3F3F3Fu;
+    H.m03 = h.z & 0x3F3F3F3Fu;
+    H.sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    H.m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    H.nd23 = -8388608.0f * H.d;
+    H.pm23 = 8388608.0f * H.dmin;
+    return H;
+}
+
+// Sub-block pair c of one super-block for two rows (weights at pA, pB) that
+// share every activation load: the arithmetic of pair_dot, once per row.
+template <int NC>
+__device__ __forceinline__ void pair_dot2(uint32_t pA, uint32_t pB, uint32_t act, int c, const SbHead &A,
+                                          const SbHead &B, uint64_t (&accA)[NC], uint64_t (&accB)[NC]) {
+    const int b0 = (c & 1) * 2;
+    const uint32_t scA = c < 2 ? A.sc03 : A.sc47, mA = c < 2 ? A.m03 : A.m47;
+    const uint32_t scB = c < 2 ? B.sc03 : B.sc47, mB = c < 2 ? B.m03 : B.m47;
+    const uint64_t dscA = f2_pack(fmaf(byte_magic(scA, b0), A.d, A.nd23), fmaf(byte_magic(scA, b0 + 1), A.d, A.nd23));
+    const uint64_t ndmA =
+        f2_pack(fmaf(byte_magic(mA, b0), -A.dmin, A.pm23), fmaf(byte_magic(mA, b0 + 1), -A.dmin, A.pm23));
+    const uint64_t dscB = f2_pack(fmaf(byte_magic(scB, b0), B.d, B.nd23), fmaf(byte_magic(scB, b0 + 1), B.d, B.nd23));
+    const uint64_t ndmB =
+        f2_pack(fmaf(byte_magic(mB, b0), -B.dmin, B.pm23), fmaf(byte_magic(mB, b0 + 1), -B.dmin, B.pm23));
+    uint32_t loA[8], hiA[8], loB[8], hiB[8];
+    {
+        const uint4 wa = lds128(pA + 16 + 32 * c), wb = lds128(pA + 32 + 32 * c);
+        const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            loA[k] = w[k] & 0x0F0F0F0Fu;
+            hiA[k] = w[k] & 0xF0F0F0F0u;
+        }
+    }
+    {
+        const uint4 wa = lds128(pB + 16 + 32 * c), wb = lds128(pB + 32 + 32 * c);
+        const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            loB[k] = w[k] & 0x0F0F0F0Fu;
+            hiB[k] = w[k] & 0xF0F0F0F0u;
+        }
+    }
+    const uint64_t magic2 = f2_pack(-kMagicF, -kMagicF);
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+        const uint32_t aj = act + j * (kKS * kActSBBytes);
+        const uint4 qe0 = lds128(aj + 64 * c);
+        const uint4 qe1 = lds128(aj + 64 * c + 16);
+        const uint4 qo0 = lds128(aj + 64 * c + 32);
+        const uint4 qo1 = lds128(aj + 64 * c + 48);
+        const uint4 meta = lds128(aj + kActMetaOff + 16 * c);
+        const uint32_t qe[8] = {qe0.x, qe0.y, qe0.z, qe0.w, qe1.x, qe1.y, qe1.z, qe1.w};
+        const uint32_t qo[8] = {qo0.x, qo0.y, qo0.z, qo0.w, qo1.x, qo1.y, qo1.z, qo1.w};
+        int seA = kMagicI, soA = kMagicI, seB = kMagicI, soB = kMagicI;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            seA = dp4a_us(loA[k], qe[k], seA);
+            soA = dp4a_us(hiA[k], qo[k], soA);
+            seB = dp4a_us(loB[k], qe[k], seB);
+            soB = dp4a_us(hiB[k], qo[k], soB);
+        }
+        const uint64_t f = f2_pack(__uint_as_float(meta.x), __uint_as_float(meta.y));
+        const uint64_t a = f2_pack(__uint_as_float(meta.z), __uint_as_float(meta.w));
+        const uint64_t gA = f2_mul(f2_add(f2_pack(__int_as_float(seA), __int_as_float(soA)), magic2), f);
+        const uint64_t gB = f2_mul(f2_add(f2_pack(__int_as_float(seB), __int_as_float(soB)), magic2), f);
+        accA[j] = f2_fma(a, ndmA, f2_fma(gA, dscA, accA[j]));
+        accB[j] = f2_fma(a, ndmB, f2_fma(gB, dscB, accB[j]));
+    }
+}
+
+// One super-block of two rows (weights at pA and pB) against NC activation
+// records: sb_dot for both, with the activation loads shared.
+template <int NC>
+__device__ __forceinline__ void sb_dot2(uint32_t pA, uint32_t pB, uint32_t act, uint64_t (&accA)[NC],
+                                        uint64_t (&accB)[NC]) {
+    const SbHead A = sb_head(pA), B = sb_head(pB);
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) pair_dot2<NC>(pA, pB, act, c, A, B, accA, accB);
+}
+
 template <int NCW>
 __device__ __forceinline__ void add_sb(RowAcc<NCW> &acc, const uint64_t (&sb)[NCW]) {
 #pragma unroll
@@ -381,6 +505,18 @@ template <int NCW, int NC, int MODE>
 __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCursor &c, uint32_t stage, int lane,
                                              int j0, RowAcc<NCW> &acc, RowAcc<NCW> &gacc) {
     const TaskDesc &T = P.task[c.t];
+    if constexpr (MODE == kModeR2) {
+        // 64-row group: lane holds rows 64g + lane (box 0) and 64g + 32 + lane
+        // (box 1) of super-block c.kp; rows past the end are zero-filled.
+        uint64_t sbA[NCW], sbB[NCW];
+#pragma unroll
+        for (int j = 0; j < NCW; ++j) sbA[j] = sbB[j] = 0ull;
+        sb_dot2<NCW>(stage + lane * kPitch, stage + kBoxBytes + lane * kPitch, stage + Stage<NC>::kActOff, sbA,
+                     sbB);
+        add_sb(acc, sbA);
+        add_sb(gacc, sbB);
+        return;
+    }
     const int rows = min(32, T.nrows - c.g * 32);
     if (lane >= rows) return;
     constexpr bool DUMP = MODE == kModeDump;
@@ -487,29 +623,37 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
     constexpr int kSplit = split_for(NC);
     constexpr bool DUMP = MODE == kModeDump;
     constexpr bool GATED = MODE == kModeGated;
+    constexpr bool R2 = MODE == kModeR2;
     const TaskDesc &T = P.task[cur.t];
-    const bool gated = GATED && T.has_gate;
+    // second set of sums: the gate (gated task) or row 64g + 32 + lane (two-row launch)
+    const bool gated = R2 || (GATED && T.has_gate);
     float v[NCW], gv[NCW];
 #pragma unroll
     for (int j = 0; j < NCW; ++j) {
         v[j] = acc.value(j);
-        gv[j] = GATED ? gacc.value(j) : 0.0f;
+        gv[j] = (GATED || R2) ? gacc.value(j) : 0.0f;
     }
     const int64_t sg = T.atom_base + static_cast<int64_t>(cur.g) * T.apr;
     const int64_t eg = sg + T.apr;
-    const int row = cur.g * 32 + lane;
+    const int row = cur.g * (R2 ? 64 : 32) + lane;
     const bool valid = row < T.nrows;
+    const bool valid2 = R2 && row + 32 < T.nrows;
     if (sg >= a0 && eg <= a1) {
         if (!DUMP && valid) {
 #pragma unroll
             for (int j = 0; j < NCW; ++j) store_final<GATED>(P, T, j0 + j, row, v[j], gv[j]);
         }
+        if (valid2) {
+#pragma unroll
+            for (int j = 0; j < NCW; ++j) store_out(P, T, j0 + j, row + 32, gv[j]);
+        }
         return;
     }
     // Partial slot: [pcols][32] floats, the main sums of the NC columns and,
-    // for a gated task, the gate sums after them.
+    // for a gated task, the gate sums after them (two-row launch: the second
+    // row's sums).
     const int slot = (a0 > sg) ? 0 : 1;  // 0: group began before this worker, 1: it covers the start
-    constexpr int kPC = GATED ? 2 * NC : NC;  // floats per partial slot and lane (the host sizes pcols alike)
+    constexpr int kPC = (GATED || R2) ? 2 * NC : NC;  // floats per partial slot and lane (host pcols alike)
     float *mine = P.partials + ((worker * 2 + slot) * kPC + j0) * 32;
 #pragma unroll
     for (int j = 0; j < NCW; ++j) mine[j * 32 + lane] = v[j];
@@ -551,6 +695,10 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
 #pragma unroll
         for (int j = 0; j < NC; ++j) store_final<GATED>(P, T, j, row, tot[j], gtot[j]);
     }
+    if (valid2) {
+#pragma unroll
+        for (int j = 0; j < NC; ++j) store_out(P, T, j, row + 32, gtot[j]);
+    }
     if (lane == 0) {
         if (local)
             cta_cnt[w1 - cta_w0] = 0;
@@ -571,7 +719,7 @@ struct WorkerPipe {
 // Issue the weight copies of the first kStages atoms (they do not depend on
 // any earlier grid: the weights are read-only).
 // (A column-split partner only follows the cursors: issue == false.)
-template <int NC, bool GATED>
+template <int NC, int MODE>
 __device__ __forceinline__ void worker_prologue(const GemvParams &P, WorkerPipe &W, int lane,
                                                 const uint32_t (&bar)[kStages], bool issue) {
     constexpr int kSB = Stage<NC>::kBytes;
@@ -580,7 +728,7 @@ __device__ __forceinline__ void worker_prologue(const GemvParams &P, WorkerPipe 
     for (int s = 0; s < kStages; ++s) {
         W.pro[s] = W.icur;
         if (s < W.n) {
-            if (issue) issue_weights<NC, GATED>(P, W.icur, W.ring + s * kSB, bar[s], lane);
+            if (issue) issue_weights<NC, MODE>(P, W.icur, W.ring + s * kSB, bar[s], lane);
             advance(P, W.icur);
         }
     }
@@ -605,12 +753,14 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
     if (issuer) {
 #pragma unroll
         for (int s = 0; s < kStages; ++s)
-            if (s < n) issue_acts<NC, MODE == kModeGated>(P, W.pro[s], ring + s * kSB, full[s], lane);
+            if (s < n) issue_acts<NC, MODE>(P, W.pro[s], ring + s * kSB, full[s], lane);
     }
 
-    RowAcc<NCW> acc, gacc;  // main and (gated launches) gate sums of the open row group
+    // Sums of the open row group: main and gate (gated launches), or rows
+    // 64g + lane and 64g + 32 + lane (two-row launches).
+    RowAcc<NCW> acc, gacc;
     acc.clear();
-    if constexpr (MODE == kModeGated) gacc.clear();
+    if constexpr (MODE == kModeGated || MODE == kModeR2) gacc.clear();
     AtomCursor cur = W.pro[0];
     int open_t = -1, open_g = -1;
 
@@ -626,7 +776,7 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
             open_t = cur.t;
             open_g = cur.g;
             acc.clear();
-            if constexpr (MODE == kModeGated) gacc.clear();
+            if constexpr (MODE == kModeGated || MODE == kModeR2) gacc.clear();
         }
         bool ok = wait_phase(full[s], parity, kWaitLimitNs);
         if (ok) {
@@ -639,8 +789,8 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
                 if constexpr (kShared) ok = wait_phase(empty[s], parity, kWaitLimitNs);
                 if (ok) {
                     fence_proxy_async_smem();
-                    issue_weights<NC, MODE == kModeGated>(P, icur, ring + s * kSB, full[s], lane);
-                    issue_acts<NC, MODE == kModeGated>(P, icur, ring + s * kSB, full[s], lane);
+                    issue_weights<NC, MODE>(P, icur, ring + s * kSB, full[s], lane);
+                    issue_acts<NC, MODE>(P, icur, ring + s * kSB, full[s], lane);
                     advance(P, icur);
                 }
             }
@@ -821,7 +971,7 @@ __global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_con
     // Weights stream while the previous grid on the stream (the prep launch,
     // or the previous single-launch GEMV) finishes; griddepcontrol.wait
     // returns once it has completed.
-    if (active) worker_prologue<NC, MODE == kModeGated>(P, W, lane, full, issuer);
+    if (active) worker_prologue<NC, MODE>(P, W, lane, full, issuer);
     pdl_wait();
     if (P.fused) {
         // Single launch: quantize this CTA's share of the activations, then a
@@ -879,6 +1029,29 @@ cudaError_t set_attrs_all() {
     return set_attrs<8, MODE>();
 }
 
+// The two-row variant exists for ncols >= kR2Min only.
+cudaError_t set_attrs_r2() {
+    cudaError_t e;
+    if ((e = set_attrs<3, kModeR2>()) != cudaSuccess) return e;
+    if ((e = set_attrs<4, kModeR2>()) != cudaSuccess) return e;
+    if ((e = set_attrs<5, kModeR2>()) != cudaSuccess) return e;
+    if ((e = set_attrs<6, kModeR2>()) != cudaSuccess) return e;
+    if ((e = set_attrs<7, kModeR2>()) != cudaSuccess) return e;
+    return set_attrs<8, kModeR2>();
+}
+
+void *gemv_fn_r2(int ncols) {
+    switch (ncols) {
+        case 3: return reinterpret_cast<void *>(k_gemv<3, kModeR2>);
+        case 4: return reinterpret_cast<void *>(k_gemv<4, kModeR2>);
+        case 5: return reinterpret_cast<void *>(k_gemv<5, kModeR2>);
+        case 6: return reinterpret_cast<void *>(k_gemv<6, kModeR2>);
+        case 7: return reinterpret_cast<void *>(k_gemv<7, kModeR2>);
+        case 8: return reinterpret_cast<void *>(k_gemv<8, kModeR2>);
+        default: return nullptr;
+    }
+}
+
 template <int MODE>
 void *gemv_fn(int ncols) {
     switch (ncols) {
@@ -907,6 +1080,7 @@ cudaError_t device_setup(int *num_sms) {
         if ((e = set_attrs_all<kModePlain>()) != cudaSuccess) return e;
         if ((e = set_attrs_all<kModeDump>()) != cudaSuccess) return e;
         if ((e = set_attrs_all<kModeGated>()) != cudaSuccess) return e;
+        if ((e = set_attrs_r2()) != cudaSuccess) return e;
         st.ready = true;
     }
     *num_sms = st.num_sms;
@@ -938,6 +1112,7 @@ cudaError_t launch_prep(const PrepParams &p, cudaStream_t s) {
 cudaError_t launch_gemv(const GemvParams &p, int ncols, int mode, int grid, cudaStream_t s) {
     void *fn = mode == kModeDump    ? gemv_fn<kModeDump>(ncols)
                : mode == kModeGated ? gemv_fn<kModeGated>(ncols)
+               : mode == kModeR2    ? gemv_fn_r2(ncols)
                                     : gemv_fn<kModePlain>(ncols);
     if (fn == nullptr) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};

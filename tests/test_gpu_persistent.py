@@ -56,6 +56,12 @@ def layer(q4k, torch, dev, seed, shapes, x_of, ncols, on_device=False):
     return Ws, Wd, xl
 
 
+def n_rowgroups(shapes, ncols):
+    """Row groups of a plain launch: 32 rows, or 64 (two rows per lane) from 3 columns on."""
+    g = 64 if ncols >= 3 else 32
+    return sum((r + g - 1) // g for r, _ in shapes)
+
+
 def control_words_zero(ws, n_rowgroups):
     """status and gdone (bytes 0..7) and the row-group counters (from 256);
     the barrier's arrival counter (128) counts up by design."""
@@ -84,7 +90,7 @@ def test_persistent_equals_two_launch_path_and_oracle(q4k, oracle, torch_mod, de
         assert np.array_equal(oa.cpu().numpy(), ob_np), f"task {i}: differs from the two-launch path"
         assert_close(ob_np, oracle.gemv_f32(W, x.cpu().numpy()), f"task {i}")
     assert ws_b.status() == 0
-    assert control_words_zero(ws_b, sum((r + 31) // 32 for r, _ in shapes))
+    assert control_words_zero(ws_b, n_rowgroups(shapes, ncols))
 
 
 @pytest.mark.parametrize("ncols", [1, 4])
@@ -101,7 +107,7 @@ def test_persistent_full_layer_bitwise(q4k, torch_mod, dev, ncols):
     for i, (oa, ob) in enumerate(zip(a, b)):
         assert torch.equal(oa, ob), f"task {i}"
     assert ws_b.status() == 0
-    assert control_words_zero(ws_b, sum((r + 31) // 32 for r, _ in MISTRAL))
+    assert control_words_zero(ws_b, n_rowgroups(MISTRAL, ncols))
 
 
 def test_persistent_small_unpacked_and_empty_tasks(q4k, oracle, torch_mod, dev):
