@@ -131,15 +131,30 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
 }
 // 2D tensor-map tile load (no multicast): box at element coordinates (x, y).
 // x * element size must be a multiple of 16 bytes.
+// L2 policy for data read once (the weight stream): evicted first, so the
+// activations, their q8a records and the outputs stay resident.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap *tm, int x, int y, uint32_t bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(tm), "r"(x), "r"(y), "r"(bar), "l"(policy)
+        : "memory");
+}
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, int x, int y, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
         "l"(tm), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
-// Non-binding L2 prefetch of the line holding p.
+// Non-binding L2 prefetch of the line holding p, kept in L2 ahead of streamed data.
 __device__ __forceinline__ void prefetch_l2(const void *p) {
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
 }
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");

@@ -33,6 +33,10 @@ constexpr int kMaxPeers = 8;
 #ifndef Q4K_KS
 #define Q4K_KS 2
 #endif
+// Weight boxes are copied with an L2 evict-first policy (read once).
+#ifndef Q4K_WEIGHT_EVICT_FIRST
+#define Q4K_WEIGHT_EVICT_FIRST 1
+#endif
 constexpr int kMaxWarps = Q4K_MAX_WARPS;
 constexpr int kStages = Q4K_STAGES;
 constexpr int kKS = Q4K_KS;  // super-blocks per atom and row

@@ -250,25 +250,32 @@ __device__ __forceinline__ void issue_weights(const GemvParams &P, const AtomCur
     constexpr bool GATED = MODE == kModeGated;
     const TaskDesc &T = P.task[c.t];
     if (lane == 0) {
+#if Q4K_WEIGHT_EVICT_FIRST
+        const uint64_t pol = l2_evict_first_policy();
+#define Q4K_TMA(dst, tm, x, y, b) tma_load_2d_hint(dst, tm, x, y, b, pol)
+#else
+#define Q4K_TMA(dst, tm, x, y, b) tma_load_2d(dst, tm, x, y, b)
+#endif
         if (MODE == kModeR2) {
             // one super-block of 64 rows: two boxes of 32 rows
             mbar_expect_tx(bar, static_cast<uint32_t>(2 * kBoxBytes + NC * kActSBBytes));
-            tma_load_2d(stage, &P.tmap[c.t], c.kp * 36, c.g * 64, bar);
-            tma_load_2d(stage + kBoxBytes, &P.tmap[c.t], c.kp * 36, c.g * 64 + 32, bar);
+            Q4K_TMA(stage, &P.tmap[c.t], c.kp * 36, c.g * 64, bar);
+            Q4K_TMA(stage + kBoxBytes, &P.tmap[c.t], c.kp * 36, c.g * 64 + 32, bar);
         } else if (GATED && T.has_gate) {
             // one super-block position of both matrices: box 0 main, box 1 gate
             static_assert(kKS >= 2, "a gated atom needs two boxes per stage");
             mbar_expect_tx(bar, static_cast<uint32_t>(2 * kBoxBytes + NC * kActSBBytes));
-            tma_load_2d(stage, &P.tmap[c.t], c.kp * 36, c.g * 32, bar);
-            tma_load_2d(stage + kBoxBytes, &P.tmap_gate[T.gate_map], c.kp * 36, c.g * 32, bar);
+            Q4K_TMA(stage, &P.tmap[c.t], c.kp * 36, c.g * 32, bar);
+            Q4K_TMA(stage + kBoxBytes, &P.tmap_gate[T.gate_map], c.kp * 36, c.g * 32, bar);
         } else {
             const int kb0 = c.kp * kKS;
             const int nsb = min(kKS, T.nb - kb0);
             mbar_expect_tx(bar, static_cast<uint32_t>(nsb * (kBoxBytes + NC * kActSBBytes)));
 #pragma unroll
             for (int i = 0; i < kKS; ++i)
-                if (i < nsb) tma_load_2d(stage + i * kBoxBytes, &P.tmap[c.t], (kb0 + i) * 36, c.g * 32, bar);
+                if (i < nsb) Q4K_TMA(stage + i * kBoxBytes, &P.tmap[c.t], (kb0 + i) * 36, c.g * 32, bar);
         }
+#undef Q4K_TMA
     }
     __syncwarp();
 }
