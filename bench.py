@@ -66,12 +66,22 @@ WORKLOADS = {
     "2f": ("mistral-7b-decode-gemv-set-ffn-gate-up-swiglu-fused", MISTRAL_LAYER_FUSED, 32,
            [[("head", 32000, 4096, "head")]]),
     "ffn": ("ffn-gate-up-swiglu-2x14336x4096", [("gate_up", 14336, 4096, "x", "swiglu")], 16, []),
+    # Q6_K weights (the output heads of Q4_K_M checkpoints)
+    "q6": ("mistral-7b-q6_k-head-32000x4096", [("head_q6", 32000, 4096, "x", "q6")], 16, []),
+    "q6l": ("llama-3-q6_k-head-128256x8192", [("head_q6", 128256, 8192, "x", "q6")], 6, []),
 }
 
 
 def ent(e):
-    """(name, rows, K, activation group, glu op or None) of a group entry."""
+    """(name, rows, K, activation group, glu op or None) of a group entry ("q6": Q6_K weights)."""
     return (e[0], e[1], e[2], e[3], e[4] if len(e) > 4 else None)
+
+
+def wbytes(r, K, glu):
+    """Weight bytes of an entry: Q4_K 0.5625 B/weight (two matrices when fused), Q6_K 0.8203."""
+    if glu == "q6":
+        return r * K * 210 // 256
+    return r * K * 9 // 16 * (2 if glu else 1)
 
 
 def build_groups(cfg: str, repeats: int):
@@ -88,7 +98,7 @@ def group_bytes(group, ncols: int, world: int = 1) -> int:
     acts = {}
     for _, r, K, a, _ in map(ent, group):
         acts[a] = K
-    w = sum(r * K * 9 // 16 * (2 if glu else 1) for _, r, K, _, glu in map(ent, group))
+    w = sum(wbytes(r, K, glu) for _, r, K, _, glu in map(ent, group))
     x = sum(ncols * K * 4 for K in acts.values()) * world
     y = sum(ncols * r * 4 for _, r, _, _, _ in map(ent, group))
     return w + x + y
@@ -182,8 +192,13 @@ class ClockSampler:
 # CPU legs (the oracle and the reference's own dot product; checkers only)
 # ---------------------------------------------------------------------------
 def host_group(q4k, group, ncols, rng):
-    mats = [(q4k.gen_q4k_numpy(rng, r, K), K, a) for _, r, K, a, glu in map(ent, group)
-            for _ in range(2 if glu else 1)]
+    """Host matrices (W, K, activation group, Q6_K?) of one launch group, and its activations."""
+    mats = []
+    for _, r, K, a, glu in map(ent, group):
+        if glu == "q6":
+            mats.append((q4k.gen_q6k_numpy(rng, r, K), K, a, True))
+        else:
+            mats += [(q4k.gen_q4k_numpy(rng, r, K), K, a, False) for _ in range(2 if glu else 1)]
     xs = {a: rng.standard_normal((ncols, K)).astype(np.float32) for _, _, K, a, _ in map(ent, group)}
     return mats, xs
 
@@ -197,17 +212,20 @@ def run_reference(args) -> None:
         return
     O = load_oracle()
     q4k = load_package()
-    kind = "reference" if O.ref_available() else "port"
     name, groups = build_groups(args.config, 1)
     group = groups[0]
     ncols = args.ncols
     mats, xs = host_group(q4k, group, ncols, np.random.default_rng(0))
+    # the reference's compiled dot product covers Q4_K; Q6_K runs on the port
+    kind = "reference" if O.ref_available() and not any(m[3] for m in mats) else "port"
     threads = O.max_threads() if kind == "port" else O.ref_lib().ref_max_threads()
 
     def one_step():
-        for W, K, a in mats:
+        for W, K, a, is_q6 in mats:
             yq = O.quantize_q8_1(xs[a])
-            if kind == "reference":
+            if is_q6:
+                O.gemv_q6k_q8_1(W, K, yq, nthreads=threads)
+            elif kind == "reference":
                 O.ref_gemv_q8_1(W, K, yq, nthreads=threads)
             else:
                 O.gemv_q8_1(W, K, yq, nthreads=threads)
@@ -240,8 +258,8 @@ def cpu_baseline(O, mats, group, ncols, budget_s: float = 12.0) -> dict:
     threads = O.max_threads()
     n, t0 = 0, time.perf_counter()
     while True:
-        for W, K, a in mats:
-            O.gemv_f32(W, xs[a], nthreads=threads)
+        for W, K, a, is_q6 in mats:
+            (O.gemv_q6k_f32 if is_q6 else O.gemv_f32)(W, xs[a], nthreads=threads)
         n += 1
         el = time.perf_counter() - t0
         if el > budget_s:
@@ -301,9 +319,10 @@ def main():
     g.manual_seed(1234 + rank)
     peer = world > 1 and args.gather == "peer"
     full_elems = sum(r * ncols for grp in groups for _, r, _, _, _ in map(ent, grp))
-    fused = any(glu for grp in groups for *_, glu in map(ent, grp))
-    if fused and world > 1:
-        raise SystemExit(f"config {args.config} (fused gate/up epilogue) runs on one GPU")
+    q6 = any(glu == "q6" for grp in groups for *_, glu in map(ent, grp))
+    fused = not q6 and any(glu for grp in groups for *_, glu in map(ent, grp))
+    if (fused or q6) and world > 1:
+        raise SystemExit(f"config {args.config} (fused epilogue / Q6_K) runs on one GPU")
     pg = q4k.PeerGather(full_elems) if peer else None
     L = []
     base = 0
@@ -312,8 +331,11 @@ def main():
         ents = []
         for name, rows, K, a, glu in map(ent, grp):
             lo, hi, per = q4k.shard_rows(rows, rank, world)
-            W = q4k.gen_q4k_torch(hi - lo, K, generator=g, device=dev)
-            Wg = q4k.gen_q4k_torch(hi - lo, K, generator=g, device=dev) if glu else None
+            if glu == "q6":
+                W, Wg = q4k.gen_q6k_torch(hi - lo, K, generator=g, device=dev), None
+            else:
+                W = q4k.gen_q4k_torch(hi - lo, K, generator=g, device=dev)
+                Wg = q4k.gen_q4k_torch(hi - lo, K, generator=g, device=dev) if glu else None
             ents.append(dict(name=name, W=W, W_gate=Wg, glu=glu, x=xs[a], rows=rows, K=K, lo=lo, n=hi - lo,
                              per=per))
         if peer:
@@ -335,7 +357,11 @@ def main():
                 e["stride"] = e["per"]
                 off += e["per"] * ncols
             gath = torch.empty((per_tot * ncols * world,), device=dev) if world > 1 else None
-        if fused:
+        if q6:
+            tasks = q4k.make_tasks_q6_k([e["W"] for e in ents], [e["x"] for e in ents], outs)
+            for i, e in enumerate(ents):
+                tasks[i].stride_col_dst = e["stride"]
+        elif fused:
             tasks = q4k.make_tasks_ex([dict(W=e["W"], W_gate=e["W_gate"], x=e["x"], out=o,
                                             glu=e["glu"] or "none") for e, o in zip(ents, outs)])
             for i, e in enumerate(ents):
@@ -346,7 +372,9 @@ def main():
                 tasks[i].stride_col_dst = e["stride"]
         L.append(dict(xs=xs, ents=ents, ybuf=ybuf, tasks=tasks, gath=gath))
 
-    wsb = q4k.batch_ex_workspace_bytes if fused else q4k.batch_workspace_bytes
+    wsb = (q4k.batch_ex_workspace_bytes if fused else
+           (lambda t, n: int(q4k.lib().q4k_batch_q6_k_workspace_bytes(t, len(t), n))) if q6 else
+           q4k.batch_workspace_bytes)
     ws = q4k.Workspace(max(wsb(G["tasks"], ncols) for G in L), dev)
     stream = torch.cuda.Stream(device=dev)
 
@@ -355,6 +383,8 @@ def main():
             q4k.gemv_batch_allgather(tasks, ncols, pg, ws, stream=stream)
         elif fused:
             q4k.gemv_batch_ex(tasks, ncols, ws, stream=stream)
+        elif q6:
+            q4k.gemv_batch_q6_k(tasks, ncols, ws, stream=stream)
         else:
             q4k.gemv_batch(tasks, ncols, ws, stream=stream)
 
@@ -465,8 +495,7 @@ def main():
     if world == 1:
         launch_bytes = group_bytes(g0, ncols)
     else:  # this rank's share of the first launch group
-        launch_bytes = (sum(e["n"] * e["K"] * 9 // 16 * (2 if e["glu"] else 1) + ncols * e["n"] * 4
-                            for e in L[0]["ents"]) +
+        launch_bytes = (sum(wbytes(e["n"], e["K"], e["glu"]) + ncols * e["n"] * 4 for e in L[0]["ents"]) +
                         sum(ncols * x.shape[1] * 4 for x in L[0]["xs"].values()))
 
     # ---- e2e: public C-ABI calls with host buffers ------------------------------
@@ -514,7 +543,8 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         O = load_oracle()
-        mats = [(M.cpu().numpy(), e["K"], a) for e, (_, _, _, a, _) in zip(L[0]["ents"], map(ent, g0))
+        mats = [(M.cpu().numpy(), e["K"], a, e["glu"] == "q6")
+                for e, (_, _, _, a, _) in zip(L[0]["ents"], map(ent, g0))
                 for M in (e["W"], e["W_gate"]) if M is not None]
         cpu = cpu_baseline(O, mats, g0, ncols)
 

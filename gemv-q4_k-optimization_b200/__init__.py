@@ -130,6 +130,11 @@ def lib() -> ctypes.CDLL:
             "q4k_mul_mat_vec_fused": (None, [_P, _P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _P, _I,
                                              _P, _SZ, _P]),
             "q4k_rms_norm_quantize_q8_1": (None, [_P, _I64, _I64, _I64, _I, _P, ctypes.c_float, _P, _P]),
+            "q4k_q6_k_workspace_bytes": (_SZ, [_I64, _I64, _I]),
+            "q4k_mul_mat_vec_q6_k": (None, [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _SZ, _P]),
+            "q4k_mul_mat_vec_q6_k_q8_1": (None, [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _SZ, _P]),
+            "q4k_batch_q6_k_workspace_bytes": (_SZ, [TP, _I, _I]),
+            "q4k_gemv_batch_q6_k": (None, [TP, _I, _I, _P, _SZ, _P]),
             "q4k_ipc_alloc": (None, [_SZ, ctypes.POINTER(ctypes.c_void_p)]),
             "q4k_ipc_free": (None, [_P]),
             "q4k_ipc_handle": (None, [_P, ctypes.c_char_p]),
@@ -473,6 +478,71 @@ def debug_subblock_sums(W, yq, K: int, ws: Workspace | None = None, stream=None)
 # ---------------------------------------------------------------------------
 # synthetic data with the benchmark's value distributions
 # ---------------------------------------------------------------------------
+Q6K_BYTES = 210
+
+
+def mul_mat_vec_q6_k(W, x, out=None, ws: Workspace | None = None, stream=None):
+    """y = W @ x for Q6_K rows W (nrows, K/256*210) uint8 and fp32 x (ncols, K)."""
+    import torch
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    ncols, K = x.shape
+    nrows = W.shape[0]
+    if out is None:
+        out = torch.empty((ncols, nrows), dtype=torch.float32, device=x.device)
+    w = _ws_for(int(lib().q4k_q6_k_workspace_bytes(nrows, K, ncols)), ws, x.device)
+    _check(lib().q4k_mul_mat_vec_q6_k(W.data_ptr(), x.data_ptr(), out.data_ptr(), K, nrows, ncols,
+                                      W.stride(0) // Q6K_BYTES, x.stride(0), out.stride(0), w.ptr, w.nbytes,
+                                      _stream(stream)))
+    return out
+
+
+def mul_mat_vec_q6_k_q8_1(W, yq, K: int, out=None, ws: Workspace | None = None, stream=None):
+    """The q8_1-input Q6_K entry.  yq: (ncols, Kpad/32*36) uint8."""
+    import torch
+    ncols, nrows = yq.shape[0], W.shape[0]
+    if out is None:
+        out = torch.empty((ncols, nrows), dtype=torch.float32, device=yq.device)
+    w = _ws_for(int(lib().q4k_q6_k_workspace_bytes(nrows, K, ncols)), ws, yq.device)
+    _check(lib().q4k_mul_mat_vec_q6_k_q8_1(W.data_ptr(), yq.data_ptr(), out.data_ptr(), K, nrows, ncols,
+                                           W.stride(0) // Q6K_BYTES, yq.stride(0) // Q8_1_BYTES, out.stride(0),
+                                           w.ptr, w.nbytes, _stream(stream)))
+    return out
+
+
+def make_tasks_q6_k(mats: Sequence, xs: Sequence, outs: Sequence):
+    """Task array for gemv_batch_q6_k (W: Q6_K rows)."""
+    arr = make_tasks(mats, xs, outs)
+    for i, W in enumerate(mats):
+        arr[i].stride_row_x = W.stride(0) // Q6K_BYTES
+    return arr
+
+
+def gemv_batch_q6_k(tasks, ncols: int, ws: Workspace, stream=None) -> None:
+    ws.ensure(int(lib().q4k_batch_q6_k_workspace_bytes(tasks, len(tasks), ncols)))
+    _check(lib().q4k_gemv_batch_q6_k(tasks, len(tasks), ncols, ws.ptr, ws.nbytes, _stream(stream)))
+
+
+def gen_q6k_numpy(rng: np.random.Generator, nrows: int, K: int) -> np.ndarray:
+    """Q6_K matrix (nrows, K/256*210) uint8: d = fp16(|N(0,1)|*0.01), int8 scales and the
+    6-bit quants uniform."""
+    nb = K // QK_K
+    W = rng.integers(0, 256, size=(nrows, nb, Q6K_BYTES), dtype=np.uint8)
+    d = (np.abs(rng.standard_normal((nrows, nb))) * 0.01).astype(np.float16)
+    W[:, :, 208:210] = d.view(np.uint8).reshape(nrows, nb, 2)
+    return W.reshape(nrows, nb * Q6K_BYTES)
+
+
+def gen_q6k_torch(nrows: int, K: int, generator=None, device="cuda"):
+    """Same distributions as gen_q6k_numpy, generated on the device."""
+    import torch
+    nb = K // QK_K
+    W = torch.randint(0, 256, (nrows, nb, Q6K_BYTES), dtype=torch.uint8, device=device, generator=generator)
+    d = (torch.randn((nrows, nb), device=device, generator=generator).abs_() * 0.01).to(torch.float16)
+    W[:, :, 208:210] = d.view(torch.uint8).reshape(nrows, nb, 2)
+    return W.view(nrows, nb * Q6K_BYTES)
+
+
 def gen_q4k_numpy(rng: np.random.Generator, nrows: int, K: int) -> np.ndarray:
     """Q4_K matrix (nrows, K/256*144) uint8: d, dmin = fp16(|N(0,1)|*0.01); scale/min
     bytes uniform (so every 6-bit scale and min is uniform on 0..63); nibbles uniform."""

@@ -81,6 +81,7 @@ struct Job {
     int norm = 0;
     float norm_eps = 0.0f;
     const float *norm_w = nullptr;
+    int q6 = 0;  // W holds Q6_K super-blocks (210 bytes) instead of Q4_K
 };
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -121,6 +122,23 @@ int encode_weight_map(CUtensorMap *tm, const void *W, int64_t nrows, int64_t nb,
     return Q4K_OK;
 }
 
+// Q6_K rows as uint64 elements: a box of 210 elements (8 super-blocks,
+// 1680 bytes) x 8 rows.  Needs nb % 8 == 0 and a row stride that is a
+// multiple of 16 bytes (stride_row_x % 8 == 0).
+int encode_q6_map(CUtensorMap *tm, const void *W, int64_t nrows, int64_t nb, int64_t row_stride_bytes) {
+    EncodeTiledFn enc = tensor_map_encoder();
+    if (!enc) return fail(Q4K_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(nb * kQ6Bytes / 8), static_cast<cuuint64_t>(nrows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_bytes)};
+    const cuuint32_t box[2] = {kQ6RowBytes / 8, kQ6Rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(W), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(Q4K_ECUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+    return Q4K_OK;
+}
+
 int validate_job(const Job &j, int ncols, int idx) {
     if (ncols < 1 || ncols > Q4K_MAX_NCOLS)
         return fail(Q4K_EINVAL, "ncols=%d outside 1..%d", ncols, Q4K_MAX_NCOLS);
@@ -133,6 +151,14 @@ int validate_job(const Job &j, int ncols, int idx) {
     if (!j.dst) return fail(Q4K_EINVAL, "task %d: null dst", idx);
     if (ncols > 1 && j.stride_col_dst < j.nrows)
         return fail(Q4K_EINVAL, "task %d: stride_col_dst=%lld < nrows", idx, (long long)j.stride_col_dst);
+    if (j.q6) {
+        if (j.K % (Q4K_QK_K * kQ6AtomSB) != 0)
+            return fail(Q4K_EINVAL, "task %d: Q6_K needs K %% 2048 == 0 (K=%lld)", idx, (long long)j.K);
+        if (j.stride_row_x % kQ6AtomSB != 0)
+            return fail(Q4K_EINVAL, "task %d: Q6_K needs stride_row_x %% 8 == 0 (rows 16-byte aligned)", idx);
+        if (j.gate || j.x_bias || j.gate_bias || j.glu_op != Q4K_GLU_NONE)
+            return fail(Q4K_EINVAL, "task %d: no fused epilogue with Q6_K weights", idx);
+    }
     const bool fused = j.gate || j.x_bias || j.gate_bias || j.glu_op != Q4K_GLU_NONE;
     if (fused) {
         if (j.gate ? (j.glu_op < Q4K_GLU_SWIGLU || j.glu_op > Q4K_GLU_MUL) : j.glu_op != Q4K_GLU_NONE)
@@ -176,6 +202,8 @@ struct Plan {
     bool any_work = false;
     bool any_fused = false;  // a task with a gate or a bias: the epilogue kernel variant
     bool r2 = false;         // the two-rows-per-lane variant (64-row groups)
+    bool q6 = false;         // Q6_K weights
+    int mode = kModePlain;   // kernel variant
 };
 
 // Build the schedule (no device memory touched).  ws may be null (sizing).
@@ -221,8 +249,14 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.any_fused = false;
     for (int i = 0; i < njobs; ++i)
         if (P.act_of_job[i] >= 0 && (jobs[i].gate || jobs[i].x_bias)) P.any_fused = true;
-    P.r2 = !dump && !P.any_fused && ncols >= kR2Min && split_for(ncols) == 1;
-    const int64_t group_rows = P.r2 ? 64 : 32;
+    // Q6_K: every task of the launch (one kernel variant per launch)
+    P.q6 = jobs[0].q6 != 0;
+    for (int i = 1; i < njobs; ++i)
+        if ((jobs[i].q6 != 0) != P.q6) return fail(Q4K_EINVAL, "Q4_K and Q6_K tasks in one launch");
+    if (P.q6 && dump) return fail(Q4K_EINVAL, "no sub-block dump for Q6_K");
+    P.r2 = !P.q6 && !dump && !P.any_fused && ncols >= kR2Min && split_for(ncols) == 1;
+    P.mode = dump ? kModeDump : P.any_fused ? kModeGated : P.q6 ? kModeQ6 : P.r2 ? kModeR2 : kModePlain;
+    const int64_t group_rows = P.r2 ? 64 : P.q6 ? kQ6Rows : 32;
     // row groups and atoms
     int64_t atoms = 0, rgs = 0;
     int nt = 0;
@@ -234,11 +268,11 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         const int64_t nb = j.K / Q4K_QK_K;
         // a gated or two-row atom is one super-block position (of both
         // matrices / of 64 rows); a plain one kKS super-blocks of 32 rows
-        const int64_t apr = (j.gate || P.r2) ? nb : (nb + kKS - 1) / kKS;
+        const int64_t apr = P.q6 ? nb / kQ6AtomSB : (j.gate || P.r2) ? nb : (nb + kKS - 1) / kKS;
         TaskDesc &T = P.gemv.task[nt++];
         T.W = static_cast<const uint8_t *>(j.W);
         T.dst = j.dst;
-        T.row_stride = j.stride_row_x * Q4K_BLOCK_BYTES;
+        T.row_stride = j.stride_row_x * (P.q6 ? kQ6Bytes : Q4K_BLOCK_BYTES);
         T.act_col_stride = nb * kActSBBytes;
         T.dst_col_stride = j.stride_col_dst;
         T.atom_base = atoms;
@@ -270,7 +304,7 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.any_work = atoms > 0;
     P.gemv.ntasks = nt;
     P.gemv.natoms = atoms;
-    const int64_t max_workers = static_cast<int64_t>(num_sms) * rings_for(ncols);
+    const int64_t max_workers = static_cast<int64_t>(num_sms) * rings_m(ncols, P.mode);
     const int64_t nw = atoms < max_workers ? atoms : max_workers;
     P.gemv.nworkers = static_cast<int32_t>(nw);
     P.gemv.packed = atoms >= 4 * max_workers ? 1 : 0;
@@ -292,7 +326,9 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     for (int i = 0; i < njobs; ++i) {
         if (P.act_of_job[i] < 0) continue;
         const Job &j = jobs[i];
-        int st = encode_weight_map(&P.gemv.tmap[nt], j.W, j.nrows, j.K / Q4K_QK_K, j.stride_row_x * Q4K_BLOCK_BYTES);
+        int st = j.q6 ? encode_q6_map(&P.gemv.tmap[nt], j.W, j.nrows, j.K / Q4K_QK_K, j.stride_row_x * kQ6Bytes)
+                      : encode_weight_map(&P.gemv.tmap[nt], j.W, j.nrows, j.K / Q4K_QK_K,
+                                          j.stride_row_x * Q4K_BLOCK_BYTES);
         if (st != Q4K_OK) return st;
         if (j.gate) {
             const int gm = P.gemv.task[nt].gate_map;
@@ -413,7 +449,7 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     } else if ((e = launch_prep(P.prep, s)) != cudaSuccess) {
         return cuda_fail(e, "prep launch");
     }
-    const int mode = dump ? kModeDump : P.any_fused ? kModeGated : P.r2 ? kModeR2 : kModePlain;
+    const int mode = P.mode;
     if ((e = launch_gemv(P.gemv, ncols, mode, num_sms, s)) != cudaSuccess)
         return cuda_fail(e, "gemv launch");
     return Q4K_OK;
@@ -672,6 +708,54 @@ int q4k_mul_mat_vec_fused(const void *W, const void *W_gate, const float *x, flo
     j.bias_col_stride = stride_col_dst;
     j.glu_op = glu_op;
     return run(&j, 1, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t q4k_q6_k_workspace_bytes(int64_t nrows, int64_t K, int ncols) {
+    static const float dummy = 0.0f;
+    static float dummy_out = 0.0f;
+    Job j{reinterpret_cast<const void *>(uintptr_t(256)), &dummy, &dummy_out, nrows, K, K / Q4K_QK_K,
+          K, nrows, kPrepF32};
+    j.q6 = 1;
+    return plan_bytes(&j, 1, ncols);
+}
+
+int q4k_mul_mat_vec_q6_k(const void *W, const float *x, float *dst, int64_t K, int64_t nrows, int ncols,
+                         int64_t stride_row_x, int64_t stride_col_x, int64_t stride_col_dst, void *workspace,
+                         size_t workspace_bytes, q4k_stream_t stream) {
+    Job j{W, x, dst, nrows, K, stride_row_x, stride_col_x, stride_col_dst, kPrepF32};
+    j.q6 = 1;
+    return run(&j, 1, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int q4k_mul_mat_vec_q6_k_q8_1(const void *W, const void *y_q8_1, float *dst, int64_t K, int64_t nrows, int ncols,
+                              int64_t stride_row_x, int64_t stride_col_y, int64_t stride_col_dst, void *workspace,
+                              size_t workspace_bytes, q4k_stream_t stream) {
+    Job j{W, y_q8_1, dst, nrows, K, stride_row_x, stride_col_y, stride_col_dst, kPrepQ81};
+    j.q6 = 1;
+    return run(&j, 1, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t q4k_batch_q6_k_workspace_bytes(const q4k_task *tasks, int ntasks, int ncols) {
+    if (!tasks || ntasks < 1 || ntasks > kMaxTasks) return 0;
+    Job jobs[kMaxTasks];
+    for (int i = 0; i < ntasks; ++i) {
+        jobs[i] = {tasks[i].W, tasks[i].x, tasks[i].dst, tasks[i].nrows, tasks[i].K,
+                   tasks[i].stride_row_x, tasks[i].stride_col_x, tasks[i].stride_col_dst, kPrepF32};
+        jobs[i].q6 = 1;
+    }
+    return plan_bytes(jobs, ntasks, ncols);
+}
+
+int q4k_gemv_batch_q6_k(const q4k_task *tasks, int ntasks, int ncols, void *workspace, size_t workspace_bytes,
+                        q4k_stream_t stream) {
+    if (!tasks || ntasks < 1 || ntasks > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..16", ntasks);
+    Job jobs[kMaxTasks];
+    for (int i = 0; i < ntasks; ++i) {
+        jobs[i] = {tasks[i].W, tasks[i].x, tasks[i].dst, tasks[i].nrows, tasks[i].K,
+                   tasks[i].stride_row_x, tasks[i].stride_col_x, tasks[i].stride_col_dst, kPrepF32};
+        jobs[i].q6 = 1;
+    }
+    return run(jobs, ntasks, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int q4k_gemv_batch_allgather(const q4k_task *tasks, int ntasks, int ncols, const q4k_gather *gather,

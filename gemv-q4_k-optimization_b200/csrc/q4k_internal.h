@@ -71,6 +71,48 @@ __host__ __device__ constexpr int smem_bytes(int ncols) { return rings_for(ncols
 static_assert(rings_for(8) >= 4, "ring too large for 8 columns");
 static_assert(warps_for(8) * 32 <= 1024, "block too large");
 
+// Kernel variants: plain, debug dump of the sub-block sums, fused epilogues.
+// kModeR2: plain tasks at ncols >= kR2Min, 64-row groups with two rows per
+// lane (one activation load serves both rows).  kModeQ6: Q6_K weights.
+enum GemvMode : int { kModePlain = 0, kModeDump = 1, kModeGated = 2, kModeR2 = 3, kModeQ6 = 4 };
+#ifndef Q4K_R2_MIN
+#define Q4K_R2_MIN 3
+#endif
+constexpr int kR2Min = Q4K_R2_MIN;
+
+// Q6_K (210-byte super-blocks: ql[128], qh[64], int8 scales[16], fp16 d).  A
+// 210-byte row chunk is never a multiple of 16 bytes, 8 super-blocks (1680 B)
+// are: an atom is 8 rows x 8 super-blocks, one tensor-map box of 210 uint64
+// x 8 rows, landing at a 1680-byte row pitch.  Lane (r = lane & 7,
+// q = lane >> 3) takes super-blocks 2q and 2q+1 of row r.  The activation
+// records of the 8 super-blocks sit at a 336-byte pitch (lanes with different
+// q read different banks).
+constexpr int kQ6Bytes = 210;
+constexpr int kQ6AtomSB = 8;
+constexpr int kQ6Rows = 8;
+constexpr int kQ6RowBytes = kQ6AtomSB * kQ6Bytes;  // 1680
+constexpr int kQ6BoxBytes = kQ6Rows * kQ6RowBytes;  // 13440
+constexpr int kQ6RecPitch = 336;
+__host__ __device__ constexpr int q6_stage_bytes(int ncols) { return kQ6BoxBytes + ncols * kQ6AtomSB * kQ6RecPitch; }
+__host__ __device__ constexpr int rings_q6(int ncols) {
+    return kSmemLimit / (kStages * q6_stage_bytes(ncols)) < kMaxWarps ? kSmemLimit / (kStages * q6_stage_bytes(ncols))
+                                                                      : kMaxWarps;
+}
+static_assert(rings_q6(8) >= 2, "Q6_K ring too large for 8 columns");
+// Geometry by kernel variant.
+__host__ __device__ constexpr int stage_bytes_m(int ncols, int mode) {
+    return mode == kModeQ6 ? q6_stage_bytes(ncols) : stage_bytes(ncols);
+}
+__host__ __device__ constexpr int rings_m(int ncols, int mode) {
+    return mode == kModeQ6 ? rings_q6(ncols) : rings_for(ncols);
+}
+__host__ __device__ constexpr int warps_m(int ncols, int mode) {
+    return mode == kModeQ6 ? rings_q6(ncols) : warps_for(ncols);
+}
+__host__ __device__ constexpr int smem_m(int ncols, int mode) {
+    return rings_m(ncols, mode) * kStages * stage_bytes_m(ncols, mode);
+}
+
 // Device status codes (match q4k_status).
 constexpr int kStatusOk = 0;
 constexpr int kStatusTimeout = 3;
@@ -180,14 +222,6 @@ struct PrepParams {
 
 // Launchers (q4k_kernels.cu).  Return cudaSuccess or the launch error.
 cudaError_t launch_prep(const PrepParams &p, cudaStream_t s);
-// Kernel variants: plain, debug dump of the sub-block sums, fused epilogues.
-// kModeR2: plain tasks at ncols >= kR2Min, 64-row groups with two rows per
-// lane (one activation load serves both rows).
-enum GemvMode : int { kModePlain = 0, kModeDump = 1, kModeGated = 2, kModeR2 = 3 };
-#ifndef Q4K_R2_MIN
-#define Q4K_R2_MIN 3
-#endif
-constexpr int kR2Min = Q4K_R2_MIN;
 cudaError_t launch_gemv(const GemvParams &p, int ncols, int mode, int grid, cudaStream_t s);
 // Per-device setup (SM count, shared-memory opt-in); thread-safe, idempotent.
 cudaError_t device_setup(int *num_sms);

@@ -230,11 +230,12 @@ __device__ __forceinline__ int64_t worker_of(const GemvParams &P, int64_t a) {
     return ((a + 1) * P.nworkers - 1) / P.natoms;
 }
 
-// Stage layout: [kKS boxes of 32 rows x 144 B][NC columns x kKS activation records].
-template <int NC>
+// Stage layout: [kKS boxes of 32 rows x 144 B][NC columns x kKS activation
+// records]; Q6_K: [8 rows x 1680 B][NC columns x 8 records at a 336-byte pitch].
+template <int NC, int MODE = kModePlain>
 struct Stage {
-    static constexpr int kActOff = kWStageBytes;
-    static constexpr int kBytes = stage_bytes(NC);
+    static constexpr int kActOff = MODE == kModeQ6 ? kQ6BoxBytes : kWStageBytes;
+    static constexpr int kBytes = stage_bytes_m(NC, MODE);
     // tensor-map boxes land 128-byte aligned: every stage, box and record
     // region starts on a multiple of 128 bytes from the ring base
     static_assert(kBoxBytes % 128 == 0 && kActOff % 128 == 0 && kBytes % 128 == 0, "stage alignment");
@@ -256,7 +257,11 @@ __device__ __forceinline__ void issue_weights(const GemvParams &P, const AtomCur
 #else
 #define Q4K_TMA(dst, tm, x, y, b) tma_load_2d(dst, tm, x, y, b)
 #endif
-        if (MODE == kModeR2) {
+        if (MODE == kModeQ6) {
+            // 8 rows x 8 super-blocks: one box of 210 uint64 x 8 rows
+            mbar_expect_tx(bar, static_cast<uint32_t>(kQ6BoxBytes + NC * kQ6AtomSB * kActSBBytes));
+            Q4K_TMA(stage, &P.tmap[c.t], c.kp * (kQ6RowBytes / 8), c.g * kQ6Rows, bar);
+        } else if (MODE == kModeR2) {
             // one super-block of 64 rows: two boxes of 32 rows
             mbar_expect_tx(bar, static_cast<uint32_t>(2 * kBoxBytes + NC * kActSBBytes));
             Q4K_TMA(stage, &P.tmap[c.t], c.kp * 36, c.g * 64, bar);
@@ -286,12 +291,23 @@ template <int NC, int MODE>
 __device__ __forceinline__ void issue_acts(const GemvParams &P, const AtomCursor &c, uint32_t stage,
                                            uint32_t bar, int lane) {
     const TaskDesc &T = P.task[c.t];
+    if constexpr (MODE == kModeQ6) {
+        // the 8 records of the atom's super-blocks, per column, at a 336-byte pitch
+        for (int i = lane; i < NC * kQ6AtomSB; i += 32) {
+            const int j = i / kQ6AtomSB, sbi = i % kQ6AtomSB;
+            const uint8_t *src =
+                T.act + j * T.act_col_stride + static_cast<int64_t>(c.kp * kQ6AtomSB + sbi) * kActSBBytes;
+            bulk_g2s(stage + Stage<NC, MODE>::kActOff + j * (kQ6AtomSB * kQ6RecPitch) + sbi * kQ6RecPitch, src,
+                     static_cast<uint32_t>(kActSBBytes), bar);
+        }
+        return;
+    }
     const bool gated = MODE == kModeR2 || (MODE == kModeGated && T.has_gate);  // one record per atom
     const int kb0 = gated ? c.kp : c.kp * kKS;
     const int nsb = gated ? 1 : min(kKS, T.nb - kb0);
     if (lane < NC) {
         const uint8_t *src = T.act + lane * T.act_col_stride + static_cast<int64_t>(kb0) * kActSBBytes;
-        bulk_g2s(stage + Stage<NC>::kActOff + lane * (kKS * kActSBBytes), src,
+        bulk_g2s(stage + Stage<NC, MODE>::kActOff + lane * (kKS * kActSBBytes), src,
                  static_cast<uint32_t>(nsb * kActSBBytes), bar);
     }
 }
@@ -408,6 +424,19 @@ struct RowAcc {
     __device__ __forceinline__ float value(int j) const { return sum[j] - comp[j]; }
 };
 
+// Q6_K rows: super-block terms reach ~1e5 (int8 scales times 6-bit values)
+// while rows cancel to ~1, and a row's super-blocks are spread over four
+// lanes, so the sums run in fp64 (one rounding at the end).
+template <int NCW>
+struct RowAccD {
+    double s[NCW];
+    __device__ __forceinline__ void clear() {
+#pragma unroll
+        for (int j = 0; j < NCW; ++j) s[j] = 0.0;
+    }
+    __device__ __forceinline__ void add(int j, double v) { s[j] += v; }
+};
+
 // Per-row constants of one super-block: d, dmin and the 6-bit scales/mins.
 struct SbHead {
     float d, dmin, nd23, pm23;
@@ -499,6 +528,84 @@ __device__ __forceinline__ void sb_dot2(uint32_t pA, uint32_t pB, uint32_t act, 
     for (int c = 0; c < 4; ++c) pair_dot2<NC>(pA, pB, act, c, A, B, accA, accB);
 }
 
+// ---- Q6_K --------------------------------------------------------------------
+// Word i (4 bytes) of the super-block at smem byte address a; MIS: a is 2 mod 4
+// (odd super-blocks of a 1680-byte row), read as two aligned words and a
+// funnel shift.
+template <bool MIS>
+__device__ __forceinline__ uint32_t q6_word(uint32_t a, int i) {
+    if constexpr (!MIS) {
+        return lds32(a + 4 * i);
+    } else {
+        return __funnelshift_r(lds32(a - 2 + 4 * i), lds32(a + 2 + 4 * i), 16);
+    }
+}
+
+// Signed 6-bit values minus 32, four per word: v - 32 for v in 0..63 is v ^ 0x20
+// with bit 5 of the result copied into bits 6 and 7 (sign extension).
+__device__ __forceinline__ uint32_t q6_signed(uint32_t v) {
+    const uint32_t t = v ^ 0x20202020u;
+    const uint32_t m = t & 0x20202020u;
+    return t | (m << 1) | (m << 2);
+}
+
+// One Q6_K super-block of one row (at smem a) against NC activation records
+// (act, column pitch 8 * 336): per q8_1 block k, S = sum over each 16-weight
+// half of (q6 - 32) * q8 (signed dp4a), isum = sc[2k] S0 + sc[2k+1] S1, times
+// d8; the super-block total times d (kernels/vecdotq.cuh:576-601, :867-890).
+template <int NC, bool MIS>
+__device__ __forceinline__ void q6_sb(uint32_t a, uint32_t act, RowAccD<NC> &acc) {
+    const uint32_t dw = MIS ? lds32(a + 206) : lds32(a + 208);
+    const double d = __half2float(__ushort_as_half(static_cast<unsigned short>(MIS ? dw >> 16 : dw & 0xFFFFu)));
+    uint32_t scw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) scw[i] = q6_word<MIS>(a + 192, i);
+    double s[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) s[c] = 0.0;
+#pragma unroll 1
+    for (int n = 0; n < 2; ++n) {
+        uint32_t ql[16], qh[8];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) ql[i] = q6_word<MIS>(a + 64 * n, i);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qh[i] = q6_word<MIS>(a + 128 + 32 * n, i);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const int k = 4 * n + jj;
+            uint32_t vi[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t lo = (ql[8 * (jj & 1) + i] >> (4 * (jj >> 1))) & 0x0F0F0F0Fu;
+                const uint32_t hi = (jj < 2 ? (qh[i] << (4 - 2 * jj)) : (qh[i] >> (2 * jj - 4))) & 0x30303030u;
+                vi[i] = q6_signed(lo | hi);
+            }
+            const uint32_t sw = scw[k >> 1];
+            const int sc0 = static_cast<int32_t>(sw << (24 - 16 * (k & 1))) >> 24;
+            const int sc1 = static_cast<int32_t>(sw << (16 - 16 * (k & 1))) >> 24;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const uint32_t ac = act + c * (kQ6AtomSB * kQ6RecPitch);
+                const uint4 q0 = lds128(ac + 32 * k), q1 = lds128(ac + 32 * k + 16);
+                int S0 = dp4a_ss(vi[0], q0.x, 0);
+                S0 = dp4a_ss(vi[1], q0.y, S0);
+                S0 = dp4a_ss(vi[2], q0.z, S0);
+                S0 = dp4a_ss(vi[3], q0.w, S0);
+                int S1 = dp4a_ss(vi[4], q1.x, 0);
+                S1 = dp4a_ss(vi[5], q1.y, S1);
+                S1 = dp4a_ss(vi[6], q1.z, S1);
+                S1 = dp4a_ss(vi[7], q1.w, S1);
+                // d8 of block k: the record keeps d8 for even k and d8/16 for odd k
+                const float f = __uint_as_float(lds32(ac + kActMetaOff + 16 * (k >> 1) + 4 * (k & 1)));
+                const double d8 = (k & 1) ? f * 16.0f : f;  // exact (power-of-two factor)
+                s[c] = fma(d8, static_cast<double>(sc0 * S0 + sc1 * S1), s[c]);  // products exact in fp64
+            }
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < NC; ++c) acc.add(c, s[c] * d);
+}
+
 template <int NCW>
 __device__ __forceinline__ void add_sb(RowAcc<NCW> &acc, const uint64_t (&sb)[NCW]) {
 #pragma unroll
@@ -510,15 +617,24 @@ __device__ __forceinline__ void add_sb(RowAcc<NCW> &acc, const uint64_t (&sb)[NC
 
 template <int NCW, int NC, int MODE>
 __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCursor &c, uint32_t stage, int lane,
-                                             int j0, RowAcc<NCW> &acc, RowAcc<NCW> &gacc) {
+                                             int j0, RowAcc<NCW> &acc, RowAcc<NCW> &gacc, RowAccD<NCW> &dacc) {
     const TaskDesc &T = P.task[c.t];
+    if constexpr (MODE == kModeQ6) {
+        // row lane & 7 of the group, super-blocks 2q and 2q+1 (q = lane >> 3)
+        const int r = lane & 7, q = lane >> 3;
+        const uint32_t rowa = stage + r * kQ6RowBytes;
+        const uint32_t acts = stage + Stage<NC, MODE>::kActOff;
+        q6_sb<NCW, false>(rowa + (2 * q) * kQ6Bytes, acts + (2 * q) * kQ6RecPitch, dacc);
+        q6_sb<NCW, true>(rowa + (2 * q + 1) * kQ6Bytes, acts + (2 * q + 1) * kQ6RecPitch, dacc);
+        return;
+    }
     if constexpr (MODE == kModeR2) {
         // 64-row group: lane holds rows 64g + lane (box 0) and 64g + 32 + lane
         // (box 1) of super-block c.kp; rows past the end are zero-filled.
         uint64_t sbA[NCW], sbB[NCW];
 #pragma unroll
         for (int j = 0; j < NCW; ++j) sbA[j] = sbB[j] = 0ull;
-        sb_dot2<NCW>(stage + lane * kPitch, stage + kBoxBytes + lane * kPitch, stage + Stage<NC>::kActOff, sbA,
+        sb_dot2<NCW>(stage + lane * kPitch, stage + kBoxBytes + lane * kPitch, stage + Stage<NC, MODE>::kActOff, sbA,
                      sbB);
         add_sb(acc, sbA);
         add_sb(gacc, sbB);
@@ -527,7 +643,7 @@ __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCurs
     const int rows = min(32, T.nrows - c.g * 32);
     if (lane >= rows) return;
     constexpr bool DUMP = MODE == kModeDump;
-    const uint32_t act = stage + Stage<NC>::kActOff + j0 * (kKS * kActSBBytes);
+    const uint32_t act = stage + Stage<NC, MODE>::kActOff + j0 * (kKS * kActSBBytes);
     if constexpr (MODE == kModeGated) {
         if (T.has_gate) {
             uint64_t sb[NCW];
@@ -625,7 +741,8 @@ __device__ __forceinline__ void store_final(const GemvParams &P, const TaskDesc 
 // is used.
 template <int NCW, int NC, int MODE>
 __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCursor &cur, const RowAcc<NCW> &acc,
-                                            const RowAcc<NCW> &gacc, int64_t worker, int64_t a0, int64_t a1,
+                                            const RowAcc<NCW> &gacc, const RowAccD<NCW> &dacc, int64_t worker,
+                                            int64_t a0, int64_t a1,
                                             int lane, int j0, int64_t cta_w0, int64_t cta_w1, int *cta_cnt) {
     constexpr int kSplit = split_for(NC);
     constexpr bool DUMP = MODE == kModeDump;
@@ -634,16 +751,24 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
     const TaskDesc &T = P.task[cur.t];
     // second set of sums: the gate (gated task) or row 64g + 32 + lane (two-row launch)
     const bool gated = R2 || (GATED && T.has_gate);
+    constexpr bool Q6 = MODE == kModeQ6;
     float v[NCW], gv[NCW];
 #pragma unroll
     for (int j = 0; j < NCW; ++j) {
         v[j] = acc.value(j);
         gv[j] = (GATED || R2) ? gacc.value(j) : 0.0f;
+        if constexpr (Q6) {
+            // the four lanes of a row (lane & 7) hold two super-blocks each (fp64)
+            double t = dacc.s[j];
+            t += __shfl_xor_sync(0xffffffffu, t, 8);
+            t += __shfl_xor_sync(0xffffffffu, t, 16);
+            v[j] = static_cast<float>(t);
+        }
     }
     const int64_t sg = T.atom_base + static_cast<int64_t>(cur.g) * T.apr;
     const int64_t eg = sg + T.apr;
-    const int row = cur.g * (R2 ? 64 : 32) + lane;
-    const bool valid = row < T.nrows;
+    const int row = cur.g * (R2 ? 64 : Q6 ? kQ6Rows : 32) + lane;
+    const bool valid = row < T.nrows && (!Q6 || lane < kQ6Rows);
     const bool valid2 = R2 && row + 32 < T.nrows;
     if (sg >= a0 && eg <= a1) {
         if (!DUMP && valid) {
@@ -729,7 +854,7 @@ struct WorkerPipe {
 template <int NC, int MODE>
 __device__ __forceinline__ void worker_prologue(const GemvParams &P, WorkerPipe &W, int lane,
                                                 const uint32_t (&bar)[kStages], bool issue) {
-    constexpr int kSB = Stage<NC>::kBytes;
+    constexpr int kSB = Stage<NC, MODE>::kBytes;
     W.icur = locate_atom(P, W.a0);
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
@@ -752,7 +877,7 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
                                             bool issuer, const uint32_t (&full)[kStages],
                                             const uint32_t (&empty)[kStages], int64_t cta_w0, int64_t cta_w1,
                                             int *cta_cnt) {
-    constexpr int kSB = Stage<NC>::kBytes;
+    constexpr int kSB = Stage<NC, MODE>::kBytes;
     constexpr bool kShared = split_for(NC) > 1;
     const int n = W.n;
     const uint32_t ring = W.ring;
@@ -766,8 +891,10 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
     // Sums of the open row group: main and gate (gated launches), or rows
     // 64g + lane and 64g + 32 + lane (two-row launches).
     RowAcc<NCW> acc, gacc;
+    RowAccD<NCW> dacc;  // Q6_K launches
     acc.clear();
     if constexpr (MODE == kModeGated || MODE == kModeR2) gacc.clear();
+    if constexpr (MODE == kModeQ6) dacc.clear();
     AtomCursor cur = W.pro[0];
     int open_t = -1, open_g = -1;
 
@@ -777,17 +904,18 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
         if (cur.t != open_t || cur.g != open_g) {
             if (open_t >= 0) {
                 AtomCursor o{open_t, open_g, 0};
-                flush_group<NCW, NC, MODE>(P, o, acc, gacc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1,
+                flush_group<NCW, NC, MODE>(P, o, acc, gacc, dacc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1,
                                            cta_cnt);
             }
             open_t = cur.t;
             open_g = cur.g;
             acc.clear();
             if constexpr (MODE == kModeGated || MODE == kModeR2) gacc.clear();
+            if constexpr (MODE == kModeQ6) dacc.clear();
         }
         bool ok = wait_phase(full[s], parity, kWaitLimitNs);
         if (ok) {
-            compute_atom<NCW, NC, MODE>(P, cur, ring + s * kSB, lane, j0, acc, gacc);
+            compute_atom<NCW, NC, MODE>(P, cur, ring + s * kSB, lane, j0, acc, gacc, dacc);
             __syncwarp();
             if constexpr (kShared) {
                 if (lane == 0) mbar_arrive(empty[s]);
@@ -818,7 +946,7 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
     }
     if (open_t >= 0) {
         AtomCursor o{open_t, open_g, 0};
-        flush_group<NCW, NC, MODE>(P, o, acc, gacc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1,
+        flush_group<NCW, NC, MODE>(P, o, acc, gacc, dacc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1,
                                    cta_cnt);
     }
 }
@@ -926,12 +1054,12 @@ __device__ __forceinline__ void gather_epilogue(const GemvParams &P) {
 }
 
 template <int NC, int MODE>
-__global__ void __launch_bounds__(warps_for(NC) * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
+__global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
     constexpr bool DUMP = MODE == kModeDump;
-    constexpr int kR = rings_for(NC);
+    constexpr int kR = rings_m(NC, MODE);
     constexpr int kSplit = split_for(NC);
     constexpr int kNC0 = (NC + kSplit - 1) / kSplit;  // columns of the issuer warp
-    constexpr int kSB = Stage<NC>::kBytes;
+    constexpr int kSB = Stage<NC, MODE>::kBytes;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bars[kR][kStages];
     __shared__ __align__(8) uint64_t empty_bars[kR][kStages];
@@ -1020,7 +1148,7 @@ DevState g_dev[64];
 
 template <int NC, int MODE>
 cudaError_t set_attrs() {
-    return cudaFuncSetAttribute(k_gemv<NC, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(NC));
+    return cudaFuncSetAttribute(k_gemv<NC, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_m(NC, MODE));
 }
 
 template <int MODE>
@@ -1088,6 +1216,7 @@ cudaError_t device_setup(int *num_sms) {
         if ((e = set_attrs_all<kModeDump>()) != cudaSuccess) return e;
         if ((e = set_attrs_all<kModeGated>()) != cudaSuccess) return e;
         if ((e = set_attrs_r2()) != cudaSuccess) return e;
+        if ((e = set_attrs_all<kModeQ6>()) != cudaSuccess) return e;
         st.ready = true;
     }
     *num_sms = st.num_sms;
@@ -1120,12 +1249,13 @@ cudaError_t launch_gemv(const GemvParams &p, int ncols, int mode, int grid, cuda
     void *fn = mode == kModeDump    ? gemv_fn<kModeDump>(ncols)
                : mode == kModeGated ? gemv_fn<kModeGated>(ncols)
                : mode == kModeR2    ? gemv_fn_r2(ncols)
+               : mode == kModeQ6    ? gemv_fn<kModeQ6>(ncols)
                                     : gemv_fn<kModePlain>(ncols);
     if (fn == nullptr) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
-    cfg.blockDim = dim3(warps_for(ncols) * 32);
-    cfg.dynamicSmemBytes = smem_bytes(ncols);
+    cfg.blockDim = dim3(warps_m(ncols, mode) * 32);
+    cfg.dynamicSmemBytes = smem_m(ncols, mode);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -225,6 +225,26 @@ Q4K_API int q4k_mul_mat_vec_fused(const void *W, const void *W_gate, const float
                                   int64_t stride_col_dst, const float *x_bias, const float *gate_bias, int glu_op,
                                   void *workspace, size_t workspace_bytes, q4k_stream_t stream);
 
+/* ---- Q6_K weights -----------------------------------------------------------------
+ * The reference's MMVQ also serves Q6_K (mul_mat_vec_q<GGML_TYPE_Q6_K>; dot
+ * product kernels/vecdotq.cuh:576-601, :867-890): the output head and some
+ * layers of Q4_K_M checkpoints.  block_q6_K is 210 bytes per 256 weights
+ * (ql[128] low 4 bits, qh[64] high 2 bits, int8 scales[16] per 16 weights,
+ * fp16 d); weight = d * scale * (q6 - 32).  Same activations (fp32 or q8_1),
+ * same output layout and strides (stride_row_x in super-blocks) as the Q4_K
+ * entries.  Needs K % 2048 == 0 and stride_row_x % 8 == 0 (each row starts on
+ * a 16-byte boundary); Q4_K and Q6_K tasks do not share a launch. */
+Q4K_API size_t q4k_q6_k_workspace_bytes(int64_t nrows, int64_t K, int ncols);
+Q4K_API int q4k_mul_mat_vec_q6_k(const void *W, const float *x, float *dst, int64_t K, int64_t nrows, int ncols,
+                                 int64_t stride_row_x, int64_t stride_col_x, int64_t stride_col_dst,
+                                 void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+Q4K_API int q4k_mul_mat_vec_q6_k_q8_1(const void *W, const void *y_q8_1, float *dst, int64_t K, int64_t nrows,
+                                      int ncols, int64_t stride_row_x, int64_t stride_col_y, int64_t stride_col_dst,
+                                      void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+Q4K_API size_t q4k_batch_q6_k_workspace_bytes(const q4k_task *tasks, int ntasks, int ncols);
+Q4K_API int q4k_gemv_batch_q6_k(const q4k_task *tasks, int ntasks, int ncols, void *workspace,
+                                size_t workspace_bytes, q4k_stream_t stream);
+
 /* ---- row-sharded multi-GPU: GEMV fused with the output all-gather ------------- */
 
 /* Row-split across GPUs is the reference's multi-GPU mode (mmvq.cu:764-793,

@@ -58,6 +58,9 @@ def lib() -> ctypes.CDLL:
         L.or_f2h.restype = ctypes.c_uint16
         L.or_quantize_q8_1.argtypes = [_c_p, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p]
         L.or_rmsnorm.argtypes = [_c_p, _c_i64, _c_i64, ctypes.c_int, _c_p, ctypes.c_float, _c_p]
+        L.or_dequant_q6k.argtypes = [_c_p, _c_i64, _c_i64, _c_i64, _c_p]
+        L.or_gemv_q6k_q8_1.argtypes = [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, ctypes.c_int, _c_p, _c_i64,
+                                       ctypes.c_int]
         L.or_rmsnorm_scale.argtypes = [_c_p, _c_i64, ctypes.c_float]
         L.or_rmsnorm_scale.restype = ctypes.c_float
         L.or_subblock_sums_sb.argtypes = [_c_p, _c_p, _c_p, _c_p]
@@ -112,6 +115,36 @@ def quantize_q8_1(x: np.ndarray, Kpad: int | None = None) -> np.ndarray:
     out = np.zeros((ncols, Kp // QK8_1 * Q81_BYTES), dtype=np.uint8)
     lib().or_quantize_q8_1(_ptr(x), K, K, Kp, ncols, _ptr(out))
     return out
+
+
+Q6K_BYTES = 210
+
+
+def dequant_q6k(W: np.ndarray, K: int) -> np.ndarray:
+    """Q6_K rows (nrows, K/256*210) uint8 -> (nrows, K) float32."""
+    W = np.ascontiguousarray(W, dtype=np.uint8)
+    out = np.empty((W.shape[0], K), dtype=np.float32)
+    lib().or_dequant_q6k(_ptr(W), W.shape[0], K, W.shape[1] // Q6K_BYTES, _ptr(out))
+    return out
+
+
+def gemv_q6k_q8_1(W: np.ndarray, K: int, yq: np.ndarray, nthreads: int = 0) -> np.ndarray:
+    """Q6_K rows x q8_1 columns (ncols, Kpad/32*36) -> (ncols, nrows) float32 (exact sums)."""
+    W = np.ascontiguousarray(W, dtype=np.uint8)
+    yq = np.ascontiguousarray(yq, dtype=np.uint8)
+    nrows, ncols = W.shape[0], yq.shape[0]
+    out = np.empty((ncols, nrows), dtype=np.float32)
+    lib().or_gemv_q6k_q8_1(_ptr(W), nrows, K, W.shape[1] // Q6K_BYTES, _ptr(yq), yq.shape[1] // Q81_BYTES, ncols,
+                           _ptr(out), nrows, nthreads)
+    return out
+
+
+def gemv_q6k_f32(W: np.ndarray, x: np.ndarray, nthreads: int = 0) -> np.ndarray:
+    """fp32 x (ncols, K): q8_1 quantization, then the Q6_K product."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if x.ndim == 1:
+        x = x[None, :]
+    return gemv_q6k_q8_1(W, x.shape[1], quantize_q8_1(x), nthreads)
 
 
 def rmsnorm(x: np.ndarray, w: np.ndarray | None = None, eps: float = 1e-5) -> np.ndarray:

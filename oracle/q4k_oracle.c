@@ -137,6 +137,84 @@ void or_quantize_q8_1(const float *x, int64_t K, int64_t stride_col_x,
 }
 
 /* ------------------------------------------------------------------------ */
+/* Q6_K (the other k-quant of Q4_K_M checkpoints: output head, some layers)  */
+/* ------------------------------------------------------------------------ */
+
+#define Q6K_BYTES 210 /* ql[128], qh[64], int8 scales[16], fp16 d */
+
+/*
+ * Signed 6-bit value of weight w (0..255) of a Q6_K super-block: low 4 bits
+ * from ql, high 2 bits from qh, minus 32.  With w = 128n + 32j + l (n = 0,1,
+ * j = 0..3, l = 0..31): low nibble (j >> 1) of ql[64n + 32(j & 1) + l], bits
+ * 2j..2j+1 of qh[32n + l]; its 16-weight sub-block is s = w / 16 with scale
+ * scales[s].  This is the indexing of kernels/vecdotq.cuh:867-890 (vl from
+ * ql at iqs, vh from qh shifted by vh_shift, scales at scale_offset) spelled
+ * out per weight.
+ */
+static int q6_value(const uint8_t *sb, int w) {
+    const int n = w >> 7, j = (w >> 5) & 3, l = w & 31;
+    const int lo = (sb[64 * n + 32 * (j & 1) + l] >> (4 * (j >> 1))) & 0xF;
+    const int hi = (sb[128 + 32 * n + l] >> (2 * j)) & 3;
+    return (lo | (hi << 4)) - 32;
+}
+
+/* Dequantized weights of Q6_K rows (for cross-checks): (nrows, K) floats. */
+void or_dequant_q6k(const uint8_t *W, int64_t nrows, int64_t K, int64_t stride_row_blocks, float *out) {
+    const int64_t nb = K / QK_K;
+    for (int64_t r = 0; r < nrows; ++r)
+        for (int64_t kb = 0; kb < nb; ++kb) {
+            const uint8_t *sb = W + (r * stride_row_blocks + kb) * Q6K_BYTES;
+            const float d = or_h2f((uint16_t)(sb[208] | (sb[209] << 8)));
+            for (int w = 0; w < QK_K; ++w)
+                out[r * K + kb * QK_K + w] = d * (float)(int8_t)sb[192 + w / 16] * (float)q6_value(sb, w);
+        }
+}
+
+/*
+ * y[col][row] = sum over super-blocks of d * sum_k d8_k * (sc[2k] * S[2k] +
+ * sc[2k+1] * S[2k+1]), S[s] = sum over sub-block s (16 weights) of (q6 - 32)
+ * * q8 -- vec_dot_q6_K_q8_1_impl_mmvq (kernels/vecdotq.cuh:576-601): integer
+ * dot per 4 weights, times the int8 scale, times d8 of the q8_1 block, the
+ * total times d.  Exact sums in fp64.
+ */
+void or_gemv_q6k_q8_1(const uint8_t *W, int64_t nrows, int64_t K, int64_t stride_row_blocks,
+                      const uint8_t *y_q8_1, int64_t stride_col_y_blocks, int ncols, float *dst,
+                      int64_t stride_col_dst, int nthreads) {
+    const int64_t nb = K / QK_K;
+#ifdef _OPENMP
+    if (nthreads <= 0) nthreads = omp_get_max_threads();
+#pragma omp parallel for schedule(static) num_threads(nthreads)
+#endif
+    for (int64_t r = 0; r < nrows; ++r) {
+        for (int j = 0; j < ncols; ++j) {
+            const uint8_t *yc = y_q8_1 + (int64_t)j * stride_col_y_blocks * Q81_BYTES;
+            double acc = 0.0;
+            for (int64_t kb = 0; kb < nb; ++kb) {
+                const uint8_t *sb = W + (r * stride_row_blocks + kb) * Q6K_BYTES;
+                const double d = or_h2f((uint16_t)(sb[208] | (sb[209] << 8)));
+                double sbsum = 0.0;
+                for (int k = 0; k < 8; ++k) {
+                    const uint8_t *blk = yc + (kb * 8 + k) * Q81_BYTES;
+                    const double d8 = or_h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+                    long isum = 0;
+                    for (int h = 0; h < 2; ++h) {
+                        long S = 0;
+                        for (int i = 0; i < 16; ++i) {
+                            const int w = 32 * k + 16 * h + i;
+                            S += (long)q6_value(sb, w) * (int8_t)blk[4 + 16 * h + i];
+                        }
+                        isum += (long)(int8_t)sb[192 + 2 * k + h] * S;
+                    }
+                    sbsum += d8 * (double)isum;
+                }
+                acc += d * sbsum;
+            }
+            dst[(int64_t)j * stride_col_dst + r] = (float)acc;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* RMSNorm ahead of the quantizer                                            */
 /* ------------------------------------------------------------------------ */
 

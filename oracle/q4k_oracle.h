@@ -71,6 +71,13 @@ void or_subblock_sums(const uint8_t *W, int64_t nrows, int64_t K,
 /* Number of OpenMP threads the oracle would use with nthreads <= 0. */
 int or_max_threads(void);
 
+/* Q6_K: dequantized rows and the exact GEMV against q8_1 columns
+ * (kernels/vecdotq.cuh:576-601, :867-890). */
+void or_dequant_q6k(const uint8_t *W, int64_t nrows, int64_t K, int64_t stride_row_blocks, float *out);
+void or_gemv_q6k_q8_1(const uint8_t *W, int64_t nrows, int64_t K, int64_t stride_row_blocks,
+                      const uint8_t *y_q8_1, int64_t stride_col_y_blocks, int ncols, float *dst,
+                      int64_t stride_col_dst, int nthreads);
+
 /* RMSNorm in the library's reduction order: y (ncols x K, dense) from x. */
 float or_rmsnorm_scale(const float *x, int64_t K, float eps);
 void or_rmsnorm(const float *x, int64_t K, int64_t stride_col_x, int ncols, const float *w, float eps,

@@ -128,3 +128,12 @@ def test_rms_norm_quantize_argument_checks(q4k):
     assert L.q4k_rms_norm_quantize_q8_1(256, 64, 64, 64, 9, None, 1e-5, 512, None) == EINVAL     # ncols
     assert L.q4k_rms_norm_quantize_q8_1(256, 64, 64, 64, 1, None, -1.0, 512, None) == EINVAL     # eps
     assert L.q4k_rms_norm_quantize_q8_1(None, 64, 64, 64, 1, None, 1e-5, 512, None) == EINVAL    # null x
+
+
+def test_q6k_argument_checks(q4k):
+    L = q4k.lib()
+    # K not a multiple of 2048, row stride not a multiple of 8 super-blocks
+    assert L.q4k_mul_mat_vec_q6_k(256, 512, 1024, 1024, 8, 1, 4, 1024, 8, None, 0, None) == EINVAL
+    assert L.q4k_mul_mat_vec_q6_k(256, 512, 1024, 2048, 8, 1, 9, 2048, 8, None, 0, None) == EINVAL
+    assert "2048" in L.q4k_last_error().decode() or "% 8" in L.q4k_last_error().decode()
+    assert q4k.lib().q4k_q6_k_workspace_bytes(32000, 4096, 1) > 0
