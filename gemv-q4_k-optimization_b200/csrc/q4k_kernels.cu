@@ -570,6 +570,11 @@ __device__ __forceinline__ void q6_sb(uint32_t a, uint32_t act, RowAccD<NC> &acc
         for (int i = 0; i < 16; ++i) ql[i] = q6_word<MIS>(a + 64 * n, i);
 #pragma unroll
         for (int i = 0; i < 8; ++i) qh[i] = q6_word<MIS>(a + 128 + 32 * n, i);
+        // One column: unsigned 6-bit values (dp4a.u32.s32) and the 16-value
+        // activation sums T0, T1 (dp4a with 0x01010101) for the -32 offset:
+        // fewer operations per weight than the bytewise subtraction, which
+        // pays off once the per-row work is not shared by several columns.
+        constexpr bool kUnsigned = NC == 1;
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
             const int k = 4 * n + jj;
@@ -578,7 +583,7 @@ __device__ __forceinline__ void q6_sb(uint32_t a, uint32_t act, RowAccD<NC> &acc
             for (int i = 0; i < 8; ++i) {
                 const uint32_t lo = (ql[8 * (jj & 1) + i] >> (4 * (jj >> 1))) & 0x0F0F0F0Fu;
                 const uint32_t hi = (jj < 2 ? (qh[i] << (4 - 2 * jj)) : (qh[i] >> (2 * jj - 4))) & 0x30303030u;
-                vi[i] = q6_signed(lo | hi);
+                vi[i] = kUnsigned ? (lo | hi) : q6_signed(lo | hi);
             }
             const uint32_t sw = scw[k >> 1];
             const int sc0 = static_cast<int32_t>(sw << (24 - 16 * (k & 1))) >> 24;
@@ -587,14 +592,36 @@ __device__ __forceinline__ void q6_sb(uint32_t a, uint32_t act, RowAccD<NC> &acc
             for (int c = 0; c < NC; ++c) {
                 const uint32_t ac = act + c * (kQ6AtomSB * kQ6RecPitch);
                 const uint4 q0 = lds128(ac + 32 * k), q1 = lds128(ac + 32 * k + 16);
-                int S0 = dp4a_ss(vi[0], q0.x, 0);
-                S0 = dp4a_ss(vi[1], q0.y, S0);
-                S0 = dp4a_ss(vi[2], q0.z, S0);
-                S0 = dp4a_ss(vi[3], q0.w, S0);
-                int S1 = dp4a_ss(vi[4], q1.x, 0);
-                S1 = dp4a_ss(vi[5], q1.y, S1);
-                S1 = dp4a_ss(vi[6], q1.z, S1);
-                S1 = dp4a_ss(vi[7], q1.w, S1);
+                int S0, S1;
+                if constexpr (kUnsigned) {
+                    S0 = dp4a_us(vi[0], q0.x, 0);
+                    S0 = dp4a_us(vi[1], q0.y, S0);
+                    S0 = dp4a_us(vi[2], q0.z, S0);
+                    S0 = dp4a_us(vi[3], q0.w, S0);
+                    S1 = dp4a_us(vi[4], q1.x, 0);
+                    S1 = dp4a_us(vi[5], q1.y, S1);
+                    S1 = dp4a_us(vi[6], q1.z, S1);
+                    S1 = dp4a_us(vi[7], q1.w, S1);
+                    int T0 = dp4a_us(0x01010101u, q0.x, 0);
+                    T0 = dp4a_us(0x01010101u, q0.y, T0);
+                    T0 = dp4a_us(0x01010101u, q0.z, T0);
+                    T0 = dp4a_us(0x01010101u, q0.w, T0);
+                    int T1 = dp4a_us(0x01010101u, q1.x, 0);
+                    T1 = dp4a_us(0x01010101u, q1.y, T1);
+                    T1 = dp4a_us(0x01010101u, q1.z, T1);
+                    T1 = dp4a_us(0x01010101u, q1.w, T1);
+                    S0 -= 32 * T0;
+                    S1 -= 32 * T1;
+                } else {
+                    S0 = dp4a_ss(vi[0], q0.x, 0);
+                    S0 = dp4a_ss(vi[1], q0.y, S0);
+                    S0 = dp4a_ss(vi[2], q0.z, S0);
+                    S0 = dp4a_ss(vi[3], q0.w, S0);
+                    S1 = dp4a_ss(vi[4], q1.x, 0);
+                    S1 = dp4a_ss(vi[5], q1.y, S1);
+                    S1 = dp4a_ss(vi[6], q1.z, S1);
+                    S1 = dp4a_ss(vi[7], q1.w, S1);
+                }
                 // d8 of block k: the record keeps d8 for even k and d8/16 for odd k
                 const float f = __uint_as_float(lds32(ac + kActMetaOff + 16 * (k >> 1) + 4 * (k & 1)));
                 const double d8 = (k & 1) ? f * 16.0f : f;  // exact (power-of-two factor)
