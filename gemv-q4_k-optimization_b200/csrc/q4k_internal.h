@@ -93,6 +93,11 @@ constexpr int kQ6Rows = 8;
 constexpr int kQ6RowBytes = kQ6AtomSB * kQ6Bytes;  // 1680
 constexpr int kQ6BoxBytes = kQ6Rows * kQ6RowBytes;  // 13440
 constexpr int kQ6RecPitch = 336;
+// Up to this many columns the Q6_K path takes the -32 offset out of the sums
+// (unsigned dp4a and activation sums) instead of out of the bytes.
+#ifndef Q4K_Q6_UNSIGNED_MAX
+#define Q4K_Q6_UNSIGNED_MAX 2
+#endif
 __host__ __device__ constexpr int q6_stage_bytes(int ncols) { return kQ6BoxBytes + ncols * kQ6AtomSB * kQ6RecPitch; }
 __host__ __device__ constexpr int rings_q6(int ncols) {
     return kSmemLimit / (kStages * q6_stage_bytes(ncols)) < kMaxWarps ? kSmemLimit / (kStages * q6_stage_bytes(ncols))

@@ -570,11 +570,11 @@ __device__ __forceinline__ void q6_sb(uint32_t a, uint32_t act, RowAccD<NC> &acc
         for (int i = 0; i < 16; ++i) ql[i] = q6_word<MIS>(a + 64 * n, i);
 #pragma unroll
         for (int i = 0; i < 8; ++i) qh[i] = q6_word<MIS>(a + 128 + 32 * n, i);
-        // One column: unsigned 6-bit values (dp4a.u32.s32) and the 16-value
-        // activation sums T0, T1 (dp4a with 0x01010101) for the -32 offset:
-        // fewer operations per weight than the bytewise subtraction, which
-        // pays off once the per-row work is not shared by several columns.
-        constexpr bool kUnsigned = NC == 1;
+        // Up to two columns: unsigned 6-bit values (dp4a.u32.s32) and the
+        // 16-value activation sums T0, T1 (dp4a with 0x01010101) for the -32
+        // offset: fewer operations per weight than the bytewise subtraction,
+        // which pays off while the per-row work is shared by few columns.
+        constexpr bool kUnsigned = NC <= Q4K_Q6_UNSIGNED_MAX;
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
             const int k = 4 * n + jj;
