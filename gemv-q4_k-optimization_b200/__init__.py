@@ -356,10 +356,25 @@ def batch_workspace_bytes(tasks, ncols: int) -> int:
     return int(lib().q4k_batch_workspace_bytes(tasks, len(tasks), ncols))
 
 
+def _sized_call(fn, tasks, ncols: int, ws: Workspace, stream, size_fn) -> None:
+    """Call a batch entry with the workspace as it is; only when the library
+    answers Q4K_EWORKSPACE is the size asked for, the buffer grown and the call
+    repeated (what a refused call did, zeroing the outputs of K = 0 tasks, is
+    idempotent), so steady-state calls pay one library call, not two."""
+    s = _stream(stream)
+    st = fn(tasks, len(tasks), ncols, ws.ptr, ws.nbytes, s)
+    if st == 5:
+        need = int(size_fn(tasks, len(tasks), ncols))
+        if need > ws.nbytes:
+            ws.ensure(need)
+            st = fn(tasks, len(tasks), ncols, ws.ptr, ws.nbytes, s)
+    _check(st)
+
+
 def gemv_batch(tasks, ncols: int, ws: Workspace, stream=None) -> None:
     """Every task's GEMV in one prep + one persistent GEMV launch."""
-    ws.ensure(batch_workspace_bytes(tasks, ncols))
-    _check(lib().q4k_gemv_batch(tasks, len(tasks), ncols, ws.ptr, ws.nbytes, _stream(stream)))
+    L = lib()
+    _sized_call(L.q4k_gemv_batch, tasks, ncols, ws, stream, L.q4k_batch_workspace_bytes)
 
 
 def _ptr_or_none(t):
@@ -408,8 +423,8 @@ def batch_ex_workspace_bytes(tasks, ncols: int) -> int:
 
 def gemv_batch_ex(tasks, ncols: int, ws: Workspace, stream=None) -> None:
     """Batched launch of tasks with optional fused bias/gate epilogues."""
-    ws.ensure(batch_ex_workspace_bytes(tasks, ncols))
-    _check(lib().q4k_gemv_batch_ex(tasks, len(tasks), ncols, ws.ptr, ws.nbytes, _stream(stream)))
+    L = lib()
+    _sized_call(L.q4k_gemv_batch_ex, tasks, ncols, ws, stream, L.q4k_batch_ex_workspace_bytes)
 
 
 def mul_mat_vec_fused(W, W_gate, x, glu: str = "swiglu", x_bias=None, gate_bias=None, out=None,
@@ -519,8 +534,8 @@ def make_tasks_q6_k(mats: Sequence, xs: Sequence, outs: Sequence):
 
 
 def gemv_batch_q6_k(tasks, ncols: int, ws: Workspace, stream=None) -> None:
-    ws.ensure(int(lib().q4k_batch_q6_k_workspace_bytes(tasks, len(tasks), ncols)))
-    _check(lib().q4k_gemv_batch_q6_k(tasks, len(tasks), ncols, ws.ptr, ws.nbytes, _stream(stream)))
+    L = lib()
+    _sized_call(L.q4k_gemv_batch_q6_k, tasks, ncols, ws, stream, L.q4k_batch_q6_k_workspace_bytes)
 
 
 def gen_q6k_numpy(rng: np.random.Generator, nrows: int, K: int) -> np.ndarray:

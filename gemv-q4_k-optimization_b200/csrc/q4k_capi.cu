@@ -16,6 +16,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 using namespace q4k;
 
@@ -108,7 +109,42 @@ EncodeTiledFn tensor_map_encoder() {
 
 // Weight matrix as a 2D uint32 tensor {nb*36 words, nrows}, row stride in
 // bytes, box {36 words = one super-block, 32 rows}.
+// Encoded tensor maps of recent calls: a pure function of (matrix, shape,
+// stride, format), so calls that reuse their weights (every decode step)
+// skip the driver's encoder.  Per host thread, bounded.
+struct MapKey {
+    const void *W;
+    int64_t nrows, nb, stride;
+    int q6;
+    bool operator==(const MapKey &o) const {
+        return W == o.W && nrows == o.nrows && nb == o.nb && stride == o.stride && q6 == o.q6;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey &k) const {
+        uint64_t h = reinterpret_cast<uintptr_t>(k.W) * 0x9E3779B97F4A7C15ull;
+        h ^= static_cast<uint64_t>(k.nrows) + 0x7F4A7C15ull + (h << 6) + (h >> 2);
+        h ^= static_cast<uint64_t>(k.nb * 131 + k.stride) + (h << 6) + (h >> 2);
+        return static_cast<size_t>(h ^ static_cast<uint64_t>(k.q6));
+    }
+};
+constexpr size_t kMapCacheMax = 4096;
+thread_local std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_map_cache;
+
+bool cached_map(const MapKey &k, CUtensorMap *tm) {
+    auto it = g_map_cache.find(k);
+    if (it == g_map_cache.end()) return false;
+    *tm = it->second;
+    return true;
+}
+void remember_map(const MapKey &k, const CUtensorMap &tm) {
+    if (g_map_cache.size() >= kMapCacheMax) g_map_cache.clear();
+    g_map_cache.emplace(k, tm);
+}
+
 int encode_weight_map(CUtensorMap *tm, const void *W, int64_t nrows, int64_t nb, int64_t row_stride_bytes) {
+    const MapKey key{W, nrows, nb, row_stride_bytes, 0};
+    if (cached_map(key, tm)) return Q4K_OK;
     EncodeTiledFn enc = tensor_map_encoder();
     if (!enc) return fail(Q4K_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(nb * 36), static_cast<cuuint64_t>(nrows)};
@@ -119,6 +155,7 @@ int encode_weight_map(CUtensorMap *tm, const void *W, int64_t nrows, int64_t nb,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(Q4K_ECUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+    remember_map(key, *tm);
     return Q4K_OK;
 }
 
@@ -126,6 +163,8 @@ int encode_weight_map(CUtensorMap *tm, const void *W, int64_t nrows, int64_t nb,
 // 1680 bytes) x 8 rows.  Needs nb % 8 == 0 and a row stride that is a
 // multiple of 16 bytes (stride_row_x % 8 == 0).
 int encode_q6_map(CUtensorMap *tm, const void *W, int64_t nrows, int64_t nb, int64_t row_stride_bytes) {
+    const MapKey key{W, nrows, nb, row_stride_bytes, 1};
+    if (cached_map(key, tm)) return Q4K_OK;
     EncodeTiledFn enc = tensor_map_encoder();
     if (!enc) return fail(Q4K_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(nb * kQ6Bytes / 8), static_cast<cuuint64_t>(nrows)};
@@ -136,6 +175,7 @@ int encode_q6_map(CUtensorMap *tm, const void *W, int64_t nrows, int64_t nb, int
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(Q4K_ECUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+    remember_map(key, *tm);
     return Q4K_OK;
 }
 
@@ -208,7 +248,7 @@ struct Plan {
 
 // Build the schedule (no device memory touched).  ws may be null (sizing).
 int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, Plan &P,
-              int32_t *dump_T = nullptr, bool dump = false) {
+              int32_t *dump_T = nullptr, bool dump = false, size_t ws_bytes = 0) {
     if (njobs < 1 || njobs > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..%d", njobs, kMaxTasks);
     for (int i = 0; i < njobs; ++i) {
         int st = validate_job(jobs[i], ncols, i);
@@ -316,6 +356,8 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.gemv.fused = 0;
     P.gemv.ncols = ncols;
     if (ws == nullptr) return Q4K_OK;
+    if (ws_bytes < P.layout.total)
+        return fail(Q4K_EWORKSPACE, "workspace of %zu bytes < %zu required", ws_bytes, P.layout.total);
 
     // pointers into the workspace
     P.gemv.status = reinterpret_cast<int32_t *>(ws);
@@ -414,8 +456,6 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     int num_sms = 0;
     cudaError_t e = device_setup(&num_sms);
     if (e != cudaSuccess) return cuda_fail(e, "device setup");
-    st = make_plan(jobs, njobs, ncols, nullptr, num_sms, P, nullptr, dump);
-    if (st != Q4K_OK) return st;
     st = zero_outputs(jobs, njobs, ncols, s);
     if (st != Q4K_OK) return st;
     // With a fused all-gather the launch happens even without local rows: the
@@ -424,9 +464,9 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     if (!P.any_work && !gathering) return Q4K_OK;
     if (workspace == nullptr) return fail(Q4K_EWORKSPACE, "workspace is null");
     if (!aligned16(workspace)) return fail(Q4K_EWORKSPACE, "workspace is not 16-byte aligned");
-    if (ws_bytes < P.layout.total)
-        return fail(Q4K_EWORKSPACE, "workspace of %zu bytes < %zu required", ws_bytes, P.layout.total);
-    st = make_plan(jobs, njobs, ncols, static_cast<uint8_t *>(workspace), num_sms, P, dump_T, dump);
+    // The device's plan (its SM count fixes the workers and the layout); the
+    // workspace size is checked before any pointer into it is formed.
+    st = make_plan(jobs, njobs, ncols, static_cast<uint8_t *>(workspace), num_sms, P, dump_T, dump, ws_bytes);
     if (st != Q4K_OK) return st;
     P.gemv.dump_S = dump_S;
     P.gemv.gworld = 1;
