@@ -140,6 +140,9 @@ def lib() -> ctypes.CDLL:
             "q4k_ipc_handle": (None, [_P, ctypes.c_char_p]),
             "q4k_ipc_open": (None, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
             "q4k_ipc_close": (None, [_P]),
+            "q4k_timeline_bytes": (_SZ, []),
+            "q4k_timeline_read": (None, [_P, _SZ, ctypes.POINTER(_I)]),
+            "q4k_timeline_reset": (None, []),
         }
         overridden = "Q4K_LIB" in os.environ
         for name, (res, args) in sigs.items():
@@ -679,3 +682,31 @@ def gemv_batch_allgather(tasks, ncols: int, gather: PeerGather, ws: Workspace, s
     ws.ensure(batch_workspace_bytes(tasks, ncols))
     _check(lib().q4k_gemv_batch_allgather(tasks, len(tasks), ncols, ctypes.byref(gather.desc), ws.ptr, ws.nbytes,
                                           _stream(stream)))
+
+
+# ---------------------------------------------------------------------------
+# launch timeline (diagnostic library built with -DQ4K_TIMELINE=1)
+# ---------------------------------------------------------------------------
+TIMELINE_LIB = HERE / "libq4k_gemv_timeline.so"  # load it with Q4K_LIB=<this path>
+TL_SLOTS, TL_CTAS, TL_PREP_CTAS = 64, 256, 4096  # Q4K_TIMELINE_* in include/q4k_gemv.h
+
+
+def timeline_reset() -> None:
+    _check(lib().q4k_timeline_reset())
+
+
+def timeline_read():
+    """(gemv, prep, ncalls) from a timeline build: gemv u64[slot][CTA][warp][8]
+    = {start, wait return, end, atoms, SM, worker, first atom, end atom} and
+    prep u64[slot][CTA][4] = {start, wait return, end, 1}, in %globaltimer ns;
+    slot = call index since the last reset, modulo TL_SLOTS."""
+    L = lib()
+    nb = int(L.q4k_timeline_bytes())
+    if nb == 0:
+        raise Q4KError(1, f"{LIB_PATH.name} is built without Q4K_TIMELINE (set Q4K_LIB={TIMELINE_LIB})")
+    buf = np.zeros(nb // 8, np.uint64)
+    n = ctypes.c_int(0)
+    _check(L.q4k_timeline_read(buf.ctypes.data, nb, ctypes.byref(n)))
+    ng = TL_SLOTS * TL_CTAS * 16 * 8
+    return (buf[:ng].reshape(TL_SLOTS, TL_CTAS, 16, 8).astype(np.int64),
+            buf[ng:].reshape(TL_SLOTS, TL_PREP_CTAS, 4).astype(np.int64), n.value)

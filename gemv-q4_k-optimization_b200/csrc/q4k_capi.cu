@@ -13,6 +13,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -51,7 +52,8 @@ int num_sms_or_bound() {
     return kFallbackSMs;
 }
 
-// Workspace layout: [status word | pad][counters][partials][activations].
+// Workspace layout: [status word | pad][counters][partials][activations];
+// header bytes 4 (gather), 64 (dynamic tickets) and 128 (grid barrier) hold sync words.
 struct Layout {
     size_t counters_off = 0, partials_off = 0, act_off = 0, total = 0;
 };
@@ -247,8 +249,12 @@ struct Plan {
 };
 
 // Build the schedule (no device memory touched).  ws may be null (sizing).
+// want_dyn: use the dynamically scheduled kernel when the launch qualifies
+// (plain or gated Q4_K tasks whose row groups give every warp of a CTA at
+// least one atom, and at least two row groups per SM); its tasks are ordered
+// by decreasing K.
 int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, Plan &P,
-              int32_t *dump_T = nullptr, bool dump = false, size_t ws_bytes = 0) {
+              int32_t *dump_T = nullptr, bool dump = false, size_t ws_bytes = 0, bool want_dyn = false) {
     if (njobs < 1 || njobs > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..%d", njobs, kMaxTasks);
     for (int i = 0; i < njobs; ++i) {
         int st = validate_job(jobs[i], ncols, i);
@@ -296,12 +302,50 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     if (P.q6 && dump) return fail(Q4K_EINVAL, "no sub-block dump for Q6_K");
     P.r2 = !P.q6 && !dump && !P.any_fused && ncols >= kR2Min && split_for(ncols) == 1;
     P.mode = dump ? kModeDump : P.any_fused ? kModeGated : P.q6 ? kModeQ6 : P.r2 ? kModeR2 : kModePlain;
+    if (want_dyn && !dump && !P.q6) {
+        const bool gated = P.mode == kModeGated;
+        const int R = rings_dyn(ncols, gated);
+        int64_t G = 0, natoms = 0;
+        bool fits = true;
+        for (int i = 0; i < njobs; ++i) {
+            if (P.act_of_job[i] < 0) continue;
+            const int64_t nb = jobs[i].K / Q4K_QK_K;
+            const int64_t apr = (gated && jobs[i].gate) ? nb : (nb + kKS - 1) / kKS;
+            if (apr < R) fits = false;
+            G += (jobs[i].nrows + 31) / 32;
+            natoms += (jobs[i].nrows + 31) / 32 * apr;
+        }
+        // Measured on B200 (chained launches of one 14336 x 4096 matrix, us):
+        // ncols 1 11.8 -> 10.8, 2 13.5 -> 12.5, 4 17.2 -> 17.1, 8 24.5 -> 34.8;
+        // whole Mistral / Llama-3 layers and the 128256-row head 7-12 % slower
+        // (their per-warp streams cut into shares of one or two atoms per
+        // group).  So: one or two columns, and only where the static kernel
+        // spreads fewer than four atoms per worker over the SMs.
+        const bool spread = natoms < 4 * static_cast<int64_t>(num_sms) * rings_for(ncols);
+        if (fits && spread && ncols <= 2 && G >= 2 * static_cast<int64_t>(num_sms) && G < (int64_t{1} << 30)) {
+            P.r2 = false;
+            P.mode = gated ? kModeDynGated : kModeDynPlain;
+        }
+    }
+    const bool dyn = is_dyn(P.mode);
     const int64_t group_rows = P.r2 ? 64 : P.q6 ? kQ6Rows : 32;
+    // task order: as given, or by decreasing K (stable) for the dynamic kernel
+    int ord[kMaxTasks];
+    for (int i = 0; i < njobs; ++i) ord[i] = i;
+    if (dyn) {
+        for (int a = 1; a < njobs; ++a)
+            for (int b = a; b > 0 && jobs[ord[b]].K > jobs[ord[b - 1]].K; --b) {
+                const int tmp = ord[b];
+                ord[b] = ord[b - 1];
+                ord[b - 1] = tmp;
+            }
+    }
     // row groups and atoms
     int64_t atoms = 0, rgs = 0;
     int nt = 0;
     int ngated = 0;
-    for (int i = 0; i < njobs; ++i) {
+    for (int ii = 0; ii < njobs; ++ii) {
+        const int i = ord[ii];
         const Job &j = jobs[i];
         if (P.act_of_job[i] < 0) continue;
         const int64_t groups = (j.nrows + group_rows - 1) / group_rows;
@@ -351,7 +395,7 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.gemv.pad0_ = 0;
     // the epilogue variant keeps gate partials, the two-row one the second row's
     P.gemv.pcols = (P.any_fused || P.r2) ? 2 * ncols : ncols;
-    P.gemv.pad1_ = 0;
+    P.gemv.dyn_groups = dyn ? static_cast<int32_t>(rgs) : 0;
     P.layout = make_layout(rgs, P.gemv.pcols, P.act_bytes, 2 * nw);
     P.gemv.fused = 0;
     P.gemv.ncols = ncols;
@@ -362,10 +406,14 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     // pointers into the workspace
     P.gemv.status = reinterpret_cast<int32_t *>(ws);
     P.gemv.counters = reinterpret_cast<int32_t *>(ws + P.layout.counters_off);
+    // header word 16 (bytes 64..67): the dynamic kernel's ticket counter,
+    // cleared with the header by every quantization launch
+    P.gemv.dyn_claim = reinterpret_cast<int32_t *>(ws + 64);
     P.gemv.partials = reinterpret_cast<float *>(ws + P.layout.partials_off);
     P.gemv.dump_S = nullptr;
     nt = 0;
-    for (int i = 0; i < njobs; ++i) {
+    for (int ii = 0; ii < njobs; ++ii) {
+        const int i = ord[ii];
         if (P.act_of_job[i] < 0) continue;
         const Job &j = jobs[i];
         int st = j.q6 ? encode_q6_map(&P.gemv.tmap[nt], j.W, j.nrows, j.K / Q4K_QK_K, j.stride_row_x * kQ6Bytes)
@@ -442,6 +490,43 @@ int validate_gather(const q4k_gather *g) {
     return Q4K_OK;
 }
 
+#if Q4K_TIMELINE
+// Launch timeline records (one buffer, on the device of the first call).
+std::mutex g_tl_mu;
+unsigned long long *g_tl = nullptr;
+int g_tl_calls = 0;
+constexpr size_t kTlGemvWords = static_cast<size_t>(Q4K_TIMELINE_SLOTS) * Q4K_TIMELINE_CTAS * 16 * 8;
+constexpr size_t kTlPrepWords = static_cast<size_t>(Q4K_TIMELINE_SLOTS) * Q4K_TIMELINE_PREP_CTAS * 4;
+constexpr size_t kTlBytes = (kTlGemvWords + kTlPrepWords) * sizeof(unsigned long long);
+
+// Points the launch parameters at the next ring slot.  The first call
+// allocates and clears the buffer (synchronously: not inside a graph capture).
+int timeline_attach(Plan &P) {
+    std::lock_guard<std::mutex> lk(g_tl_mu);
+    if (g_tl == nullptr) {
+        cudaError_t e = cudaMalloc(&g_tl, kTlBytes);
+        if (e == cudaSuccess) e = cudaMemset(g_tl, 0, kTlBytes);
+        if (e != cudaSuccess) return cuda_fail(e, "timeline buffer");
+    }
+    const int slot = g_tl_calls++ % Q4K_TIMELINE_SLOTS;
+    P.gemv.tl = g_tl;
+    P.gemv.tl_slot = slot;
+    P.prep.tl = g_tl + kTlGemvWords;
+    P.prep.tl_slot = slot;
+    return Q4K_OK;
+}
+#endif
+
+// Q4K_SCHED=static in the environment keeps every launch on the statically
+// partitioned kernel (read once per process).
+bool dyn_schedule_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("Q4K_SCHED");
+        return !(e != nullptr && std::strcmp(e, "static") == 0);
+    }();
+    return on;
+}
+
 // fused: one launch that quantizes the activations itself (fp32 jobs only;
 // the workspace header and counters must be zero on entry, which every
 // completed call leaves them).
@@ -466,7 +551,8 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     if (!aligned16(workspace)) return fail(Q4K_EWORKSPACE, "workspace is not 16-byte aligned");
     // The device's plan (its SM count fixes the workers and the layout); the
     // workspace size is checked before any pointer into it is formed.
-    st = make_plan(jobs, njobs, ncols, static_cast<uint8_t *>(workspace), num_sms, P, dump_T, dump, ws_bytes);
+    st = make_plan(jobs, njobs, ncols, static_cast<uint8_t *>(workspace), num_sms, P, dump_T, dump, ws_bytes,
+                   !fused && !gathering && dyn_schedule_enabled());
     if (st != Q4K_OK) return st;
     P.gemv.dump_S = dump_S;
     P.gemv.gworld = 1;
@@ -481,6 +567,9 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
         P.gemv.gepoch = gather->epoch;
         P.gemv.gdone = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace) + 4);
     }
+#if Q4K_TIMELINE
+    if ((st = timeline_attach(P)) != Q4K_OK) return st;
+#endif
     if (fused) {
         uint8_t *w8 = static_cast<uint8_t *>(workspace);
         P.gemv.fused = 1;
@@ -896,6 +985,48 @@ int q4k_workspace_status(const void *workspace, int *device_status, q4k_stream_t
     if (e != cudaSuccess) return cuda_fail(e, "status read");
     *device_status = v;
     return Q4K_OK;
+}
+
+size_t q4k_timeline_bytes(void) {
+#if Q4K_TIMELINE
+    return kTlBytes;
+#else
+    return 0;
+#endif
+}
+
+int q4k_timeline_read(void *host, size_t bytes, int *ncalls) {
+#if Q4K_TIMELINE
+    if (host == nullptr || bytes > kTlBytes)
+        return fail(Q4K_EINVAL, "timeline read of %zu bytes (at most %zu)", bytes, kTlBytes);
+    std::lock_guard<std::mutex> lk(g_tl_mu);
+    if (ncalls) *ncalls = g_tl_calls;
+    if (g_tl == nullptr) {
+        std::memset(host, 0, bytes);
+        return Q4K_OK;
+    }
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(host, g_tl, bytes, cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? Q4K_OK : cuda_fail(e, "timeline read");
+#else
+    (void)host;
+    (void)bytes;
+    (void)ncalls;
+    return fail(Q4K_EINVAL, "library built without Q4K_TIMELINE");
+#endif
+}
+
+int q4k_timeline_reset(void) {
+#if Q4K_TIMELINE
+    std::lock_guard<std::mutex> lk(g_tl_mu);
+    g_tl_calls = 0;
+    if (g_tl == nullptr) return Q4K_OK;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemset(g_tl, 0, kTlBytes);
+    return e == cudaSuccess ? Q4K_OK : cuda_fail(e, "timeline reset");
+#else
+    return fail(Q4K_EINVAL, "library built without Q4K_TIMELINE");
+#endif
 }
 
 }  // extern "C"

@@ -186,6 +186,13 @@ __device__ __forceinline__ int atom_add_acqrel_gpu(int *p, int v) {
     asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
 }
+// Device-scope fetch-add without ordering: a ticket.  No memory clobber, so the
+// warp runs on until it reads the result.
+__device__ __forceinline__ int atom_add_relaxed_gpu(int *p, int v) {
+    int old;
+    asm volatile("atom.relaxed.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v));
+    return old;
+}
 __device__ __forceinline__ void st_relaxed_gpu(int *p, int v) {
     asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

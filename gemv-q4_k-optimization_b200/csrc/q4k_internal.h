@@ -33,6 +33,10 @@ constexpr int kMaxPeers = 8;
 #ifndef Q4K_KS
 #define Q4K_KS 2
 #endif
+// Launch timeline stamps (diagnostic builds only; q4k_timeline_* in the C-ABI).
+#ifndef Q4K_TIMELINE
+#define Q4K_TIMELINE 0
+#endif
 // Weight boxes are copied with an L2 evict-first policy (read once).
 #ifndef Q4K_WEIGHT_EVICT_FIRST
 #define Q4K_WEIGHT_EVICT_FIRST 1
@@ -74,7 +78,17 @@ static_assert(warps_for(8) * 32 <= 1024, "block too large");
 // Kernel variants: plain, debug dump of the sub-block sums, fused epilogues.
 // kModeR2: plain tasks at ncols >= kR2Min, 64-row groups with two rows per
 // lane (one activation load serves both rows).  kModeQ6: Q6_K weights.
-enum GemvMode : int { kModePlain = 0, kModeDump = 1, kModeGated = 2, kModeR2 = 3, kModeQ6 = 4 };
+// kModeDynPlain / kModeDynGated: the plain and gated arithmetic in the
+// dynamically scheduled kernel (k_gemv_dyn: whole row groups per CTA).
+enum GemvMode : int {
+    kModePlain = 0,
+    kModeDump = 1,
+    kModeGated = 2,
+    kModeR2 = 3,
+    kModeQ6 = 4,
+    kModeDynPlain = 5,
+    kModeDynGated = 6
+};
 #ifndef Q4K_R2_MIN
 #define Q4K_R2_MIN 3
 #endif
@@ -104,15 +118,27 @@ __host__ __device__ constexpr int rings_q6(int ncols) {
                                                                       : kMaxWarps;
 }
 static_assert(rings_q6(8) >= 2, "Q6_K ring too large for 8 columns");
+// Dynamically scheduled launches: one warp per ring, each warp holds a
+// fixed share of every row group's atoms, and the CTA adds the warps' sums in
+// double-buffered shared memory (2 x rings x pcols x 32 floats beside the
+// rings; pcols = 2 * ncols with a gate).
+__host__ __device__ constexpr int dyn_pcols(int ncols, bool gated) { return gated ? 2 * ncols : ncols; }
+__host__ __device__ constexpr int rings_dyn(int ncols, bool gated) {
+    int r = kMaxWarps;
+    while (r > 1 && r * kStages * stage_bytes(ncols) + 2 * r * dyn_pcols(ncols, gated) * 128 > kSmemLimit - 2048) --r;
+    return r;
+}
+static_assert(rings_dyn(8, true) >= 4, "dynamic ring too small for 8 gated columns");
 // Geometry by kernel variant.
+__host__ __device__ constexpr bool is_dyn(int mode) { return mode == kModeDynPlain || mode == kModeDynGated; }
 __host__ __device__ constexpr int stage_bytes_m(int ncols, int mode) {
     return mode == kModeQ6 ? q6_stage_bytes(ncols) : stage_bytes(ncols);
 }
 __host__ __device__ constexpr int rings_m(int ncols, int mode) {
-    return mode == kModeQ6 ? rings_q6(ncols) : rings_for(ncols);
+    return mode == kModeQ6 ? rings_q6(ncols) : is_dyn(mode) ? rings_dyn(ncols, mode == kModeDynGated) : rings_for(ncols);
 }
 __host__ __device__ constexpr int warps_m(int ncols, int mode) {
-    return mode == kModeQ6 ? rings_q6(ncols) : warps_for(ncols);
+    return mode == kModeQ6 ? rings_q6(ncols) : is_dyn(mode) ? rings_dyn(ncols, mode == kModeDynGated) : warps_for(ncols);
 }
 __host__ __device__ constexpr int smem_m(int ncols, int mode) {
     return rings_m(ncols, mode) * kStages * stage_bytes_m(ncols, mode);
@@ -171,7 +197,7 @@ struct GemvParams {
     int32_t *counters;       // one per global row group, zero at kernel start
     float *partials;         // [nworkers][2][pcols][32]
     int32_t pcols;           // columns per partial slot: ncols, or 2*ncols when a task has a gate
-    int32_t pad1_;
+    int32_t dyn_groups;      // dynamically scheduled launches: row groups of all tasks
     int32_t *status;
     int32_t *dump_S;         // debug: sub-block sums (nullptr in the product path)
     // Fused all-gather over peer memory (gworld > 1): every output value is
@@ -189,6 +215,10 @@ struct GemvParams {
     int32_t fused;
     int32_t ncols;
     unsigned long long *bar_arrive;  // grid-barrier arrivals, counts up by gridDim.x per launch
+    int32_t *dyn_claim;              // dynamically scheduled launches: group tickets (zero at kernel start)
+    unsigned long long *tl;          // launch timeline records (Q4K_TIMELINE builds; else nullptr)
+    int32_t tl_slot;
+    int32_t tl_pad_;
 };
 
 enum PrepKind : int32_t { kPrepF32 = 0, kPrepQ81 = 1 };
@@ -223,6 +253,9 @@ struct PrepParams {
     int32_t *zero_ptr;
     int32_t norm_ctas;       // leading CTAs that normalize whole columns (RMSNorm jobs)
     int32_t pad_;
+    unsigned long long *tl;  // launch timeline records (Q4K_TIMELINE builds; else nullptr)
+    int32_t tl_slot;
+    int32_t tl_pad_;
 };
 
 // Launchers (q4k_kernels.cu).  Return cudaSuccess or the launch error.

@@ -21,6 +21,7 @@
 //     scale/min unpacking) and :461-483 (d*sum d8*sc*S - dmin*sum d8*m*T).
 //   row/column strides and output layout: kernels/mmvq.cu:233-247, :285, :337.
 #include "q4k_device.cuh"
+#include "q4k_gemv.h"  // Q4K_TIMELINE_* record geometry
 #include "q4k_internal.h"
 
 #include <mutex>
@@ -102,6 +103,9 @@ __device__ __forceinline__ void prep_norm_column(const PrepJob &J, int col) {
 }
 
 __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams P) {
+#if Q4K_TIMELINE
+    const uint64_t tl_start = globaltimer_ns();
+#endif
     // Let the dependent GEMV grid launch now: it only issues weight copies
     // before its griddepcontrol.wait, which returns after this grid completes.
     pdl_launch_dependents();
@@ -137,6 +141,9 @@ __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams
     // This grid may itself be a programmatic dependent of the previous GEMV
     // launch (which shares the workspace): wait for it before writing.
     pdl_wait();
+#if Q4K_TIMELINE
+    const uint64_t tl_wait = globaltimer_ns();
+#endif
 
     for (int64_t i = tid; i < P.zero_count; i += nthr) P.zero_ptr[i] = 0;
 
@@ -186,6 +193,17 @@ __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams
             write_q8a(J.act + col * J.act_col_stride, b, lane, q, dh, dT);
         }
     }
+#if Q4K_TIMELINE
+    // (the normalizing CTAs returned above: block-uniform, so the barrier is safe)
+    __syncthreads();
+    if (threadIdx.x == 0 && P.tl != nullptr && blockIdx.x < Q4K_TIMELINE_PREP_CTAS) {
+        unsigned long long *o = P.tl + (static_cast<int64_t>(P.tl_slot) * Q4K_TIMELINE_PREP_CTAS + blockIdx.x) * 4;
+        o[0] = tl_start;
+        o[1] = tl_wait;
+        o[2] = globaltimer_ns();
+        o[3] = 1;
+    }
+#endif
 }
 
 // ============================================================================
@@ -1092,6 +1110,9 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
     __shared__ __align__(8) uint64_t empty_bars[kR][kStages];
     __shared__ int cta_cnt[kR];  // arrivals at row groups split between this CTA's workers
 
+#if Q4K_TIMELINE
+    const uint64_t tl_start = globaltimer_ns();
+#endif
     // The next launch on the stream may start now; it waits for this grid's
     // completion before it touches the workspace.
     pdl_launch_dependents();
@@ -1135,6 +1156,9 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
     // returns once it has completed.
     if (active) worker_prologue<NC, MODE>(P, W, lane, full, issuer);
     pdl_wait();
+#if Q4K_TIMELINE
+    const uint64_t tl_wait = globaltimer_ns();
+#endif
     if (P.fused) {
         // Single launch: quantize this CTA's share of the activations, then a
         // grid barrier before any activation copy.  (Issuing the weights after
@@ -1159,7 +1183,297 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
                                              cta_cnt);
         }
     }
+#if Q4K_TIMELINE
+    if (lane == 0 && P.tl != nullptr && blockIdx.x < Q4K_TIMELINE_CTAS && warp < 16) {
+        unsigned long long *o =
+            P.tl + ((static_cast<int64_t>(P.tl_slot) * Q4K_TIMELINE_CTAS + blockIdx.x) * 16 + warp) * 8;
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        o[0] = tl_start;
+        o[1] = tl_wait;
+        o[2] = globaltimer_ns();
+        o[3] = active ? static_cast<unsigned long long>(W.n) : 0ull;
+        o[4] = smid;
+        o[5] = static_cast<unsigned long long>(worker);
+        o[6] = active ? static_cast<unsigned long long>(W.a0) : 0ull;
+        o[7] = active ? static_cast<unsigned long long>(W.a1) : 0ull;
+    }
+#endif
     if (!DUMP && P.gworld > 1) gather_epilogue(P);
+}
+
+// ============================================================================
+// Dynamically scheduled GEMV (kModeDynPlain / kModeDynGated)
+// ============================================================================
+// The unit of work is a whole row group (32 rows x all super-blocks of a
+// task).  Every warp of a CTA takes a fixed share of each group's atoms (warp
+// w: atoms [w*apr/R, (w+1)*apr/R)) through its own ring, and the CTA adds the
+// R warp sums of each row in warp order in shared memory, so a row's result
+// does not depend on which CTA computed it.  CTAs take groups from a global
+// ticket counter (a workspace header word, cleared by the quantization
+// launch): group
+// blockIdx.x first, then claims, a few groups ahead so that the weight
+// copies never wait for a claim.  The host orders the tasks by decreasing K,
+// so the last groups handed out are the shortest (longest-first).  Row groups
+// are never split between CTAs: no device-scope counters, no partials in
+// global memory.
+//
+// Queue of claimed groups: entry k (the CTA's k-th group) sits in slot
+// k % kDynQ; lane 0 of warp 0 fills it and arrives on q_bar[slot], the warps
+// wait for phase k / kDynQ.  The filler is at most kDynAhead entries ahead of
+// its own group, and no warp is more than two groups behind another (a
+// warp's sums for group k + 2 wait until group k's have been added up), so a
+// slot is rewritten only after every warp has read it.
+constexpr int kDynQ = 16;
+constexpr int kDynAhead = 3;
+
+__device__ __forceinline__ void dyn_locate(const GemvParams &P, int gi, int &t, int &g) {
+    t = 0;
+    while (t + 1 < P.ntasks && gi >= P.task[t + 1].rg_base) ++t;
+    g = gi - P.task[t].rg_base;
+}
+
+// One warp's walk over its atoms of the CTA's groups.  A cursor that has
+// passed its last atom of a group reads the next queue entry only when it is
+// used (need): the filler publishes entry k + 2 as it starts group k, which is
+// exactly as far as a warp's copies run ahead of its sums.
+struct DynCursor {
+    int k;      // queue entry (the CTA's k-th group)
+    int gi;     // global row group (-1: no more work)
+    AtomCursor c;
+    int s1;     // end of this warp's atoms in the group
+    bool need;  // the atoms of entry k are done; entry k + 1 is next
+};
+
+template <int R>
+__device__ __forceinline__ void dyn_enter(const GemvParams &P, DynCursor &d, int k, int gi, int warp) {
+    d.k = k;
+    d.gi = gi;
+    d.need = false;
+    if (gi < 0) return;
+    int t, g;
+    dyn_locate(P, gi, t, g);
+    const int apr = P.task[t].apr;
+    d.c = AtomCursor{t, g, warp * apr / R};
+    d.s1 = (warp + 1) * apr / R;
+}
+
+// Entry k of the queue (waits until it is filled).  Entry 0 is static.
+__device__ __forceinline__ int dyn_entry(const int *q_group, const uint64_t *q_bar, int k, bool &ok) {
+    if (k == 0) return static_cast<int>(blockIdx.x);
+    const int slot = k % kDynQ;
+    ok = ok && wait_phase(smem_addr(&q_bar[slot]), static_cast<uint32_t>((k / kDynQ) & 1), kWaitLimitNs);
+    return ok ? q_group[slot] : -1;
+}
+
+// Step past the current atom; at the end of the warp's share mark the cursor.
+__device__ __forceinline__ void dyn_step(DynCursor &d) {
+    if (++d.c.kp == d.s1) d.need = true;
+}
+
+// Move a marked cursor to the next entry (waiting for it to be filled).
+template <int R>
+__device__ __forceinline__ void dyn_resolve(const GemvParams &P, DynCursor &d, const int *q_group,
+                                            const uint64_t *q_bar, int warp, bool &ok) {
+    if (!d.need || d.gi < 0) return;
+    const int gi = dyn_entry(q_group, q_bar, d.k + 1, ok);
+    dyn_enter<R>(P, d, d.k + 1, gi, warp);
+}
+
+template <int NC, int BASE>
+__global__ void __launch_bounds__(rings_dyn(NC, BASE == kModeGated) * 32, 1)
+    k_gemv_dyn(const __grid_constant__ GemvParams P) {
+    constexpr bool GATED = BASE == kModeGated;
+    constexpr int R = rings_dyn(NC, GATED);
+    constexpr int kPC = dyn_pcols(NC, GATED);
+    constexpr int kSB = Stage<NC, BASE>::kBytes;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full_bars[R][kStages];
+    __shared__ __align__(8) uint64_t q_bar[kDynQ];
+    __shared__ __align__(8) uint64_t free_bar[2];
+    __shared__ int q_group[kDynQ];
+    __shared__ int red_cnt[2];
+    __shared__ float part[2][R][kPC][32];
+
+#if Q4K_TIMELINE
+    const uint64_t tl_start = globaltimer_ns();
+#endif
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) {
+        for (int r = 0; r < R; ++r)
+            for (int s = 0; s < kStages; ++s) mbar_init(smem_addr(&full_bars[r][s]), 1);
+        for (int q = 0; q < kDynQ; ++q) mbar_init(smem_addr(&q_bar[q]), 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_addr(&free_bar[b]), 1);
+            red_cnt[b] = 0;
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+    uint32_t full[kStages];
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) full[s] = smem_addr(&full_bars[warp][s]);
+    const uint32_t ring = smem_addr(smem) + static_cast<uint32_t>(warp * kStages * kSB);
+    const int G = P.dyn_groups;
+    const bool producer = warp == 0 && lane == 0;
+    if (producer) {
+        // entry 0 (static) also completes its slot's first phase, so that entry
+        // k always completes phase k / kDynQ of slot k % kDynQ
+        q_group[0] = static_cast<int>(blockIdx.x);
+        mbar_arrive(smem_addr(&q_bar[0]));
+    }
+
+    // Prologue: this warp's first atoms of the static group (read-only weights).
+    bool ok = true;
+    DynCursor ic, cc;
+    dyn_enter<R>(P, ic, 0, static_cast<int>(blockIdx.x) < G ? static_cast<int>(blockIdx.x) : -1, warp);
+    cc = ic;
+    int issued = 0;
+    while (issued < kStages && ic.gi >= 0 && !ic.need) {
+        issue_weights<NC, BASE>(P, ic.c, ring + (issued % kStages) * kSB, full[issued % kStages], lane);
+        ++issued;
+        dyn_step(ic);  // entry 1 is read after the wait
+    }
+    pdl_wait();
+#if Q4K_TIMELINE
+    const uint64_t tl_wait = globaltimer_ns();
+#endif
+    // The first claims: entries 1 .. kDynAhead - 1 in one ticket range.
+    int pend = 0;
+    if (producer) {
+        const int t0 = atom_add_relaxed_gpu(P.dyn_claim, kDynAhead - 1);
+        for (int e = 1; e < kDynAhead; ++e) {
+            const int gi = static_cast<int>(gridDim.x) + t0 + (e - 1);
+            q_group[e] = gi < G ? gi : -1;
+            mbar_arrive(smem_addr(&q_bar[e]));
+        }
+    }
+    int filled = kDynAhead;       // producer: entries published so far
+    bool claiming = true;         // producer: no -1 published yet
+    for (int e = 1; e < kDynAhead && producer; ++e) claiming = claiming && q_group[e] >= 0;
+    // activation records of the prologue atoms (written by the previous grid;
+    // all of them in entry 0)
+    {
+        AtomCursor a = cc.c;
+        for (int i = 0; i < issued; ++i, ++a.kp)
+            issue_acts<NC, BASE>(P, a, ring + (i % kStages) * kSB, full[i % kStages], lane);
+    }
+    // the rest of the ring (when the first group holds fewer atoms than stages)
+    while (ok && issued < kStages) {
+        dyn_resolve<R>(P, ic, q_group, q_bar, warp, ok);
+        if (!ok || ic.gi < 0) break;
+        const int s = issued % kStages;
+        issue_weights<NC, BASE>(P, ic.c, ring + s * kSB, full[s], lane);
+        issue_acts<NC, BASE>(P, ic.c, ring + s * kSB, full[s], lane);
+        ++issued;
+        dyn_step(ic);
+    }
+
+    RowAcc<NC> acc, gacc;
+    RowAccD<NC> dacc;  // unused (Q6_K is statically scheduled)
+    acc.clear();
+    gacc.clear();
+    int done = 0;
+    int group_k = -1;  // producer: last group whose claim duties ran
+    while (ok && cc.gi >= 0) {
+        if (producer && cc.k != group_k) {
+            group_k = cc.k;
+            // publish the ticket drawn one group ago, draw the next one
+            if (claiming && cc.k >= 1) {
+                const int gi = static_cast<int>(gridDim.x) + pend;
+                const int e = filled++;
+                q_group[e % kDynQ] = gi < G ? gi : -1;
+                mbar_arrive(smem_addr(&q_bar[e % kDynQ]));
+                claiming = gi < G;
+            }
+            if (claiming) pend = atom_add_relaxed_gpu(P.dyn_claim, 1);
+        }
+        const int s = done % kStages;
+        ok = wait_phase(full[s], static_cast<uint32_t>((done / kStages) & 1), kWaitLimitNs);
+        if (!ok) break;
+        compute_atom<NC, NC, BASE>(P, cc.c, ring + s * kSB, lane, 0, acc, gacc, dacc);
+        __syncwarp();
+        dyn_resolve<R>(P, ic, q_group, q_bar, warp, ok);
+        if (!ok) break;
+        if (ic.gi >= 0) {
+            fence_proxy_async_smem();
+            issue_weights<NC, BASE>(P, ic.c, ring + s * kSB, full[s], lane);
+            issue_acts<NC, BASE>(P, ic.c, ring + s * kSB, full[s], lane);
+            ++issued;
+            dyn_step(ic);
+        }
+        ++done;
+        if (++cc.c.kp < cc.s1) continue;
+        // This warp's share of group cc.gi is summed: deposit it, and the last
+        // warp to arrive adds the R shares (warp order) and writes the rows.
+        const int b = cc.k & 1;
+        const int use = cc.k >> 1;
+        if (use >= 1) {
+            ok = wait_phase(smem_addr(&free_bar[b]), static_cast<uint32_t>((use - 1) & 1), kWaitLimitNs);
+            if (!ok) break;
+        }
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+            part[b][warp][j][lane] = acc.value(j);
+            if constexpr (GATED) part[b][warp][NC + j][lane] = gacc.value(j);
+        }
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            old = atomicAdd(&red_cnt[b], 1);
+        }
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == R - 1) {
+            __threadfence_block();
+            __syncwarp();
+            const TaskDesc &T = P.task[cc.c.t];
+            const int row = cc.c.g * 32 + lane;
+#pragma unroll
+            for (int j = 0; j < NC; ++j) {
+                float tot = 0.0f, gtot = 0.0f;
+#pragma unroll
+                for (int w = 0; w < R; ++w) {
+                    tot += part[b][w][j][lane];
+                    if constexpr (GATED) gtot += part[b][w][NC + j][lane];
+                }
+                if (row < T.nrows) store_final<GATED>(P, T, j, row, tot, gtot);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                red_cnt[b] = 0;
+                mbar_arrive(smem_addr(&free_bar[b]));
+            }
+        }
+        acc.clear();
+        gacc.clear();
+        const int gi = dyn_entry(q_group, q_bar, cc.k + 1, ok);
+        dyn_enter<R>(P, cc, cc.k + 1, gi, warp);
+    }
+    if (!ok) {
+        if (lane == 0) atomicExch(P.status, kStatusTimeout);
+        // let this warp's copies in flight land (bounded) before leaving
+        for (int i = done; i < issued; ++i)
+            wait_phase(full[i % kStages], static_cast<uint32_t>((i / kStages) & 1), kDrainLimitNs);
+    }
+#if Q4K_TIMELINE
+    if (lane == 0 && P.tl != nullptr && blockIdx.x < Q4K_TIMELINE_CTAS && warp < 16) {
+        unsigned long long *o =
+            P.tl + ((static_cast<int64_t>(P.tl_slot) * Q4K_TIMELINE_CTAS + blockIdx.x) * 16 + warp) * 8;
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        o[0] = tl_start;
+        o[1] = tl_wait;
+        o[2] = globaltimer_ns();
+        o[3] = static_cast<unsigned long long>(done > 0 ? done : 1);
+        o[4] = smid;
+        o[5] = static_cast<unsigned long long>(blockIdx.x * R + warp);
+        o[6] = 0;
+        o[7] = static_cast<unsigned long long>(cc.k);
+    }
+#endif
 }
 
 // ============================================================================
@@ -1189,6 +1503,40 @@ cudaError_t set_attrs_all() {
     if ((e = set_attrs<6, MODE>()) != cudaSuccess) return e;
     if ((e = set_attrs<7, MODE>()) != cudaSuccess) return e;
     return set_attrs<8, MODE>();
+}
+
+template <int NC, int BASE>
+cudaError_t set_attrs_dyn1() {
+    return cudaFuncSetAttribute(k_gemv_dyn<NC, BASE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                smem_m(NC, BASE == kModeGated ? kModeDynGated : kModeDynPlain));
+}
+
+template <int BASE>
+cudaError_t set_attrs_dyn() {
+    cudaError_t e;
+    if ((e = set_attrs_dyn1<1, BASE>()) != cudaSuccess) return e;
+    if ((e = set_attrs_dyn1<2, BASE>()) != cudaSuccess) return e;
+    if ((e = set_attrs_dyn1<3, BASE>()) != cudaSuccess) return e;
+    if ((e = set_attrs_dyn1<4, BASE>()) != cudaSuccess) return e;
+    if ((e = set_attrs_dyn1<5, BASE>()) != cudaSuccess) return e;
+    if ((e = set_attrs_dyn1<6, BASE>()) != cudaSuccess) return e;
+    if ((e = set_attrs_dyn1<7, BASE>()) != cudaSuccess) return e;
+    return set_attrs_dyn1<8, BASE>();
+}
+
+template <int BASE>
+void *gemv_fn_dyn(int ncols) {
+    switch (ncols) {
+        case 1: return reinterpret_cast<void *>(k_gemv_dyn<1, BASE>);
+        case 2: return reinterpret_cast<void *>(k_gemv_dyn<2, BASE>);
+        case 3: return reinterpret_cast<void *>(k_gemv_dyn<3, BASE>);
+        case 4: return reinterpret_cast<void *>(k_gemv_dyn<4, BASE>);
+        case 5: return reinterpret_cast<void *>(k_gemv_dyn<5, BASE>);
+        case 6: return reinterpret_cast<void *>(k_gemv_dyn<6, BASE>);
+        case 7: return reinterpret_cast<void *>(k_gemv_dyn<7, BASE>);
+        case 8: return reinterpret_cast<void *>(k_gemv_dyn<8, BASE>);
+        default: return nullptr;
+    }
 }
 
 // The two-row variant exists for ncols >= kR2Min only.
@@ -1244,6 +1592,8 @@ cudaError_t device_setup(int *num_sms) {
         if ((e = set_attrs_all<kModeGated>()) != cudaSuccess) return e;
         if ((e = set_attrs_r2()) != cudaSuccess) return e;
         if ((e = set_attrs_all<kModeQ6>()) != cudaSuccess) return e;
+        if ((e = set_attrs_dyn<kModePlain>()) != cudaSuccess) return e;
+        if ((e = set_attrs_dyn<kModeGated>()) != cudaSuccess) return e;
         st.ready = true;
     }
     *num_sms = st.num_sms;
@@ -1277,6 +1627,8 @@ cudaError_t launch_gemv(const GemvParams &p, int ncols, int mode, int grid, cuda
                : mode == kModeGated ? gemv_fn<kModeGated>(ncols)
                : mode == kModeR2    ? gemv_fn_r2(ncols)
                : mode == kModeQ6    ? gemv_fn<kModeQ6>(ncols)
+               : mode == kModeDynPlain ? gemv_fn_dyn<kModePlain>(ncols)
+               : mode == kModeDynGated ? gemv_fn_dyn<kModeGated>(ncols)
                                     : gemv_fn<kModePlain>(ncols);
     if (fn == nullptr) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};

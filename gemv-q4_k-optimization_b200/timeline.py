@@ -1,0 +1,161 @@
+"""Launch timeline of a decode step: where the time between the weight
+streams goes.
+
+Runs one of bench.py's Q4_K workloads through q4k_gemv_batch with the
+timeline build of the library (libq4k_gemv_timeline.so, `make timeline`),
+captured in one CUDA graph and replayed, and summarises the device-clock
+stamps every launch leaves (include/q4k_gemv.h, q4k_timeline_*):
+
+  per launch   quantization launch: release after the previous GEMV's end,
+               run time; GEMV: release after the quantization launch, the
+               spread of the workers' end times after the release
+  per ring     mean end of the workers of each ring slot of a CTA
+  per CTA      mean end by CTA index (CTAs are dispatched in index order)
+
+    python gemv-q4_k-optimization_b200/timeline.py --config 2 [--ncols N] [--reverse] [--json] [--save F.npz]
+
+The reference's own tracing was Nsight plus in-kernel clock64 probes left
+commented out (w_tile.cu:76-122); this is the same question asked of the
+persistent launch chain.  Plain Q4_K batches only (the quantization launch
+and k_gemv); numbers are from the timeline build, whose stamps cost a few
+stores per warp.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent
+os.environ.setdefault("Q4K_LIB", str(HERE / "libq4k_gemv_timeline.so"))
+sys.path.insert(0, str(ROOT))
+
+
+def build_step(q4k, bench, torch, cfg: str, ncols: int, reverse: bool, dev):
+    _, groups = bench.build_groups(cfg, bench.WORKLOADS[cfg][2])
+    if any(glu for grp in groups for *_, glu in map(bench.ent, grp)):
+        raise SystemExit(f"config {cfg}: plain Q4_K batches only")
+    if reverse:
+        groups = [list(reversed(g)) for g in groups]
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    launches = []
+    for grp in groups:
+        xs, Ws, xl, outs = {}, [], [], []
+        for _, rows, K, a, _ in map(bench.ent, grp):
+            if a not in xs:
+                xs[a] = torch.randn((ncols, K), device=dev, generator=g)
+            Ws.append(q4k.gen_q4k_torch(rows, K, generator=g, device=dev))
+            xl.append(xs[a])
+            outs.append(torch.empty((ncols, rows), device=dev))
+        launches.append(dict(tasks=q4k.make_tasks(Ws, xl, outs), keep=(Ws, xs, outs),
+                             names=[e[0] for e in grp]))
+    return launches
+
+
+def summarize(G, Pr, n):
+    """Per-launch and aggregate figures (us) from the records of slots 0..n-1."""
+    per = []
+    for i in range(n):
+        cta, warp = np.nonzero(G[i][:, :, 3] > 0)
+        w = G[i][cta, warp]
+        p = Pr[i][Pr[i][:, 3] == 1]
+        if len(w) == 0 or len(p) == 0:
+            raise SystemExit(f"launch {i}: no records (was the timeline library loaded?)")
+        rel = w[:, 1].min()
+        per.append(dict(prep_release=p[:, 1].min(), prep_end=p[:, 2].max(), gemv_release=rel,
+                        gemv_end=w[:, 2].max(), ends=np.sort(w[:, 2] - rel) / 1e3,
+                        end=(w[:, 2] - rel) / 1e3, cta=cta, warp=warp))
+    rows = []
+    for i in range(1, n):
+        a, b = per[i - 1], per[i]
+        rows.append(dict(
+            launch=i,
+            period=(b["gemv_end"] - a["gemv_end"]) / 1e3,
+            prev_end_to_prep_release=(b["prep_release"] - a["gemv_end"]) / 1e3,
+            prep_run=(b["prep_end"] - b["prep_release"]) / 1e3,
+            prep_end_to_gemv_release=(b["gemv_release"] - b["prep_end"]) / 1e3,
+            end_p10=float(np.percentile(b["ends"], 10)), end_p50=float(np.percentile(b["ends"], 50)),
+            end_p90=float(np.percentile(b["ends"], 90)), end_max=float(b["ends"][-1])))
+    keys = [k for k in rows[0] if k != "launch"]
+    mean = {k: float(np.mean([r[k] for r in rows])) for k in keys}
+    # worker end times by warp (ring slot of the CTA) and by CTA index, launches 1..n-1
+    end = np.concatenate([r["end"] for r in per[1:]])
+    warp = np.concatenate([r["warp"] for r in per[1:]])
+    cta = np.concatenate([r["cta"] for r in per[1:]])
+    ring = {int(k): float(end[warp == k].mean()) for k in np.unique(warp)}
+    ncta = int(cta.max()) + 1
+    bins = {}
+    for lo in range(0, ncta, 16):
+        m = (cta >= lo) & (cta < lo + 16)
+        bins[f"{lo}-{min(lo + 16, ncta) - 1}"] = float(end[m].mean())
+    return rows, mean, ring, bins
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--config", default="2")
+    ap.add_argument("--ncols", type=int, default=1)
+    ap.add_argument("--reverse", action="store_true", help="reverse the task order inside each launch")
+    ap.add_argument("--replays", type=int, default=3)
+    ap.add_argument("--json", action="store_true", help="print one JSON line instead of tables")
+    ap.add_argument("--save", default=None, help="also write the raw records of the step (.npz)")
+    args = ap.parse_args()
+
+    import torch
+    import bench
+    q4k = bench.load_package()
+    if q4k.lib().q4k_timeline_bytes() == 0:
+        raise SystemExit(f"{q4k.LIB_PATH} is not a timeline build (make -C {HERE} timeline)")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    launches = build_step(q4k, bench, torch, args.config, args.ncols, args.reverse, dev)
+    if len(launches) > q4k.TL_SLOTS:
+        raise SystemExit(f"{len(launches)} launches per step > {q4k.TL_SLOTS} timeline slots")
+    ws = q4k.Workspace(max(q4k.batch_workspace_bytes(L["tasks"], args.ncols) for L in launches), dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for L in launches:
+            q4k.gemv_batch(L["tasks"], args.ncols, ws, stream=stream)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(dev)
+    q4k.timeline_reset()  # the graph's launches take slots 0..n-1
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(args.replays):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    G, Pr, ncalls = q4k.timeline_read()
+    n = len(launches)
+    if args.save:
+        np.savez_compressed(args.save, gemv=G[:n], prep=Pr[:n])
+    rows, mean, ring, cta = summarize(G, Pr, n)
+    out = {"config": args.config, "ncols": args.ncols, "reverse": args.reverse, "launches": n,
+           "mean_us": {k: round(v, 3) for k, v in mean.items()},
+           "ring_mean_end_us": {k: round(v, 3) for k, v in ring.items()},
+           "cta_mean_end_us": {k: round(v, 3) for k, v in cta.items()}}
+    if args.json:
+        print(json.dumps(out))
+        return
+    print(f"config {args.config}, ncols {args.ncols}, {n} launches per step, graph replay; us")
+    print("launch  period  GEMVend->prepRel  prepRun  prepEnd->GEMVrel  worker end after release: p10 p50 p90 max")
+    for r in rows:
+        print(f"{r['launch']:6d} {r['period']:7.2f} {r['prev_end_to_prep_release']:17.2f} {r['prep_run']:8.2f} "
+              f"{r['prep_end_to_gemv_release']:17.2f}   {r['end_p10']:6.2f} {r['end_p50']:6.2f} "
+              f"{r['end_p90']:6.2f} {r['end_max']:6.2f}")
+    print("mean   " + "  ".join(f"{k} {v:.2f}" for k, v in mean.items()))
+    print("mean worker end by ring slot: " + "  ".join(f"{k}:{v:.2f}" for k, v in ring.items()))
+    print("mean worker end by CTA index: " + "  ".join(f"{k}:{v:.2f}" for k, v in cta.items()))
+
+
+if __name__ == "__main__":
+    main()

@@ -343,6 +343,29 @@ Q4K_API int q4k_debug_subblock_sums(const void *W, const void *y_q8_1, int64_t K
  * otherwise a q4k_status such as Q4K_ETIMEOUT).  Synchronises the stream. */
 Q4K_API int q4k_workspace_status(const void *workspace, int *device_status, q4k_stream_t stream);
 
+/* Launch timeline (diagnostics).  A library built with -DQ4K_TIMELINE=1
+ * (make timeline: libq4k_gemv_timeline.so) stamps the device clock
+ * (%globaltimer, ns) in every GEMV launch, per CTA and warp, at three points:
+ * the warp starts, its griddepcontrol.wait returns, it has flushed its last
+ * row group; and in every quantization launch, per CTA: start, wait return,
+ * end.  Records go to a ring of Q4K_TIMELINE_SLOTS launches in a device
+ * buffer of the current device (allocated at the first call), slot = call
+ * index modulo the ring, reset by q4k_timeline_reset:
+ *   GEMV  u64[slot][Q4K_TIMELINE_CTAS][16 warps][8] =
+ *         {start, wait return, end, atoms of the worker (0: idle), SM id,
+ *          worker index, first atom, end atom}
+ *   prep  u64[slot][Q4K_TIMELINE_PREP_CTAS][4] = {start, wait return, end, 1}
+ * q4k_timeline_bytes() is the size of both regions (GEMV first); it returns 0
+ * and the other two Q4K_EINVAL in a library built without the option. */
+#define Q4K_TIMELINE_SLOTS 64
+#define Q4K_TIMELINE_CTAS 256
+#define Q4K_TIMELINE_PREP_CTAS 4096
+Q4K_API size_t q4k_timeline_bytes(void);
+/* Copies the records (bytes <= q4k_timeline_bytes()) after a device
+ * synchronisation; *ncalls = calls recorded since the last reset. */
+Q4K_API int q4k_timeline_read(void *host, size_t bytes, int *ncalls);
+Q4K_API int q4k_timeline_reset(void);
+
 #ifdef __cplusplus
 }
 #endif

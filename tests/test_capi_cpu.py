@@ -137,3 +137,23 @@ def test_q6k_argument_checks(q4k):
     assert L.q4k_mul_mat_vec_q6_k(256, 512, 1024, 2048, 8, 1, 9, 2048, 8, None, 0, None) == EINVAL
     assert "2048" in L.q4k_last_error().decode() or "% 8" in L.q4k_last_error().decode()
     assert q4k.lib().q4k_q6_k_workspace_bytes(32000, 4096, 1) > 0
+
+
+def test_timeline_entry_points(q4k):
+    """The product library carries the timeline API but no stamps; the
+    diagnostic build (make timeline) sizes its record ring."""
+    L = q4k.lib()
+    assert L.q4k_timeline_bytes() == 0
+    n = ctypes.c_int(-1)
+    buf = ctypes.create_string_buffer(64)
+    assert L.q4k_timeline_read(buf, 64, ctypes.byref(n)) == EINVAL
+    assert L.q4k_timeline_reset() == EINVAL
+    tl_path = q4k.TIMELINE_LIB
+    if not tl_path.exists():
+        pytest.skip("timeline library not built")
+    T = ctypes.CDLL(str(tl_path))
+    T.q4k_timeline_bytes.restype = ctypes.c_size_t
+    want = (q4k.TL_SLOTS * q4k.TL_CTAS * 16 * 8 + q4k.TL_SLOTS * q4k.TL_PREP_CTAS * 4) * 8
+    assert T.q4k_timeline_bytes() == want
+    T.q4k_timeline_read.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int)]
+    assert T.q4k_timeline_read(None, 8, ctypes.byref(n)) == EINVAL  # null destination

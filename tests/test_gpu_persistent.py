@@ -94,19 +94,28 @@ def test_persistent_equals_two_launch_path_and_oracle(q4k, oracle, torch_mod, de
 
 
 @pytest.mark.parametrize("ncols", [1, 4])
-def test_persistent_full_layer_bitwise(q4k, torch_mod, dev, ncols):
-    """A whole 7-matrix decoder layer at full size: identical to the two-launch path."""
+def test_persistent_full_layer(q4k, oracle, torch_mod, dev, ncols):
+    """A whole 7-matrix decoder layer at full size through the single-launch
+    path, three times: bit-identical calls, every row at the parity bar.  The
+    two-launch path runs this layer on the dynamically scheduled kernel, whose
+    per-row sums are split differently (eight warp shares per row group), so
+    the two agree to the parity bar, not bit for bit."""
     torch = torch_mod
     _, Wd, xs = layer(q4k, torch, dev, 7, MISTRAL, MISTRAL_X, ncols, on_device=True)
     a = [torch.empty((ncols, r), device=dev) for r, _ in MISTRAL]
-    b = [torch.empty((ncols, r), device=dev) for r, _ in MISTRAL]
     ws_a, ws_b = q4k.Workspace(), q4k.Workspace()
     q4k.gemv_batch(q4k.make_tasks(Wd, xs, a), ncols, ws_a)
+    runs = []
     for _ in range(3):
+        b = [torch.empty((ncols, r), device=dev) for r, _ in MISTRAL]
         q4k.gemv_batch_persistent(q4k.make_tasks(Wd, xs, b), ncols, ws_b)
-    for i, (oa, ob) in enumerate(zip(a, b)):
-        assert torch.equal(oa, ob), f"task {i}"
-    assert ws_b.status() == 0
+        runs.append(b)
+    for i in range(len(MISTRAL)):
+        assert torch.equal(runs[0][i], runs[1][i]) and torch.equal(runs[0][i], runs[2][i]), f"task {i}"
+        want = oracle.gemv_f32(Wd[i].cpu().numpy(), xs[i].cpu().numpy())
+        assert_close(runs[0][i].cpu().numpy(), want, f"task {i} single launch")
+        assert_close(a[i].cpu().numpy(), want, f"task {i} two launches")
+    assert ws_b.status() == 0 and ws_a.status() == 0
     assert control_words_zero(ws_b, n_rowgroups(MISTRAL, ncols))
 
 

@@ -1,0 +1,33 @@
+"""The launch-timeline diagnostic (gemv-q4_k-optimization_b200/timeline.py
+over the Q4K_TIMELINE build): one small chained workload, recorded from a CUDA
+graph replay, gives a sane record for every launch."""
+from __future__ import annotations
+
+import json
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def test_timeline_records_every_launch(q4k):
+    if not q4k.TIMELINE_LIB.exists():
+        pytest.skip("timeline library not built (make -C gemv-q4_k-optimization_b200 timeline)")
+    script = q4k.HERE / "timeline.py"
+    env = {"Q4K_LIB": str(q4k.TIMELINE_LIB)}
+    import os
+    env = {**os.environ, **env}
+    out = subprocess.run([sys.executable, str(script), "--config", "1", "--json"], capture_output=True,
+                         text=True, env=env, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads(out.stdout.strip().splitlines()[-1])
+    assert d["launches"] == 48
+    m = d["mean_us"]
+    # a 4096x4096 launch streams 9.4 MB: a period of microseconds, workers
+    # ending after their release, the quantization launch in between
+    assert 1.0 < m["period"] < 100.0
+    assert 0.0 < m["end_p10"] <= m["end_p50"] <= m["end_p90"] <= m["end_max"] < m["period"] + 5
+    assert 0.0 <= m["prep_run"] < m["period"]
+    assert len(d["ring_mean_end_us"]) >= 1 and len(d["cta_mean_end_us"]) >= 1
