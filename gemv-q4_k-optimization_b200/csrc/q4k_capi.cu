@@ -249,6 +249,20 @@ struct Plan {
 };
 
 // Build the schedule (no device memory touched).  ws may be null (sizing).
+// Q4K_SCHED (read once per process): "static" keeps every launch on the
+// statically partitioned kernel; "dynamic" uses the dynamically scheduled one
+// wherever it can run (for measurements); unset or anything else: the
+// measured choice.
+int dyn_schedule_mode() {
+    static const int mode = [] {
+        const char *e = std::getenv("Q4K_SCHED");
+        if (e != nullptr && std::strcmp(e, "static") == 0) return 0;
+        if (e != nullptr && std::strcmp(e, "dynamic") == 0) return 2;
+        return 1;
+    }();
+    return mode;
+}
+
 // want_dyn: use the dynamically scheduled kernel when the launch qualifies
 // (plain or gated Q4_K tasks whose row groups give every warp of a CTA at
 // least one atom, and at least two row groups per SM); its tasks are ordered
@@ -322,7 +336,9 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         // group).  So: one or two columns, and only where the static kernel
         // spreads fewer than four atoms per worker over the SMs.
         const bool spread = natoms < 4 * static_cast<int64_t>(num_sms) * rings_for(ncols);
-        if (fits && spread && ncols <= 2 && G >= 2 * static_cast<int64_t>(num_sms) && G < (int64_t{1} << 30)) {
+        const bool measured_win = spread && ncols <= 2;
+        if (fits && (measured_win || dyn_schedule_mode() == 2) && G >= 2 * static_cast<int64_t>(num_sms) &&
+            G < (int64_t{1} << 30)) {
             P.r2 = false;
             P.mode = gated ? kModeDynGated : kModeDynPlain;
         }
@@ -517,15 +533,6 @@ int timeline_attach(Plan &P) {
 }
 #endif
 
-// Q4K_SCHED=static in the environment keeps every launch on the statically
-// partitioned kernel (read once per process).
-bool dyn_schedule_enabled() {
-    static const bool on = [] {
-        const char *e = std::getenv("Q4K_SCHED");
-        return !(e != nullptr && std::strcmp(e, "static") == 0);
-    }();
-    return on;
-}
 
 // fused: one launch that quantizes the activations itself (fp32 jobs only;
 // the workspace header and counters must be zero on entry, which every
@@ -552,7 +559,7 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     // The device's plan (its SM count fixes the workers and the layout); the
     // workspace size is checked before any pointer into it is formed.
     st = make_plan(jobs, njobs, ncols, static_cast<uint8_t *>(workspace), num_sms, P, dump_T, dump, ws_bytes,
-                   !fused && !gathering && dyn_schedule_enabled());
+                   !fused && !gathering && dyn_schedule_mode() != 0);
     if (st != Q4K_OK) return st;
     P.gemv.dump_S = dump_S;
     P.gemv.gworld = 1;
