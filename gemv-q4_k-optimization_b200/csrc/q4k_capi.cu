@@ -337,7 +337,7 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         // spreads fewer than four atoms per worker over the SMs.
         const bool spread = natoms < 4 * static_cast<int64_t>(num_sms) * rings_for(ncols);
         const bool measured_win = spread && ncols <= 2;
-        if (fits && (measured_win || dyn_schedule_mode() == 2) && G >= 2 * static_cast<int64_t>(num_sms) &&
+        if (fits && (measured_win || dyn_schedule_mode() == 2) && G >= kDynAhead * static_cast<int64_t>(num_sms) &&
             G < (int64_t{1} << 30)) {
             P.r2 = false;
             P.mode = gated ? kModeDynGated : kModeDynPlain;

@@ -129,6 +129,11 @@ __host__ __device__ constexpr int rings_dyn(int ncols, bool gated) {
     return r;
 }
 static_assert(rings_dyn(8, true) >= 4, "dynamic ring too small for 8 gated columns");
+// Queue of a CTA's row groups: kDynQ slots; entries 0 .. kDynAhead-1 are
+// static (blockIdx.x + k * gridDim.x), later ones claimed kDynAhead - 1
+// groups ahead.
+constexpr int kDynQ = 16;
+constexpr int kDynAhead = 3;
 // Geometry by kernel variant.
 __host__ __device__ constexpr bool is_dyn(int mode) { return mode == kModeDynPlain || mode == kModeDynGated; }
 __host__ __device__ constexpr int stage_bytes_m(int ncols, int mode) {

@@ -1211,10 +1211,11 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
 // R warp sums of each row in warp order in shared memory, so a row's result
 // does not depend on which CTA computed it.  CTAs take groups from a global
 // ticket counter (a workspace header word, cleared by the quantization
-// launch): group
-// blockIdx.x first, then claims, a few groups ahead so that the weight
-// copies never wait for a claim.  The host orders the tasks by decreasing K,
-// so the last groups handed out are the shortest (longest-first).  Row groups
+// launch): groups blockIdx.x + k * gridDim.x for its first kDynAhead
+// entries (their weight copies can start before griddepcontrol.wait), then
+// claims, published two groups ahead so that the weight copies never wait for
+// a claim.  The host orders the tasks by decreasing K, so the last groups
+// handed out are the shortest (longest-first).  Row groups
 // are never split between CTAs: no device-scope counters, no partials in
 // global memory.
 //
@@ -1224,8 +1225,6 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
 // its own group, and no warp is more than two groups behind another (a
 // warp's sums for group k + 2 wait until group k's have been added up), so a
 // slot is rewritten only after every warp has read it.
-constexpr int kDynQ = 16;
-constexpr int kDynAhead = 3;
 
 __device__ __forceinline__ void dyn_locate(const GemvParams &P, int gi, int &t, int &g) {
     t = 0;
@@ -1258,9 +1257,13 @@ __device__ __forceinline__ void dyn_enter(const GemvParams &P, DynCursor &d, int
     d.s1 = (warp + 1) * apr / R;
 }
 
-// Entry k of the queue (waits until it is filled).  Entry 0 is static.
-__device__ __forceinline__ int dyn_entry(const int *q_group, const uint64_t *q_bar, int k, bool &ok) {
-    if (k == 0) return static_cast<int>(blockIdx.x);
+// Entry k of the queue (waits until it is filled).  Entries below kDynAhead
+// are static: group blockIdx.x + k * gridDim.x.
+__device__ __forceinline__ int dyn_entry(const int *q_group, const uint64_t *q_bar, int k, int G, bool &ok) {
+    if (k < kDynAhead) {
+        const int gi = static_cast<int>(blockIdx.x + k * gridDim.x);
+        return gi < G ? gi : -1;
+    }
     const int slot = k % kDynQ;
     ok = ok && wait_phase(smem_addr(&q_bar[slot]), static_cast<uint32_t>((k / kDynQ) & 1), kWaitLimitNs);
     return ok ? q_group[slot] : -1;
@@ -1276,7 +1279,7 @@ template <int R>
 __device__ __forceinline__ void dyn_resolve(const GemvParams &P, DynCursor &d, const int *q_group,
                                             const uint64_t *q_bar, int warp, bool &ok) {
     if (!d.need || d.gi < 0) return;
-    const int gi = dyn_entry(q_group, q_bar, d.k + 1, ok);
+    const int gi = dyn_entry(q_group, q_bar, d.k + 1, P.dyn_groups, ok);
     dyn_enter<R>(P, d, d.k + 1, gi, warp);
 }
 
@@ -1319,47 +1322,41 @@ __global__ void __launch_bounds__(rings_dyn(NC, BASE == kModeGated) * 32, 1)
     const int G = P.dyn_groups;
     const bool producer = warp == 0 && lane == 0;
     if (producer) {
-        // entry 0 (static) also completes its slot's first phase, so that entry
-        // k always completes phase k / kDynQ of slot k % kDynQ
-        q_group[0] = static_cast<int>(blockIdx.x);
-        mbar_arrive(smem_addr(&q_bar[0]));
+        // the static entries also complete their slots' first phases, so that
+        // entry k always completes phase k / kDynQ of slot k % kDynQ
+        for (int e = 0; e < kDynAhead; ++e) {
+            bool unused = true;
+            q_group[e] = dyn_entry(q_group, q_bar, e, G, unused);
+            mbar_arrive(smem_addr(&q_bar[e]));
+        }
     }
 
-    // Prologue: this warp's first atoms of the static group (read-only weights).
+    // Prologue: this warp's first atoms of the static groups (read-only weights).
     bool ok = true;
     DynCursor ic, cc;
-    dyn_enter<R>(P, ic, 0, static_cast<int>(blockIdx.x) < G ? static_cast<int>(blockIdx.x) : -1, warp);
+    dyn_enter<R>(P, ic, 0, dyn_entry(q_group, q_bar, 0, G, ok), warp);
     cc = ic;
     int issued = 0;
-    while (issued < kStages && ic.gi >= 0 && !ic.need) {
+    AtomCursor pro[kStages];
+    while (issued < kStages) {
+        if (ic.need && ic.k + 1 >= kDynAhead) break;      // a claimed entry: after the wait
+        dyn_resolve<R>(P, ic, q_group, q_bar, warp, ok);  // static entries: no wait
+        if (ic.gi < 0 || ic.k >= kDynAhead) break;
+        pro[issued] = ic.c;
         issue_weights<NC, BASE>(P, ic.c, ring + (issued % kStages) * kSB, full[issued % kStages], lane);
         ++issued;
-        dyn_step(ic);  // entry 1 is read after the wait
+        dyn_step(ic);
     }
     pdl_wait();
 #if Q4K_TIMELINE
     const uint64_t tl_wait = globaltimer_ns();
 #endif
-    // The first claims: entries 1 .. kDynAhead - 1 in one ticket range.
     int pend = 0;
-    if (producer) {
-        const int t0 = atom_add_relaxed_gpu(P.dyn_claim, kDynAhead - 1);
-        for (int e = 1; e < kDynAhead; ++e) {
-            const int gi = static_cast<int>(gridDim.x) + t0 + (e - 1);
-            q_group[e] = gi < G ? gi : -1;
-            mbar_arrive(smem_addr(&q_bar[e]));
-        }
-    }
     int filled = kDynAhead;       // producer: entries published so far
-    bool claiming = true;         // producer: no -1 published yet
-    for (int e = 1; e < kDynAhead && producer; ++e) claiming = claiming && q_group[e] >= 0;
-    // activation records of the prologue atoms (written by the previous grid;
-    // all of them in entry 0)
-    {
-        AtomCursor a = cc.c;
-        for (int i = 0; i < issued; ++i, ++a.kp)
-            issue_acts<NC, BASE>(P, a, ring + (i % kStages) * kSB, full[i % kStages], lane);
-    }
+    bool claiming = producer && dyn_entry(q_group, q_bar, kDynAhead - 1, G, ok) >= 0;
+    // activation records of the prologue atoms (written by the previous grid)
+    for (int i = 0; i < issued; ++i)
+        issue_acts<NC, BASE>(P, pro[i], ring + (i % kStages) * kSB, full[i % kStages], lane);
     // the rest of the ring (when the first group holds fewer atoms than stages)
     while (ok && issued < kStages) {
         dyn_resolve<R>(P, ic, q_group, q_bar, warp, ok);
@@ -1382,7 +1379,7 @@ __global__ void __launch_bounds__(rings_dyn(NC, BASE == kModeGated) * 32, 1)
             group_k = cc.k;
             // publish the ticket drawn one group ago, draw the next one
             if (claiming && cc.k >= 1) {
-                const int gi = static_cast<int>(gridDim.x) + pend;
+                const int gi = static_cast<int>(gridDim.x) * kDynAhead + pend;
                 const int e = filled++;
                 q_group[e % kDynQ] = gi < G ? gi : -1;
                 mbar_arrive(smem_addr(&q_bar[e % kDynQ]));
@@ -1449,7 +1446,7 @@ __global__ void __launch_bounds__(rings_dyn(NC, BASE == kModeGated) * 32, 1)
         }
         acc.clear();
         gacc.clear();
-        const int gi = dyn_entry(q_group, q_bar, cc.k + 1, ok);
+        const int gi = dyn_entry(q_group, q_bar, cc.k + 1, G, ok);
         dyn_enter<R>(P, cc, cc.k + 1, gi, warp);
     }
     if (!ok) {
