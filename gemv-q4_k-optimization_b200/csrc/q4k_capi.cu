@@ -258,9 +258,21 @@ int dyn_schedule_mode() {
         const char *e = std::getenv("Q4K_SCHED");
         if (e != nullptr && std::strcmp(e, "static") == 0) return 0;
         if (e != nullptr && std::strcmp(e, "dynamic") == 0) return 2;
+        if (e != nullptr && std::strcmp(e, "mixed") == 0) return 3;
         return 1;
     }();
     return mode;
+}
+
+// Share of the row groups (per mille) that a static-prefix launch hands out
+// dynamically: Q4K_DYN_TAIL, 1..1000, default 150.
+int64_t dyn_tail_permille() {
+    static const int64_t v = [] {
+        const char *e = std::getenv("Q4K_DYN_TAIL");
+        const long x = e != nullptr ? std::strtol(e, nullptr, 10) : 150;
+        return static_cast<int64_t>(x >= 1 && x <= 1000 ? x : 150);
+    }();
+    return v;
 }
 
 // want_dyn: use the dynamically scheduled kernel when the launch qualifies
@@ -343,6 +355,18 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
             P.mode = gated ? kModeDynGated : kModeDynPlain;
         }
     }
+    if (want_dyn && dyn_schedule_mode() == 3 && !dump && !P.q6 && !P.any_fused && !is_dyn(P.mode)) {
+        // static prefix + dynamic tail: plain tasks whose row groups give every
+        // warp of a CTA at least one atom
+        const int R = rings_dyn(ncols, false);
+        bool fits = true;
+        for (int i = 0; i < njobs; ++i)
+            if (P.act_of_job[i] >= 0 && (jobs[i].K / Q4K_QK_K + kKS - 1) / kKS < R) fits = false;
+        if (fits) {
+            P.r2 = false;
+            P.mode = kModeMixPlain;
+        }
+    }
     const bool dyn = is_dyn(P.mode);
     const int64_t group_rows = P.r2 ? 64 : P.q6 ? kQ6Rows : 32;
     // task order: as given, or by decreasing K (stable) for the dynamic kernel
@@ -412,6 +436,28 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     // the epilogue variant keeps gate partials, the two-row one the second row's
     P.gemv.pcols = (P.any_fused || P.r2) ? 2 * ncols : ncols;
     P.gemv.dyn_groups = dyn ? static_cast<int32_t>(rgs) : 0;
+    P.gemv.dyn_first = 0;
+    if (P.mode == kModeMixPlain) {
+        // groups [0, S) static over all warps, [S, rgs) handed out dynamically
+        const int64_t S = rgs - (rgs * dyn_tail_permille() + 999) / 1000;
+        int64_t na = 0;
+        for (int t = 0; t < nt; ++t) {
+            const TaskDesc &T = P.gemv.task[t];
+            const int64_t g = S - T.rg_base < 0 ? 0 : (S - T.rg_base < T.ngroups ? S - T.rg_base : T.ngroups);
+            na += g * T.apr;
+        }
+        const int64_t wk = static_cast<int64_t>(num_sms) * rings_dyn(ncols, false);
+        if (na < 4 * wk || S >= rgs) {
+            // too little for either part: the static kernel (tasks as ordered)
+            P.mode = kModePlain;
+            P.gemv.dyn_groups = 0;
+        } else {
+            P.gemv.natoms = na;
+            P.gemv.nworkers = static_cast<int32_t>(wk);
+            P.gemv.packed = 1;
+            P.gemv.dyn_first = static_cast<int32_t>(S);
+        }
+    }
     P.layout = make_layout(rgs, P.gemv.pcols, P.act_bytes, 2 * nw);
     P.gemv.fused = 0;
     P.gemv.ncols = ncols;

@@ -87,7 +87,8 @@ enum GemvMode : int {
     kModeR2 = 3,
     kModeQ6 = 4,
     kModeDynPlain = 5,
-    kModeDynGated = 6
+    kModeDynGated = 6,
+    kModeMixPlain = 7
 };
 #ifndef Q4K_R2_MIN
 #define Q4K_R2_MIN 3
@@ -135,7 +136,9 @@ static_assert(rings_dyn(8, true) >= 4, "dynamic ring too small for 8 gated colum
 constexpr int kDynQ = 16;
 constexpr int kDynAhead = 3;
 // Geometry by kernel variant.
-__host__ __device__ constexpr bool is_dyn(int mode) { return mode == kModeDynPlain || mode == kModeDynGated; }
+__host__ __device__ constexpr bool is_dyn(int mode) {
+    return mode == kModeDynPlain || mode == kModeDynGated || mode == kModeMixPlain;
+}
 __host__ __device__ constexpr int stage_bytes_m(int ncols, int mode) {
     return mode == kModeQ6 ? q6_stage_bytes(ncols) : stage_bytes(ncols);
 }
@@ -221,6 +224,8 @@ struct GemvParams {
     int32_t ncols;
     unsigned long long *bar_arrive;  // grid-barrier arrivals, counts up by gridDim.x per launch
     int32_t *dyn_claim;              // dynamically scheduled launches: group tickets (zero at kernel start)
+    int32_t dyn_first;               // kModeMixPlain: first dynamically scheduled row group
+    int32_t dyn_pad_;
     unsigned long long *tl;          // launch timeline records (Q4K_TIMELINE builds; else nullptr)
     int32_t tl_slot;
     int32_t tl_pad_;
