@@ -564,6 +564,10 @@ def main():
                        "step one copy of all its activations pinned host -> device before the calls and one "
                        "copy of all its outputs device -> pinned host after them"}
 
+    # the GEMV kernel each distinct launch group runs (the library's own choice)
+    kernels = "k_gemv (Q6_K)" if q6 else (
+        "k_gemv (gather epilogue)" if peer else sorted({q4k.batch_kernel(G["tasks"], ncols) for G in L}))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         O = load_oracle()
@@ -587,7 +591,7 @@ def main():
             "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded, generated on the device)",
             "config": {"workload": wname if full_run else f"{wname} (profiling subset)",
                        "baseline_config": args.config, "launch_groups": nlaunch, "shapes": shapes,
-                       "ncols": ncols,
+                       "ncols": ncols, "gemv_kernels": kernels,
                        "launches": "per group: prep (q8_1 quantization) + persistent GEMV over the group's "
                                    "matrices, chained with programmatic dependencies" + (
                                        "; ffn gate+up as one task with the SwiGLU epilogue" if fused else ""),
@@ -601,7 +605,8 @@ def main():
             "pct_hbm_peak": 100.0 * value * 1e3 / world / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
-                         "kernel": "k_gemv: every launch of the step, each with its programmatic-dependent prep "
+                         "kernel": f"{', '.join(kernels) if isinstance(kernels, list) else kernels}: "
+                                   "every launch of the step, each with its programmatic-dependent prep "
                                    "launch; achieved = step bytes per rank / step time",
                          "algorithmic_bytes_per_launch": launch_bytes,
                          "launch_isolated_gbs": launch_bytes / (iso_ms * 1e-3) / 1e9},

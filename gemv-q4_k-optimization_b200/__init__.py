@@ -140,6 +140,7 @@ def lib() -> ctypes.CDLL:
             "q4k_ipc_handle": (None, [_P, ctypes.c_char_p]),
             "q4k_ipc_open": (None, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
             "q4k_ipc_close": (None, [_P]),
+            "q4k_batch_ex_kernel": (_I, [TXP, _I, _I, _I]),
             "q4k_timeline_bytes": (_SZ, []),
             "q4k_timeline_read": (None, [_P, _SZ, ctypes.POINTER(_I)]),
             "q4k_timeline_reset": (None, []),
@@ -422,6 +423,28 @@ def rms_norm_quantize_q8_1(x, norm_weight=None, eps: float = 1e-5, Kpad: int | N
 
 def batch_ex_workspace_bytes(tasks, ncols: int) -> int:
     return int(lib().q4k_batch_ex_workspace_bytes(tasks, len(tasks), ncols))
+
+
+KERNEL_NAMES = {0: "k_gemv", 2: "k_gemv (epilogue)", 3: "k_gemv (two rows per lane)", 5: "k_gemv_dyn",
+                6: "k_gemv_dyn (epilogue)", 7: "k_gemv_mix"}
+
+
+def batch_kernel(tasks, ncols: int, num_sms: int | None = None) -> str:
+    """Name of the GEMV kernel a batch call with these tasks (q4k_task or
+    q4k_task_ex array) runs on a device with num_sms SMs (default: the
+    current device's); touches no device memory."""
+    if num_sms is None:
+        import torch
+        num_sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    if len(tasks) and isinstance(tasks[0], Task):
+        ex = (TaskEx * len(tasks))()
+        for i, t in enumerate(tasks):
+            ex[i].t = t
+        tasks = ex
+    k = int(lib().q4k_batch_ex_kernel(tasks, len(tasks), ncols, num_sms))
+    if k < 0:
+        _check(1)
+    return KERNEL_NAMES.get(k, str(k))
 
 
 def gemv_batch_ex(tasks, ncols: int, ws: Workspace, stream=None) -> None:

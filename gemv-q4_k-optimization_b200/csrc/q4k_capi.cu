@@ -841,6 +841,28 @@ int q4k_gemv_batch(const q4k_task *tasks, int ntasks, int ncols, void *workspace
     return run(jobs, ntasks, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int q4k_batch_ex_kernel(const q4k_task_ex *tasks, int ntasks, int ncols, int num_sms) {
+    if (!tasks || ntasks < 1 || ntasks > kMaxTasks) {
+        fail(Q4K_EINVAL, "ntasks=%d outside 1..16", ntasks);
+        return -1;
+    }
+    if (num_sms < 1 || num_sms > 4096) {
+        fail(Q4K_EINVAL, "num_sms=%d outside 1..4096", num_sms);
+        return -1;
+    }
+    Job jobs[kMaxTasks];
+    for (int i = 0; i < ntasks; ++i) jobs[i] = job_of(tasks[i]);
+    Plan P;
+    // the decision run() makes for a plain (not single-launch, not gathering) call
+    if (make_plan(jobs, ntasks, ncols, nullptr, num_sms, P, nullptr, false, 0, dyn_schedule_mode() != 0) != Q4K_OK)
+        return -1;
+    static_assert(Q4K_KERNEL_STATIC == kModePlain && Q4K_KERNEL_STATIC_GATED == kModeGated &&
+                      Q4K_KERNEL_STATIC_TWO_ROW == kModeR2 && Q4K_KERNEL_DYNAMIC == kModeDynPlain &&
+                      Q4K_KERNEL_DYNAMIC_GATED == kModeDynGated && Q4K_KERNEL_MIXED == kModeMixPlain,
+                  "kernel ids");
+    return P.mode;
+}
+
 size_t q4k_batch_ex_workspace_bytes(const q4k_task_ex *tasks, int ntasks, int ncols) {
     if (!tasks || ntasks < 1 || ntasks > kMaxTasks) return 0;
     Job jobs[kMaxTasks];

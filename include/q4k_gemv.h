@@ -328,6 +328,19 @@ Q4K_API size_t q4k_noalloc_scratch_bytes(void);
 
 /* ---- diagnostics ------------------------------------------------------------- */
 
+/* Which GEMV kernel q4k_gemv_batch_ex (or q4k_gemv_batch) would run for these
+ * tasks on a device with num_sms SMs, under this process's Q4K_SCHED setting.
+ * Touches no device.  Returns a Q4K_KERNEL_* value, or -1 (reason in
+ * q4k_last_error()) for tasks the call would reject.  No counterpart in the
+ * reference, which has one kernel per ncols. */
+#define Q4K_KERNEL_STATIC 0          /* statically partitioned atom stream */
+#define Q4K_KERNEL_STATIC_GATED 2    /* the same with the bias / GLU epilogue */
+#define Q4K_KERNEL_STATIC_TWO_ROW 3  /* the same, two rows per lane (ncols >= 3) */
+#define Q4K_KERNEL_DYNAMIC 5         /* whole row groups per CTA from a ticket queue */
+#define Q4K_KERNEL_DYNAMIC_GATED 6   /* the same with the bias / GLU epilogue */
+#define Q4K_KERNEL_MIXED 7           /* static prefix + dynamic tail (Q4K_SCHED=mixed) */
+Q4K_API int q4k_batch_ex_kernel(const q4k_task_ex *tasks, int ntasks, int ncols, int num_sms);
+
 /* Per-sub-block integer sums as the kernels form them, for bit-exact parity
  * checks (the GEMV kernel runs in a dump mode and writes no dst):
  *   S_out[(j*nrows + r)*(K/32) + b] = sum over sub-block b of row r of

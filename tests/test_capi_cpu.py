@@ -157,3 +157,48 @@ def test_timeline_entry_points(q4k):
     assert T.q4k_timeline_bytes() == want
     T.q4k_timeline_read.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int)]
     assert T.q4k_timeline_read(None, 8, ctypes.byref(n)) == EINVAL  # null destination
+
+
+def _tasks_ex(q4k, specs):
+    """TaskEx array from (rows, K, x_id, gated) with made-up aligned addresses
+    (the kernel-choice query reads shapes only)."""
+    arr = (q4k.TaskEx * len(specs))()
+    base = 1 << 32
+    for i, (rows, K, x_id, gated) in enumerate(specs):
+        t = arr[i].t
+        t.W, t.x, t.dst = base * (i + 1), base * (100 + x_id), base * (200 + i)
+        t.nrows, t.K, t.stride_row_x, t.stride_col_x, t.stride_col_dst = rows, K, K // 256, K, rows
+        if gated:
+            arr[i].W_gate = base * (300 + i)
+            arr[i].glu_op = q4k.GLU_SWIGLU
+    return arr
+
+
+MISTRAL_SPECS = [(4096, 4096, 0, False), (1024, 4096, 0, False), (1024, 4096, 0, False), (4096, 4096, 1, False),
+                 (14336, 4096, 2, False), (14336, 4096, 2, False), (4096, 14336, 3, False)]
+
+
+@pytest.mark.parametrize("specs,ncols,want", [
+    (MISTRAL_SPECS, 1, "k_gemv"),                              # a whole layer: long static streams
+    (MISTRAL_SPECS, 3, "k_gemv (two rows per lane)"),
+    ([(14336, 4096, 0, False)], 1, "k_gemv_dyn"),             # one matrix, spread thinly: dynamic
+    ([(14336, 4096, 0, False)], 2, "k_gemv_dyn"),
+    ([(14336, 4096, 0, False)], 4, "k_gemv (two rows per lane)"),
+    ([(4096, 4096, 0, False)], 1, "k_gemv"),                  # too few row groups for the queue
+    ([(14336, 4096, 0, True)], 1, "k_gemv (epilogue)"),        # fused gate/up: packed
+    ([(14336, 2048, 0, True)], 1, "k_gemv_dyn (epilogue)"),    # fused, spread
+])
+def test_kernel_choice(q4k, specs, ncols, want):
+    if "Q4K_SCHED" in __import__("os").environ:
+        pytest.skip("Q4K_SCHED overrides the measured choice")
+    assert q4k.batch_kernel(_tasks_ex(q4k, specs), ncols, num_sms=148) == want
+
+
+def test_kernel_choice_rejects_bad_tasks(q4k):
+    L = q4k.lib()
+    assert L.q4k_batch_ex_kernel(None, 0, 1, 148) == -1
+    bad = _tasks_ex(q4k, [(100, 300, 0, False)])  # K not a multiple of 256
+    assert L.q4k_batch_ex_kernel(bad, 1, 1, 148) == -1
+    assert b"K" in L.q4k_last_error()
+    with pytest.raises(q4k.Q4KError):
+        q4k.batch_kernel(bad, 1, num_sms=148)
