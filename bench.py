@@ -565,8 +565,11 @@ def main():
                        "copy of all its outputs device -> pinned host after them"}
 
     # the GEMV kernel each distinct launch group runs (the library's own choice)
-    kernels = "k_gemv (Q6_K)" if q6 else (
-        "k_gemv (gather epilogue)" if peer else sorted({q4k.batch_kernel(G["tasks"], ncols) for G in L}))
+    try:
+        kernels = "k_gemv (Q6_K)" if q6 else (
+            "k_gemv (gather epilogue)" if peer else sorted({q4k.batch_kernel(G["tasks"], ncols) for G in L}))
+    except Exception as e:  # a report, never a reason to lose the measurement
+        kernels = f"unknown ({e!r})"
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
