@@ -1617,6 +1617,9 @@ __global__ void __launch_bounds__(rings_dyn(NC, false) * 32, 1)
     int done = 0;
     int open_t = -1, open_g = -1;  // static phase: the open row group
     int group_k = -1;              // producer: last dynamic group whose claim duties ran
+#if Q4K_TIMELINE
+    uint64_t tl_static_end = 0;    // when this warp's sums left its static range
+#endif
     while (ok) {
         if (producer) {
             if (!drawn && done >= trig) {
@@ -1640,6 +1643,9 @@ __global__ void __launch_bounds__(rings_dyn(NC, false) * 32, 1)
                 acc.clear();
             }
         } else {
+#if Q4K_TIMELINE
+            if (tl_static_end == 0) tl_static_end = globaltimer_ns();
+#endif
             if (open_t >= 0) {  // the static range ended with the previous atom
                 AtomCursor o{open_t, open_g, 0};
                 flush_group<NC, NC, BASE>(P, o, acc, gacc, dacc, worker, a0, a1, lane, 0, cta_w0, cta_w1,
@@ -1737,7 +1743,7 @@ __global__ void __launch_bounds__(rings_dyn(NC, false) * 32, 1)
         o[3] = static_cast<unsigned long long>(done > 0 ? done : 1);
         o[4] = smid;
         o[5] = static_cast<unsigned long long>(worker);
-        o[6] = static_cast<unsigned long long>(ns);
+        o[6] = tl_static_end;  // 0: the warp never left its static range
         o[7] = static_cast<unsigned long long>(cc.k);
     }
 #endif

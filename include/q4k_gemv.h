@@ -366,7 +366,10 @@ Q4K_API int q4k_workspace_status(const void *workspace, int *device_status, q4k_
  * index modulo the ring, reset by q4k_timeline_reset:
  *   GEMV  u64[slot][Q4K_TIMELINE_CTAS][16 warps][8] =
  *         {start, wait return, end, atoms of the worker (0: idle), SM id,
- *          worker index, first atom, end atom}
+ *          worker index, first atom, end atom}; the dynamically scheduled
+ *          kernels record atoms done in word 3, and in words 6 and 7 the time
+ *          the warp left its static range (static-prefix kernel; else 0) and
+ *          its last queue entry
  *   prep  u64[slot][Q4K_TIMELINE_PREP_CTAS][4] = {start, wait return, end, 1}
  * q4k_timeline_bytes() is the size of both regions (GEMV first); it returns 0
  * and the other two Q4K_EINVAL in a library built without the option. */
