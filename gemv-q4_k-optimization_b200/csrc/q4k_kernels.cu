@@ -1573,7 +1573,7 @@ __global__ void __launch_bounds__(rings_dyn(NC, false) * 32, 1)
 
     // Claims.  trig: warp 0's static atom at which the first batch is drawn
     // (its result is published one atom later); with a short range, at once.
-    const int trig = ns - kStages - 3;
+    const int trig = ns - kStages - 1;
     int pend = 0;
     int filled = 0;
     bool drawn = false, claiming = false;

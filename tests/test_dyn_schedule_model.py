@@ -280,7 +280,7 @@ def _mix_warp(cta, warp, sh, G, S, R, ns, apr_of, counter, reduced, rnd):
         issue(issued)
         issued += 1
     yield None  # griddepcontrol.wait
-    trig = ns - KSTAGES - 3
+    trig = ns - KSTAGES - 1
     if producer and trig <= 0:
         t0 = counter[0]
         counter[0] += KAHEAD
