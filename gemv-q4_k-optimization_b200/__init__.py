@@ -56,7 +56,7 @@ class Gather(ctypes.Structure):
     """struct q4k_gather (include/q4k_gemv.h)."""
     _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("out_local", ctypes.c_void_p),
                 ("out_peer", ctypes.c_void_p * MAX_PEERS), ("flags_peer", ctypes.c_void_p * MAX_PEERS),
-                ("epoch", ctypes.c_void_p)]
+                ("epoch", ctypes.c_void_p), ("out_elems", ctypes.c_int64)]
 
 
 class Task(ctypes.Structure):
@@ -120,6 +120,7 @@ def lib() -> ctypes.CDLL:
             "q4k_mul_mat_vec_noalloc": (None, [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P]),
             "q4k_noalloc_scratch_bytes": (_SZ, []),
             "q4k_gemv_batch_allgather": (None, [TP, _I, _I, GP, _P, _SZ, _P]),
+            "q4k_gather_wait": (None, [GP, _P, _SZ, _P]),
             "q4k_workspace_init": (None, [_P, _SZ, _P]),
             "q4k_gemv_batch_persistent": (None, [TP, _I, _I, GP, _P, _SZ, _P]),
             "q4k_batch_ex_workspace_bytes": (_SZ, [TXP, _I, _I]),
@@ -426,7 +427,7 @@ def batch_ex_workspace_bytes(tasks, ncols: int) -> int:
 
 
 KERNEL_NAMES = {0: "k_gemv", 2: "k_gemv (epilogue)", 3: "k_gemv (two rows per lane)", 5: "k_gemv_dyn",
-                6: "k_gemv_dyn (epilogue)", 7: "k_gemv_mix"}
+                6: "k_gemv_dyn (epilogue)"}
 
 
 def batch_kernel(tasks, ncols: int, num_sms: int | None = None) -> str:
@@ -674,6 +675,7 @@ class PeerGather:
         g = Gather()
         g.world, g.rank = self.world, self.rank
         g.out_local = out_ptr
+        g.out_elems = out_elems
         g.epoch = epoch_ptr
         for q in range(self.world):
             if q == self.rank:
@@ -701,10 +703,17 @@ class PeerGather:
 
 
 def gemv_batch_allgather(tasks, ncols: int, gather: PeerGather, ws: Workspace, stream=None) -> None:
-    """q4k_gemv_batch on this rank's row shards, outputs gathered into every rank's buffer."""
+    """q4k_gemv_batch on this rank's row shards, outputs gathered into every rank's buffer
+    (complete once gather_wait has run on the stream)."""
     ws.ensure(batch_workspace_bytes(tasks, ncols))
     _check(lib().q4k_gemv_batch_allgather(tasks, len(tasks), ncols, ctypes.byref(gather.desc), ws.ptr, ws.nbytes,
                                           _stream(stream)))
+
+
+def gather_wait(gather: PeerGather, ws: Workspace, stream=None) -> None:
+    """q4k_gather_wait: the peers' rows of the last gathering call are in this rank's buffer
+    once this stream-ordered wait has run (a wait that gives up sets the status word)."""
+    _check(lib().q4k_gather_wait(ctypes.byref(gather.desc), ws.ptr, ws.nbytes, _stream(stream)))
 
 
 # ---------------------------------------------------------------------------

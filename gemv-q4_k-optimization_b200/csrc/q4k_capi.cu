@@ -249,31 +249,14 @@ struct Plan {
 };
 
 // Build the schedule (no device memory touched).  ws may be null (sizing).
-// Q4K_SCHED (read once per process): "static" keeps every launch on the
-// statically partitioned kernel; "dynamic" uses the dynamically scheduled one
-// wherever it can run (for measurements); unset or anything else: the
-// measured choice.
-int dyn_schedule_mode() {
-    static const int mode = [] {
-        const char *e = std::getenv("Q4K_SCHED");
-        if (e != nullptr && std::strcmp(e, "static") == 0) return 0;
-        if (e != nullptr && std::strcmp(e, "dynamic") == 0) return 2;
-        if (e != nullptr && std::strcmp(e, "mixed") == 0) return 3;
-        return 1;
-    }();
-    return mode;
-}
-
-// Share of the row groups (per mille) that a static-prefix launch hands out
-// dynamically: Q4K_DYN_TAIL, 1..1000, default 150.
-int64_t dyn_tail_permille() {
-    static const int64_t v = [] {
-        const char *e = std::getenv("Q4K_DYN_TAIL");
-        const long x = e != nullptr ? std::strtol(e, nullptr, 10) : 150;
-        return static_cast<int64_t>(x >= 1 && x <= 1000 ? x : 150);
-    }();
-    return v;
-}
+// Kernel choice: the measured one, unless the library was built with
+// Q4K_SCHED_FORCE (measurement builds only, see the Makefile's variants):
+// 1 keeps every launch on the statically partitioned kernel, 2 uses the
+// dynamically scheduled one wherever it can run.
+#ifndef Q4K_SCHED_FORCE
+#define Q4K_SCHED_FORCE 0
+#endif
+constexpr int kSchedForce = Q4K_SCHED_FORCE;
 
 // want_dyn: use the dynamically scheduled kernel when the launch qualifies
 // (plain or gated Q4_K tasks whose row groups give every warp of a CTA at
@@ -349,22 +332,10 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         // spreads fewer than four atoms per worker over the SMs.
         const bool spread = natoms < 4 * static_cast<int64_t>(num_sms) * rings_for(ncols);
         const bool measured_win = spread && ncols <= 2;
-        if (fits && (measured_win || dyn_schedule_mode() == 2) && G >= kDynAhead * static_cast<int64_t>(num_sms) &&
+        if (fits && (measured_win || kSchedForce == 2) && G >= kDynAhead * static_cast<int64_t>(num_sms) &&
             G < (int64_t{1} << 30)) {
             P.r2 = false;
             P.mode = gated ? kModeDynGated : kModeDynPlain;
-        }
-    }
-    if (want_dyn && dyn_schedule_mode() == 3 && !dump && !P.q6 && !P.any_fused && !is_dyn(P.mode)) {
-        // static prefix + dynamic tail: plain tasks whose row groups give every
-        // warp of a CTA at least one atom
-        const int R = rings_dyn(ncols, false);
-        bool fits = true;
-        for (int i = 0; i < njobs; ++i)
-            if (P.act_of_job[i] >= 0 && (jobs[i].K / Q4K_QK_K + kKS - 1) / kKS < R) fits = false;
-        if (fits) {
-            P.r2 = false;
-            P.mode = kModeMixPlain;
         }
     }
     const bool dyn = is_dyn(P.mode);
@@ -436,28 +407,6 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     // the epilogue variant keeps gate partials, the two-row one the second row's
     P.gemv.pcols = (P.any_fused || P.r2) ? 2 * ncols : ncols;
     P.gemv.dyn_groups = dyn ? static_cast<int32_t>(rgs) : 0;
-    P.gemv.dyn_first = 0;
-    if (P.mode == kModeMixPlain) {
-        // groups [0, S) static over all warps, [S, rgs) handed out dynamically
-        const int64_t S = rgs - (rgs * dyn_tail_permille() + 999) / 1000;
-        int64_t na = 0;
-        for (int t = 0; t < nt; ++t) {
-            const TaskDesc &T = P.gemv.task[t];
-            const int64_t g = S - T.rg_base < 0 ? 0 : (S - T.rg_base < T.ngroups ? S - T.rg_base : T.ngroups);
-            na += g * T.apr;
-        }
-        const int64_t wk = static_cast<int64_t>(num_sms) * rings_dyn(ncols, false);
-        if (na < 4 * wk || S >= rgs) {
-            // too little for either part: the static kernel (tasks as ordered)
-            P.mode = kModePlain;
-            P.gemv.dyn_groups = 0;
-        } else {
-            P.gemv.natoms = na;
-            P.gemv.nworkers = static_cast<int32_t>(wk);
-            P.gemv.packed = 1;
-            P.gemv.dyn_first = static_cast<int32_t>(S);
-        }
-    }
     P.layout = make_layout(rgs, P.gemv.pcols, P.act_bytes, 2 * nw);
     P.gemv.fused = 0;
     P.gemv.ncols = ncols;
@@ -549,31 +498,78 @@ int validate_gather(const q4k_gather *g) {
     for (int q = 0; q < g->world; ++q)
         if (!g->out_peer[q] || !g->flags_peer[q]) return fail(Q4K_EINVAL, "gather peer %d pointers are null", q);
     if (g->out_peer[g->rank] != g->out_local) return fail(Q4K_EINVAL, "gather out_peer[rank] != out_local");
+    if (g->out_elems < 0) return fail(Q4K_EINVAL, "gather out_elems < 0");
     return Q4K_OK;
 }
 
+// Every output of a gathering call is also stored at the same offset in every
+// peer's buffer, so each task's dst columns must lie inside the full buffer:
+// [dst, dst + (ncols-1)*stride_col_dst + nrows) within [out_local, out_local + out_elems).
+int validate_gather_tasks(const q4k_gather *g, const q4k_task *tasks, int ntasks, int ncols) {
+    const intptr_t base = reinterpret_cast<intptr_t>(g->out_local);
+    for (int i = 0; i < ntasks; ++i) {
+        const q4k_task &t = tasks[i];
+        if (t.nrows <= 0) continue;
+        const intptr_t d = reinterpret_cast<intptr_t>(t.dst);
+        if (d < base || (d - base) % static_cast<intptr_t>(sizeof(float)) != 0)
+            return fail(Q4K_EINVAL, "task %d: dst is not a float inside the gather buffer out_local", i);
+        const int64_t off = static_cast<int64_t>((d - base) / static_cast<intptr_t>(sizeof(float)));
+        if (ncols > 1 && t.stride_col_dst < t.nrows)
+            return fail(Q4K_EINVAL, "task %d: stride_col_dst=%lld < nrows", i, (long long)t.stride_col_dst);
+        const int64_t end = off + static_cast<int64_t>(ncols - 1) * (ncols > 1 ? t.stride_col_dst : 0) + t.nrows;
+        if (end > g->out_elems)
+            return fail(Q4K_EINVAL, "task %d: outputs [%lld, %lld) reach past the gather buffer's %lld floats", i,
+                        (long long)off, (long long)end, (long long)g->out_elems);
+    }
+    return Q4K_OK;
+}
+
+GatherWait gather_wait_of(const q4k_gather *g, void *workspace) {
+    GatherWait w{};
+    if (g == nullptr || g->world <= 1) return w;
+    w.flags = g->flags_peer[g->rank];
+    w.epoch = g->epoch;
+    w.status = static_cast<int32_t *>(workspace);
+    w.world = g->world;
+    w.rank = g->rank;
+    return w;
+}
+
 #if Q4K_TIMELINE
-// Launch timeline records (one buffer, on the device of the first call).
+// Launch timeline records: one buffer per device, allocated by the first call
+// on that device (a diagnostic build; the release library has none of this).
 std::mutex g_tl_mu;
-unsigned long long *g_tl = nullptr;
-int g_tl_calls = 0;
+constexpr int kTlDevices = 64;
+unsigned long long *g_tl[kTlDevices] = {};
+int g_tl_calls[kTlDevices] = {};
 constexpr size_t kTlGemvWords = static_cast<size_t>(Q4K_TIMELINE_SLOTS) * Q4K_TIMELINE_CTAS * 16 * 8;
 constexpr size_t kTlPrepWords = static_cast<size_t>(Q4K_TIMELINE_SLOTS) * Q4K_TIMELINE_PREP_CTAS * 4;
 constexpr size_t kTlBytes = (kTlGemvWords + kTlPrepWords) * sizeof(unsigned long long);
 
-// Points the launch parameters at the next ring slot.  The first call
-// allocates and clears the buffer (synchronously: not inside a graph capture).
+int tl_device(int *dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (*dev < 0 || *dev >= kTlDevices) return fail(Q4K_EINVAL, "device %d beyond the timeline table", *dev);
+    return Q4K_OK;
+}
+
+// Points the launch parameters at the next ring slot of the current device's
+// buffer.  The first call on a device allocates and clears the buffer
+// (synchronously: not inside a graph capture).
 int timeline_attach(Plan &P) {
+    int dev = 0;
+    int st = tl_device(&dev);
+    if (st != Q4K_OK) return st;
     std::lock_guard<std::mutex> lk(g_tl_mu);
-    if (g_tl == nullptr) {
-        cudaError_t e = cudaMalloc(&g_tl, kTlBytes);
-        if (e == cudaSuccess) e = cudaMemset(g_tl, 0, kTlBytes);
+    if (g_tl[dev] == nullptr) {
+        cudaError_t e = cudaMalloc(&g_tl[dev], kTlBytes);
+        if (e == cudaSuccess) e = cudaMemset(g_tl[dev], 0, kTlBytes);
         if (e != cudaSuccess) return cuda_fail(e, "timeline buffer");
     }
-    const int slot = g_tl_calls++ % Q4K_TIMELINE_SLOTS;
-    P.gemv.tl = g_tl;
+    const int slot = g_tl_calls[dev]++ % Q4K_TIMELINE_SLOTS;
+    P.gemv.tl = g_tl[dev];
     P.gemv.tl_slot = slot;
-    P.prep.tl = g_tl + kTlGemvWords;
+    P.prep.tl = g_tl[dev] + kTlGemvWords;
     P.prep.tl_slot = slot;
     return Q4K_OK;
 }
@@ -605,7 +601,7 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     // The device's plan (its SM count fixes the workers and the layout); the
     // workspace size is checked before any pointer into it is formed.
     st = make_plan(jobs, njobs, ncols, static_cast<uint8_t *>(workspace), num_sms, P, dump_T, dump, ws_bytes,
-                   !fused && !gathering && dyn_schedule_mode() != 0);
+                   !fused && !gathering && kSchedForce != 1);
     if (st != Q4K_OK) return st;
     P.gemv.dump_S = dump_S;
     P.gemv.gworld = 1;
@@ -619,6 +615,8 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
         }
         P.gemv.gepoch = gather->epoch;
         P.gemv.gdone = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace) + 4);
+        P.prep.gwait = gather_wait_of(gather, workspace);
+        P.gemv.gwait = P.prep.gwait;
     }
 #if Q4K_TIMELINE
     if ((st = timeline_attach(P)) != Q4K_OK) return st;
@@ -854,11 +852,11 @@ int q4k_batch_ex_kernel(const q4k_task_ex *tasks, int ntasks, int ncols, int num
     for (int i = 0; i < ntasks; ++i) jobs[i] = job_of(tasks[i]);
     Plan P;
     // the decision run() makes for a plain (not single-launch, not gathering) call
-    if (make_plan(jobs, ntasks, ncols, nullptr, num_sms, P, nullptr, false, 0, dyn_schedule_mode() != 0) != Q4K_OK)
+    if (make_plan(jobs, ntasks, ncols, nullptr, num_sms, P, nullptr, false, 0, kSchedForce != 1) != Q4K_OK)
         return -1;
     static_assert(Q4K_KERNEL_STATIC == kModePlain && Q4K_KERNEL_STATIC_GATED == kModeGated &&
                       Q4K_KERNEL_STATIC_TWO_ROW == kModeR2 && Q4K_KERNEL_DYNAMIC == kModeDynPlain &&
-                      Q4K_KERNEL_DYNAMIC_GATED == kModeDynGated && Q4K_KERNEL_MIXED == kModeMixPlain,
+                      Q4K_KERNEL_DYNAMIC_GATED == kModeDynGated,
                   "kernel ids");
     return P.mode;
 }
@@ -966,6 +964,7 @@ int q4k_gemv_batch_allgather(const q4k_task *tasks, int ntasks, int ncols, const
                              void *workspace, size_t workspace_bytes, q4k_stream_t stream) {
     if (!tasks || ntasks < 1 || ntasks > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..16", ntasks);
     int st = validate_gather(gather);
+    if (st == Q4K_OK) st = validate_gather_tasks(gather, tasks, ntasks, ncols);
     if (st != Q4K_OK) return st;
     Job jobs[kMaxTasks];
     for (int i = 0; i < ntasks; ++i) {
@@ -976,6 +975,16 @@ int q4k_gemv_batch_allgather(const q4k_task *tasks, int ntasks, int ncols, const
     }
     return run(jobs, ntasks, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr,
                nullptr, gather);
+}
+
+int q4k_gather_wait(const q4k_gather *gather, void *workspace, size_t workspace_bytes, q4k_stream_t stream) {
+    int st = validate_gather(gather);
+    if (st != Q4K_OK) return st;
+    if (workspace == nullptr || workspace_bytes < 4) return fail(Q4K_EWORKSPACE, "workspace is null or too small");
+    if (!aligned16(workspace)) return fail(Q4K_EWORKSPACE, "workspace is not 16-byte aligned");
+    if (gather->world <= 1) return Q4K_OK;
+    cudaError_t e = launch_gather_wait(gather_wait_of(gather, workspace), reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? Q4K_OK : cuda_fail(e, "gather wait launch");
 }
 
 int q4k_workspace_init(void *workspace, size_t workspace_bytes, q4k_stream_t stream) {
@@ -991,6 +1000,7 @@ int q4k_gemv_batch_persistent(const q4k_task *tasks, int ntasks, int ncols, cons
     if (!tasks || ntasks < 1 || ntasks > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..16", ntasks);
     if (gather) {
         int st = validate_gather(gather);
+        if (st == Q4K_OK) st = validate_gather_tasks(gather, tasks, ntasks, ncols);
         if (st != Q4K_OK) return st;
     }
     Job jobs[kMaxTasks];
@@ -1074,14 +1084,17 @@ int q4k_timeline_read(void *host, size_t bytes, int *ncalls) {
 #if Q4K_TIMELINE
     if (host == nullptr || bytes > kTlBytes)
         return fail(Q4K_EINVAL, "timeline read of %zu bytes (at most %zu)", bytes, kTlBytes);
+    int dev = 0;
+    int st = tl_device(&dev);
+    if (st != Q4K_OK) return st;
     std::lock_guard<std::mutex> lk(g_tl_mu);
-    if (ncalls) *ncalls = g_tl_calls;
-    if (g_tl == nullptr) {
+    if (ncalls) *ncalls = g_tl_calls[dev];
+    if (g_tl[dev] == nullptr) {
         std::memset(host, 0, bytes);
         return Q4K_OK;
     }
     cudaError_t e = cudaDeviceSynchronize();
-    if (e == cudaSuccess) e = cudaMemcpy(host, g_tl, bytes, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(host, g_tl[dev], bytes, cudaMemcpyDeviceToHost);
     return e == cudaSuccess ? Q4K_OK : cuda_fail(e, "timeline read");
 #else
     (void)host;
@@ -1093,11 +1106,14 @@ int q4k_timeline_read(void *host, size_t bytes, int *ncalls) {
 
 int q4k_timeline_reset(void) {
 #if Q4K_TIMELINE
+    int dev = 0;
+    int st = tl_device(&dev);
+    if (st != Q4K_OK) return st;
     std::lock_guard<std::mutex> lk(g_tl_mu);
-    g_tl_calls = 0;
-    if (g_tl == nullptr) return Q4K_OK;
+    g_tl_calls[dev] = 0;
+    if (g_tl[dev] == nullptr) return Q4K_OK;
     cudaError_t e = cudaDeviceSynchronize();
-    if (e == cudaSuccess) e = cudaMemset(g_tl, 0, kTlBytes);
+    if (e == cudaSuccess) e = cudaMemset(g_tl[dev], 0, kTlBytes);
     return e == cudaSuccess ? Q4K_OK : cuda_fail(e, "timeline reset");
 #else
     return fail(Q4K_EINVAL, "library built without Q4K_TIMELINE");

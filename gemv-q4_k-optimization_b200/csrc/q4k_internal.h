@@ -87,8 +87,7 @@ enum GemvMode : int {
     kModeR2 = 3,
     kModeQ6 = 4,
     kModeDynPlain = 5,
-    kModeDynGated = 6,
-    kModeMixPlain = 7
+    kModeDynGated = 6
 };
 #ifndef Q4K_R2_MIN
 #define Q4K_R2_MIN 3
@@ -137,7 +136,7 @@ constexpr int kDynQ = 16;
 constexpr int kDynAhead = 3;
 // Geometry by kernel variant.
 __host__ __device__ constexpr bool is_dyn(int mode) {
-    return mode == kModeDynPlain || mode == kModeDynGated || mode == kModeMixPlain;
+    return mode == kModeDynPlain || mode == kModeDynGated;
 }
 __host__ __device__ constexpr int stage_bytes_m(int ncols, int mode) {
     return mode == kModeQ6 ? q6_stage_bytes(ncols) : stage_bytes(ncols);
@@ -159,6 +158,16 @@ constexpr int kStatusTimeout = 3;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 constexpr unsigned long long kDrainLimitNs = 20000000ull;   // 20 ms
 constexpr unsigned long long kPeerWaitLimitNs = 2000000000ull;  // 2 s for the peers' epoch
+
+// Consumer wait of the fused all-gather: this rank's flag words (one per
+// sender), its epoch word, and where to report a wait that gave up.
+struct GatherWait {
+    const uint32_t *flags;
+    const uint32_t *epoch;
+    int32_t *status;
+    int32_t world;   // <= 1: no wait
+    int32_t rank;
+};
 
 struct TaskDesc {
     const uint8_t *W;        // weight row 0 (16-byte aligned)
@@ -218,14 +227,13 @@ struct GemvParams {
     uint32_t *gflags_peer[kMaxPeers];// every rank's flag words (one per sender), mapped here
     uint32_t *gepoch;                // this rank's epoch word (persists across calls)
     uint32_t *gdone;                 // CTAs finished (workspace; zero at kernel start)
+    GatherWait gwait;                // single-launch path: wait for the previous gather before reading x
     // Single-launch path (fused quantization + grid barrier): sync words in an
     // initialised workspace that every launch leaves as it found them.
     int32_t fused;
     int32_t ncols;
     unsigned long long *bar_arrive;  // grid-barrier arrivals, counts up by gridDim.x per launch
     int32_t *dyn_claim;              // dynamically scheduled launches: group tickets (zero at kernel start)
-    int32_t dyn_first;               // kModeMixPlain: first dynamically scheduled row group
-    int32_t dyn_pad_;
     unsigned long long *tl;          // launch timeline records (Q4K_TIMELINE builds; else nullptr)
     int32_t tl_slot;
     int32_t tl_pad_;
@@ -257,6 +265,7 @@ struct PrepJob {
 
 struct PrepParams {
     PrepJob job[kMaxJobs];
+    GatherWait gwait;        // gathering calls: wait for the previous gather before reading x
     int32_t njobs;
     int32_t zero_count;      // int32 words to clear at zero_ptr (counters, status)
     int64_t nitems;
@@ -271,6 +280,7 @@ struct PrepParams {
 // Launchers (q4k_kernels.cu).  Return cudaSuccess or the launch error.
 cudaError_t launch_prep(const PrepParams &p, cudaStream_t s);
 cudaError_t launch_gemv(const GemvParams &p, int ncols, int mode, int grid, cudaStream_t s);
+cudaError_t launch_gather_wait(const GatherWait &g, cudaStream_t s);
 // Per-device setup (SM count, shared-memory opt-in); thread-safe, idempotent.
 cudaError_t device_setup(int *num_sms);
 

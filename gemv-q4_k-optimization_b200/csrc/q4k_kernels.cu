@@ -102,6 +102,34 @@ __device__ __forceinline__ void prep_norm_column(const PrepJob &J, int col) {
     }
 }
 
+// Consumer side of the fused all-gather: one thread waits (bounded) until
+// every peer's flag word in this rank's flags has reached this rank's epoch,
+// i.e. every peer's rows of the last gathering launch on this stream are in
+// this rank's buffer; acquire loads at system scope.  Returns false (and sets
+// the status word) when the wait gives up.
+__device__ __forceinline__ bool gather_wait_flags(const GatherWait &G) {
+    const uint32_t e = *reinterpret_cast<const volatile uint32_t *>(G.epoch);
+    const uint64_t t0 = globaltimer_ns();
+    for (int q = 0; q < G.world; ++q) {
+        if (q == G.rank) continue;
+        for (uint32_t it = 0;; ++it) {
+            if (static_cast<int32_t>(ld_acquire_sys_u32(G.flags + q) - e) >= 0) break;
+            if ((it & 63u) == 0 && globaltimer_ns() - t0 > kPeerWaitLimitNs) {
+                if (G.status != nullptr) atomicExch(G.status, kStatusTimeout);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// q4k_gather_wait: one CTA, one waiting thread.
+__global__ void __launch_bounds__(32) k_gather_wait(const __grid_constant__ GatherWait G) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x == 0) gather_wait_flags(G);
+}
+
 __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams P) {
 #if Q4K_TIMELINE
     const uint64_t tl_start = globaltimer_ns();
@@ -146,6 +174,12 @@ __global__ void __launch_bounds__(256) k_prep(const __grid_constant__ PrepParams
 #endif
 
     for (int64_t i = tid; i < P.zero_count; i += nthr) P.zero_ptr[i] = 0;
+    // A gathering call reads activations that may come from the previous
+    // gathering call's full output: wait for the peers' rows first.
+    if (P.gwait.world > 1) {
+        if (threadIdx.x == 0) gather_wait_flags(P.gwait);
+        __syncthreads();
+    }
 
     if (static_cast<int>(blockIdx.x) < P.norm_ctas) {
         int j = 0;
@@ -1056,15 +1090,16 @@ __device__ __forceinline__ void grid_barrier_wait(const GemvParams &P, unsigned 
     __syncthreads();
 }
 
-// Fused all-gather epilogue: after every CTA of this grid has stored its
-// outputs (locally and into the peers' buffers), the last CTA to finish
-// publishes epoch+1 in each peer's flag word for this rank and waits, bounded,
-// until every peer has published the same epoch here.  The grid therefore
-// completes only when the full output is in this rank's buffer.  The epoch
+// Fused all-gather epilogue (producer side): after every CTA of this grid has
+// stored its outputs (locally and into the peers' buffers), the last CTA to
+// finish publishes epoch+1 in each peer's flag word for this rank and exits;
+// it does not wait for the peers.  A consumer of the gathered buffer waits
+// for every peer's flag to reach this rank's epoch (gather_wait_flags: the
+// next gathering call's quantization step, or q4k_gather_wait).  The epoch
 // word persists across calls, so replays of a captured sequence keep counting.
 // Ordering: each CTA's peer stores -> block barrier -> release fence (system
 // scope) -> arrival count; the last CTA's acquire fence -> per-peer release
-// stores of the flag (one lane per peer, in parallel) -> peers' acquire loads.
+// stores of the flag (one lane per peer) -> the consumer's acquire loads.
 // The last CTA also returns the arrival count to 0 for the next launch.
 __device__ __forceinline__ void gather_epilogue(const GemvParams &P) {
     __shared__ int last_cta;
@@ -1079,19 +1114,7 @@ __device__ __forceinline__ void gather_epilogue(const GemvParams &P) {
     if (lane == 0) fence_acq_rel_sys();
     __syncwarp();
     const uint32_t e = *reinterpret_cast<volatile uint32_t *>(P.gepoch) + 1u;
-    const bool peer = lane < P.gworld && lane != P.grank;
-    if (peer) st_release_sys_u32(P.gflags_peer[lane] + P.grank, e);
-    const uint32_t *mine = P.gflags_peer[P.grank];
-    const uint64_t t0 = globaltimer_ns();
-    bool done = !peer;
-    for (uint32_t it = 0;; ++it) {
-        if (!done) done = static_cast<int32_t>(ld_acquire_sys_u32(mine + lane) - e) >= 0;
-        if (__all_sync(0xffffffffu, done)) break;
-        if ((it & 63u) == 0 && globaltimer_ns() - t0 > kPeerWaitLimitNs) {
-            if (lane == 0) atomicExch(P.status, kStatusTimeout);
-            break;
-        }
-    }
+    if (lane < P.gworld && lane != P.grank) st_release_sys_u32(P.gflags_peer[lane] + P.grank, e);
     if (lane == 0) {
         *reinterpret_cast<volatile uint32_t *>(P.gepoch) = e;
         *reinterpret_cast<volatile uint32_t *>(P.gdone) = 0u;  // ready for the next launch
@@ -1168,7 +1191,9 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
         if (threadIdx.x == 0) {
             target = barrier_target(P);
             if (blockIdx.x == 0) *P.status = kStatusOk;
+            if (P.gworld > 1) gather_wait_flags(P.gwait);  // x may be a gathered output
         }
+        __syncthreads();
         fused_quantize(P);
         fence_proxy_async_global();  // this thread's q8a stores, before other CTAs' bulk copies
         grid_barrier_arrive(P);
@@ -1474,282 +1499,6 @@ __global__ void __launch_bounds__(rings_dyn(NC, BASE == kModeGated) * 32, 1)
 }
 
 // ============================================================================
-// Static prefix + dynamic tail (kModeMixPlain)
-// ============================================================================
-// The first P.dyn_first row groups (tasks by decreasing K) are split over the
-// warps as in k_gemv: contiguous atom ranges, long per-warp streams, split
-// row groups finished through partials.  The rest, the shortest groups, are
-// handed out dynamically as in k_gemv_dyn (whole groups per CTA, warp shares
-// added in shared memory), so that CTAs on fast SMs take more of them.  A
-// warp's copy cursor runs from its static range straight into the claimed
-// groups, so the ring does not drain at the change.  Lane 0 of warp 0 claims
-// the CTA's first kDynAhead groups a few atoms before its static range ends
-// and publishes one more per dynamic group, two groups ahead.
-__device__ __forceinline__ int mix_entry(const int *q_group, const uint64_t *q_bar, int k, bool &ok) {
-    const int slot = k % kDynQ;
-    ok = ok && wait_phase(smem_addr(&q_bar[slot]), static_cast<uint32_t>((k / kDynQ) & 1), kWaitLimitNs);
-    return ok ? q_group[slot] : -1;
-}
-
-template <int R>
-__device__ __forceinline__ void mix_resolve(const GemvParams &P, DynCursor &d, const int *q_group,
-                                            const uint64_t *q_bar, int warp, bool &ok) {
-    if (!d.need || d.gi < 0) return;
-    const int gi = mix_entry(q_group, q_bar, d.k + 1, ok);
-    dyn_enter<R>(P, d, d.k + 1, gi, warp);
-}
-
-template <int NC>
-__global__ void __launch_bounds__(rings_dyn(NC, false) * 32, 1)
-    k_gemv_mix(const __grid_constant__ GemvParams P) {
-    constexpr int BASE = kModePlain;
-    constexpr int R = rings_dyn(NC, false);
-    constexpr int kSB = Stage<NC, BASE>::kBytes;
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full_bars[R][kStages];
-    __shared__ __align__(8) uint64_t q_bar[kDynQ];
-    __shared__ __align__(8) uint64_t free_bar[2];
-    __shared__ int q_group[kDynQ];
-    __shared__ int red_cnt[2];
-    __shared__ int cta_cnt[R];  // static phase: arrivals at row groups split between this CTA's warps
-    __shared__ float part[2][R][NC][32];
-
-#if Q4K_TIMELINE
-    const uint64_t tl_start = globaltimer_ns();
-#endif
-    pdl_launch_dependents();
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    if (threadIdx.x == 0) {
-        for (int r = 0; r < R; ++r) {
-            for (int s = 0; s < kStages; ++s) mbar_init(smem_addr(&full_bars[r][s]), 1);
-            cta_cnt[r] = 0;
-        }
-        for (int q = 0; q < kDynQ; ++q) mbar_init(smem_addr(&q_bar[q]), 1);
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(smem_addr(&free_bar[b]), 1);
-            red_cnt[b] = 0;
-        }
-        mbar_fence_init();
-    }
-    __syncthreads();
-    uint32_t full[kStages];
-#pragma unroll
-    for (int s = 0; s < kStages; ++s) full[s] = smem_addr(&full_bars[warp][s]);
-    const uint32_t ring = smem_addr(smem) + static_cast<uint32_t>(warp * kStages * kSB);
-    const int G = P.dyn_groups;
-    const bool producer = warp == 0 && lane == 0;
-
-    // static range (CTA-major workers)
-    const int64_t worker = static_cast<int64_t>(blockIdx.x) * R + warp;
-    const int64_t cta_w0 = static_cast<int64_t>(blockIdx.x) * R;
-    const int64_t cta_w1 = cta_w0 + R - 1;
-    const int64_t a0 = worker_begin(P, worker);
-    const int64_t a1 = worker_begin(P, worker + 1);
-    const int ns = static_cast<int>(a1 - a0);
-    AtomCursor si = locate_atom(P, a0);  // static copy cursor
-    AtomCursor sc = si;                  // static sum cursor
-    DynCursor ic, cc;                    // dynamic cursors: before entry 0
-    ic.k = -1;
-    ic.gi = 0;
-    ic.need = true;
-    cc = ic;
-    bool ok = true;
-
-    int issued = 0;
-    AtomCursor pro[kStages];
-    while (issued < kStages && issued < ns) {  // weights only: read-only
-        pro[issued] = si;
-        issue_weights<NC, BASE>(P, si, ring + (issued % kStages) * kSB, full[issued % kStages], lane);
-        ++issued;
-        advance(P, si);
-    }
-    pdl_wait();
-#if Q4K_TIMELINE
-    const uint64_t tl_wait = globaltimer_ns();
-#endif
-    for (int i = 0; i < issued; ++i)
-        issue_acts<NC, BASE>(P, pro[i], ring + (i % kStages) * kSB, full[i % kStages], lane);
-
-    // Claims.  trig: warp 0's static atom at which the first batch is drawn
-    // (its result is published one atom later); with a short range, at once.
-    const int trig = ns - kStages - 1;
-    int pend = 0;
-    int filled = 0;
-    bool drawn = false, claiming = false;
-    auto publish_batch = [&](int t0) {
-        for (int e = 0; e < kDynAhead; ++e) {
-            const int gi = P.dyn_first + t0 + e;
-            q_group[e] = gi < G ? gi : -1;
-            mbar_arrive(smem_addr(&q_bar[e]));
-        }
-        filled = kDynAhead;
-        claiming = P.dyn_first + t0 + kDynAhead - 1 < G;
-    };
-    if (producer && trig <= 0) {
-        publish_batch(atom_add_relaxed_gpu(P.dyn_claim, kDynAhead));
-        drawn = true;
-        pend = -1;
-    }
-    // copies of the rest of the ring
-    auto issue_next = [&](int s) -> bool {
-        if (issued < ns) {
-            issue_weights<NC, BASE>(P, si, ring + s * kSB, full[s], lane);
-            issue_acts<NC, BASE>(P, si, ring + s * kSB, full[s], lane);
-            advance(P, si);
-        } else {
-            mix_resolve<R>(P, ic, q_group, q_bar, warp, ok);
-            if (!ok || ic.gi < 0) return false;
-            issue_weights<NC, BASE>(P, ic.c, ring + s * kSB, full[s], lane);
-            issue_acts<NC, BASE>(P, ic.c, ring + s * kSB, full[s], lane);
-            dyn_step(ic);
-        }
-        ++issued;
-        return true;
-    };
-    while (ok && issued < kStages && issue_next(issued % kStages)) {
-    }
-
-    RowAcc<NC> acc, gacc;
-    RowAccD<NC> dacc;  // unused
-    acc.clear();
-    gacc.clear();
-    int done = 0;
-    int open_t = -1, open_g = -1;  // static phase: the open row group
-    int group_k = -1;              // producer: last dynamic group whose claim duties ran
-#if Q4K_TIMELINE
-    uint64_t tl_static_end = 0;    // when this warp's sums left its static range
-#endif
-    while (ok) {
-        if (producer) {
-            if (!drawn && done >= trig) {
-                pend = atom_add_relaxed_gpu(P.dyn_claim, kDynAhead);  // read next iteration
-                drawn = true;
-            } else if (drawn && pend >= 0 && filled == 0) {
-                publish_batch(pend);
-                pend = -1;
-            }
-        }
-        const bool stat = done < ns;
-        if (stat) {
-            if (sc.t != open_t || sc.g != open_g) {
-                if (open_t >= 0) {
-                    AtomCursor o{open_t, open_g, 0};
-                    flush_group<NC, NC, BASE>(P, o, acc, gacc, dacc, worker, a0, a1, lane, 0, cta_w0, cta_w1,
-                                              cta_cnt);
-                }
-                open_t = sc.t;
-                open_g = sc.g;
-                acc.clear();
-            }
-        } else {
-#if Q4K_TIMELINE
-            if (tl_static_end == 0) tl_static_end = globaltimer_ns();
-#endif
-            if (open_t >= 0) {  // the static range ended with the previous atom
-                AtomCursor o{open_t, open_g, 0};
-                flush_group<NC, NC, BASE>(P, o, acc, gacc, dacc, worker, a0, a1, lane, 0, cta_w0, cta_w1,
-                                          cta_cnt);
-                open_t = -1;
-                acc.clear();
-            }
-            if (producer && filled == 0 && drawn) {  // the first batch, before it is needed
-                publish_batch(pend);
-                pend = -1;
-            }
-            mix_resolve<R>(P, cc, q_group, q_bar, warp, ok);
-            if (!ok || cc.gi < 0) break;
-            if (producer && cc.k != group_k) {
-                group_k = cc.k;
-                if (claiming && cc.k >= 1) {
-                    const int gi = P.dyn_first + pend;
-                    const int e = filled++;
-                    q_group[e % kDynQ] = gi < G ? gi : -1;
-                    mbar_arrive(smem_addr(&q_bar[e % kDynQ]));
-                    claiming = gi < G;
-                }
-                if (claiming) pend = atom_add_relaxed_gpu(P.dyn_claim, 1);
-            }
-        }
-        const int s = done % kStages;
-        ok = wait_phase(full[s], static_cast<uint32_t>((done / kStages) & 1), kWaitLimitNs);
-        if (!ok) break;
-        compute_atom<NC, NC, BASE>(P, stat ? sc : cc.c, ring + s * kSB, lane, 0, acc, gacc, dacc);
-        __syncwarp();
-        fence_proxy_async_smem();
-        issue_next(s);
-        if (!ok) break;
-        ++done;
-        if (stat) {
-            advance(P, sc);
-            continue;
-        }
-        if (++cc.c.kp < cc.s1) continue;
-        cc.need = true;
-        // this warp's share of dynamic group cc.gi: deposit; the last warp adds up
-        const int b = cc.k & 1;
-        const int use = cc.k >> 1;
-        if (use >= 1) {
-            ok = wait_phase(smem_addr(&free_bar[b]), static_cast<uint32_t>((use - 1) & 1), kWaitLimitNs);
-            if (!ok) break;
-        }
-#pragma unroll
-        for (int j = 0; j < NC; ++j) part[b][warp][j][lane] = acc.value(j);
-        __syncwarp();
-        int old = 0;
-        if (lane == 0) {
-            __threadfence_block();
-            old = atomicAdd(&red_cnt[b], 1);
-        }
-        old = __shfl_sync(0xffffffffu, old, 0);
-        if (old == R - 1) {
-            __threadfence_block();
-            __syncwarp();
-            const TaskDesc &T = P.task[cc.c.t];
-            const int row = cc.c.g * 32 + lane;
-#pragma unroll
-            for (int j = 0; j < NC; ++j) {
-                float tot = 0.0f;
-#pragma unroll
-                for (int w = 0; w < R; ++w) tot += part[b][w][j][lane];
-                if (row < T.nrows) store_final<false>(P, T, j, row, tot, 0.0f);
-            }
-            __syncwarp();
-            if (lane == 0) {
-                red_cnt[b] = 0;
-                mbar_arrive(smem_addr(&free_bar[b]));
-            }
-        }
-        acc.clear();
-    }
-    if (ok && open_t >= 0) {  // a static range that never reached the dynamic part
-        AtomCursor o{open_t, open_g, 0};
-        flush_group<NC, NC, BASE>(P, o, acc, gacc, dacc, worker, a0, a1, lane, 0, cta_w0, cta_w1, cta_cnt);
-    }
-    if (!ok) {
-        if (lane == 0) atomicExch(P.status, kStatusTimeout);
-        for (int i = done; i < issued; ++i)
-            wait_phase(full[i % kStages], static_cast<uint32_t>((i / kStages) & 1), kDrainLimitNs);
-    }
-#if Q4K_TIMELINE
-    if (lane == 0 && P.tl != nullptr && blockIdx.x < Q4K_TIMELINE_CTAS && warp < 16) {
-        unsigned long long *o =
-            P.tl + ((static_cast<int64_t>(P.tl_slot) * Q4K_TIMELINE_CTAS + blockIdx.x) * 16 + warp) * 8;
-        uint32_t smid;
-        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-        o[0] = tl_start;
-        o[1] = tl_wait;
-        o[2] = globaltimer_ns();
-        o[3] = static_cast<unsigned long long>(done > 0 ? done : 1);
-        o[4] = smid;
-        o[5] = static_cast<unsigned long long>(worker);
-        o[6] = tl_static_end;  // 0: the warp never left its static range
-        o[7] = static_cast<unsigned long long>(cc.k);
-    }
-#endif
-}
-
-// ============================================================================
 // host-side launchers
 // ============================================================================
 namespace {
@@ -1795,38 +1544,6 @@ cudaError_t set_attrs_dyn() {
     if ((e = set_attrs_dyn1<6, BASE>()) != cudaSuccess) return e;
     if ((e = set_attrs_dyn1<7, BASE>()) != cudaSuccess) return e;
     return set_attrs_dyn1<8, BASE>();
-}
-
-template <int NC>
-cudaError_t set_attrs_mix1() {
-    return cudaFuncSetAttribute(k_gemv_mix<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                smem_m(NC, kModeMixPlain));
-}
-
-cudaError_t set_attrs_mix() {
-    cudaError_t e;
-    if ((e = set_attrs_mix1<1>()) != cudaSuccess) return e;
-    if ((e = set_attrs_mix1<2>()) != cudaSuccess) return e;
-    if ((e = set_attrs_mix1<3>()) != cudaSuccess) return e;
-    if ((e = set_attrs_mix1<4>()) != cudaSuccess) return e;
-    if ((e = set_attrs_mix1<5>()) != cudaSuccess) return e;
-    if ((e = set_attrs_mix1<6>()) != cudaSuccess) return e;
-    if ((e = set_attrs_mix1<7>()) != cudaSuccess) return e;
-    return set_attrs_mix1<8>();
-}
-
-void *gemv_fn_mix(int ncols) {
-    switch (ncols) {
-        case 1: return reinterpret_cast<void *>(k_gemv_mix<1>);
-        case 2: return reinterpret_cast<void *>(k_gemv_mix<2>);
-        case 3: return reinterpret_cast<void *>(k_gemv_mix<3>);
-        case 4: return reinterpret_cast<void *>(k_gemv_mix<4>);
-        case 5: return reinterpret_cast<void *>(k_gemv_mix<5>);
-        case 6: return reinterpret_cast<void *>(k_gemv_mix<6>);
-        case 7: return reinterpret_cast<void *>(k_gemv_mix<7>);
-        case 8: return reinterpret_cast<void *>(k_gemv_mix<8>);
-        default: return nullptr;
-    }
 }
 
 template <int BASE>
@@ -1899,7 +1616,6 @@ cudaError_t device_setup(int *num_sms) {
         if ((e = set_attrs_all<kModeQ6>()) != cudaSuccess) return e;
         if ((e = set_attrs_dyn<kModePlain>()) != cudaSuccess) return e;
         if ((e = set_attrs_dyn<kModeGated>()) != cudaSuccess) return e;
-        if ((e = set_attrs_mix()) != cudaSuccess) return e;
         st.ready = true;
     }
     *num_sms = st.num_sms;
@@ -1928,6 +1644,20 @@ cudaError_t launch_prep(const PrepParams &p, cudaStream_t s) {
     return cudaLaunchKernelEx(&cfg, k_prep, p);
 }
 
+cudaError_t launch_gather_wait(const GatherWait &g, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_gather_wait, g);
+}
+
 cudaError_t launch_gemv(const GemvParams &p, int ncols, int mode, int grid, cudaStream_t s) {
     void *fn = mode == kModeDump    ? gemv_fn<kModeDump>(ncols)
                : mode == kModeGated ? gemv_fn<kModeGated>(ncols)
@@ -1935,7 +1665,6 @@ cudaError_t launch_gemv(const GemvParams &p, int ncols, int mode, int grid, cuda
                : mode == kModeQ6    ? gemv_fn<kModeQ6>(ncols)
                : mode == kModeDynPlain ? gemv_fn_dyn<kModePlain>(ncols)
                : mode == kModeDynGated ? gemv_fn_dyn<kModeGated>(ncols)
-               : mode == kModeMixPlain ? gemv_fn_mix(ncols)
                                     : gemv_fn<kModePlain>(ncols);
     if (fn == nullptr) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};

@@ -21,7 +21,6 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
-#include <mutex>
 
 namespace {
 
@@ -31,25 +30,16 @@ constexpr size_t kScratchBytes = size_t(4) << 20;  // 4 MiB per device
 // kernels get its device address from cudaGetSymbolAddress (below).
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_mu;
-void *g_scratch_ptr[kMaxDevices] = {};
-
-// Device address of the scratch array on the current device, looked up once
-// per device with that device current.  Returns a CUDA error on failure.
+// Device address of the scratch array on the current device.  Looked up on
+// every call (the lookup allocates nothing and is cheap), so the address
+// stays right if the device's context is reset and the module reloaded
+// somewhere else.  The first lookup on a device can load the module; make
+// that first call before any stream capture.
 cudaError_t scratch_address(void **out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (g_scratch_ptr[dev] == nullptr) {
-        void *p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess) return e;
-        g_scratch_ptr[dev] = p;
-    }
-    *out = g_scratch_ptr[dev];
+    *out = p;
     return cudaSuccess;
 }
 

@@ -250,9 +250,16 @@ Q4K_API int q4k_gemv_batch_q6_k(const q4k_task *tasks, int ntasks, int ncols, vo
 /* Row-split across GPUs is the reference's multi-GPU mode (mmvq.cu:764-793,
  * the main device then collects the slices).  Here every rank computes its
  * rows and, in the same kernel, stores them straight into every rank's full
- * output buffer over NVLink (peer memory), then exchanges one epoch flag with
- * each peer: when the launch completes on a rank, that rank's buffer holds
- * all rows.  Every rank must make the same sequence of calls. */
+ * output buffer over NVLink (peer memory); its last CTA then raises this
+ * rank's epoch flag in every peer and the launch ends without waiting for
+ * the peers.  The peers' rows of a call are in this rank's buffer once every
+ * peer's flag has reached this rank's epoch, which two things wait for
+ * (bounded, 2 s, then Q4K_ETIMEOUT in the workspace status word):
+ *   - the next gathering call on the stream, before it reads its activations
+ *     (so a chain whose activations come from gathered outputs is safe), and
+ *   - q4k_gather_wait, which the caller issues before anything else on the
+ *     stream reads the gathered buffer (e.g. before copying it to the host).
+ * Every rank must make the same sequence of calls. */
 #define Q4K_MAX_PEERS 8
 
 typedef struct q4k_gather {
@@ -263,17 +270,27 @@ typedef struct q4k_gather {
                                          (out_peer[rank] == out_local) */
     uint32_t *flags_peer[Q4K_MAX_PEERS]; /* each rank's flag words (world of them), mapped here */
     uint32_t *epoch;                  /* this rank's epoch word, zero before the first call */
+    int64_t out_elems;                /* floats in every rank's full output buffer; every
+                                         task's dst columns must lie inside it */
 } q4k_gather;
 
 /* q4k_gemv_batch over this rank's row shards, gathered into every rank's
  * buffer.  Each task's dst must point into out_local at this rank's first
- * row of that matrix (all ranks use the same layout of the full buffer).
+ * row of that matrix (all ranks use the same layout of the full buffer);
+ * a task whose columns reach outside [out_local, out_local + out_elems) is
+ * rejected with Q4K_EINVAL before anything is launched.
  * A rank stores into its peers' buffers as soon as its launch runs: a region
  * of the full buffer may be rewritten only once every rank is done reading
  * it (use different regions for consecutive calls, e.g. one per layer, or
  * synchronise the ranks before reuse). */
 Q4K_API int q4k_gemv_batch_allgather(const q4k_task *tasks, int ntasks, int ncols, const q4k_gather *gather,
                                      void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+/* Stream-ordered wait until every peer's rows of the last gathering call on
+ * this rank are in out_local (one small launch).  A wait that gives up after
+ * 2 s writes Q4K_ETIMEOUT into the workspace status word (workspace: the one
+ * the gathering calls use, at least 4 bytes). */
+Q4K_API int q4k_gather_wait(const q4k_gather *gather, void *workspace, size_t workspace_bytes,
+                            q4k_stream_t stream);
 
 /* ---- single-launch path (no reference counterpart) --------------------------- */
 
@@ -329,7 +346,8 @@ Q4K_API size_t q4k_noalloc_scratch_bytes(void);
 /* ---- diagnostics ------------------------------------------------------------- */
 
 /* Which GEMV kernel q4k_gemv_batch_ex (or q4k_gemv_batch) would run for these
- * tasks on a device with num_sms SMs, under this process's Q4K_SCHED setting.
+ * tasks on a device with num_sms SMs (the library's measured choice; builds
+ * made with -DQ4K_SCHED_FORCE for measurements force one kernel).
  * Touches no device.  Returns a Q4K_KERNEL_* value, or -1 (reason in
  * q4k_last_error()) for tasks the call would reject.  No counterpart in the
  * reference, which has one kernel per ncols. */
@@ -338,7 +356,6 @@ Q4K_API size_t q4k_noalloc_scratch_bytes(void);
 #define Q4K_KERNEL_STATIC_TWO_ROW 3  /* the same, two rows per lane (ncols >= 3) */
 #define Q4K_KERNEL_DYNAMIC 5         /* whole row groups per CTA from a ticket queue */
 #define Q4K_KERNEL_DYNAMIC_GATED 6   /* the same with the bias / GLU epilogue */
-#define Q4K_KERNEL_MIXED 7           /* static prefix + dynamic tail (Q4K_SCHED=mixed) */
 Q4K_API int q4k_batch_ex_kernel(const q4k_task_ex *tasks, int ntasks, int ncols, int num_sms);
 
 /* Per-sub-block integer sums as the kernels form them, for bit-exact parity
@@ -367,12 +384,14 @@ Q4K_API int q4k_workspace_status(const void *workspace, int *device_status, q4k_
  *   GEMV  u64[slot][Q4K_TIMELINE_CTAS][16 warps][8] =
  *         {start, wait return, end, atoms of the worker (0: idle), SM id,
  *          worker index, first atom, end atom}; the dynamically scheduled
- *          kernels record atoms done in word 3, and in words 6 and 7 the time
- *          the warp left its static range (static-prefix kernel; else 0) and
- *          its last queue entry
+ *          kernel records atoms done in word 3, 0 in word 6 and its last
+ *          queue entry in word 7
  *   prep  u64[slot][Q4K_TIMELINE_PREP_CTAS][4] = {start, wait return, end, 1}
  * q4k_timeline_bytes() is the size of both regions (GEMV first); it returns 0
- * and the other two Q4K_EINVAL in a library built without the option. */
+ * and the other two Q4K_EINVAL in a library built without the option.  Each
+ * device keeps its own buffer; read and reset act on the current device's.
+ * The timeline build allocates that buffer at its first call on a device, so
+ * in that build q4k_mul_mat_vec_noalloc does allocate (once per device). */
 #define Q4K_TIMELINE_SLOTS 64
 #define Q4K_TIMELINE_CTAS 256
 #define Q4K_TIMELINE_PREP_CTAS 4096

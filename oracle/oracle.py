@@ -31,13 +31,24 @@ _c_i64 = ctypes.c_int64
 _c_p = ctypes.c_void_p
 
 
+def reference_dir() -> Path | None:
+    """The reference checkout: $Q4K_REFERENCE, else a `reference` directory
+    beside this repository's checkout; None when neither exists."""
+    env = os.environ.get("Q4K_REFERENCE")
+    if env:
+        return Path(env)
+    sibling = HERE.parent.parent / "reference"
+    return sibling if sibling.is_dir() else None
+
+
 def build(force: bool = False) -> None:
     """Build the checkers (make in oracle/).  Cheap; safe to call repeatedly."""
     if force or not ORACLE_SO.exists():
         subprocess.run(["make", "-C", str(HERE), "liboracle_q4k.so"], check=True,
                        stdout=subprocess.DEVNULL)
-    ref_src = Path(os.environ.get("Q4K_REFERENCE", "/root/reference")) / "kernels" / "vecdotq.cuh"
-    if ref_src.exists() and (force or not REF_SO.exists()):
+    ref_dir = reference_dir()
+    ref_src = ref_dir / "kernels" / "vecdotq.cuh" if ref_dir is not None else None
+    if ref_src is not None and ref_src.exists() and (force or not REF_SO.exists()):
         subprocess.run(["make", "-C", str(HERE), "ref", f"REF={ref_src.parent.parent}"],
                        check=True, stdout=subprocess.DEVNULL)
 
@@ -89,6 +100,10 @@ def ref_lib() -> ctypes.CDLL:
         L.ref_vec_dot_q4_K_q8_1.argtypes = [_c_p, _c_p, ctypes.c_int, ctypes.c_int]
         L.ref_vec_dot_q4_K_q8_1.restype = ctypes.c_float
         L.ref_gemv_q4k_q8_1.argtypes = [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, ctypes.c_int,
+                                        _c_p, _c_i64, ctypes.c_int]
+        L.ref_vec_dot_q6_K_q8_1.argtypes = [_c_p, _c_p, ctypes.c_int, ctypes.c_int]
+        L.ref_vec_dot_q6_K_q8_1.restype = ctypes.c_float
+        L.ref_gemv_q6k_q8_1.argtypes = [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, ctypes.c_int,
                                         _c_p, _c_i64, ctypes.c_int]
         L.ref_max_threads.restype = ctypes.c_int
         _ref = L
@@ -200,6 +215,25 @@ def ref_gemv_q8_1(W: np.ndarray, K: int, yq: np.ndarray, nthreads: int = 0) -> n
     ref_lib().ref_gemv_q4k_q8_1(_ptr(W), nrows, K, W.shape[1] // Q4K_BYTES, _ptr(yq),
                                 yq.shape[1] // Q81_BYTES, ncols, _ptr(out), nrows, nthreads)
     return out
+
+
+def ref_gemv_q6k_q8_1(W: np.ndarray, K: int, yq: np.ndarray, nthreads: int = 0) -> np.ndarray:
+    """The reference's own vec_dot_q6_K_q8_1 (kernels/vecdotq.cuh:867-890) in
+    upstream MMVQ's summation order, over Q6_K rows (nrows, K/256*210)."""
+    W = np.ascontiguousarray(W, dtype=np.uint8)
+    yq = np.ascontiguousarray(yq, dtype=np.uint8)
+    nrows, ncols = W.shape[0], yq.shape[0]
+    out = np.empty((ncols, nrows), dtype=np.float32)
+    ref_lib().ref_gemv_q6k_q8_1(_ptr(W), nrows, K, W.shape[1] // Q6K_BYTES, _ptr(yq),
+                                yq.shape[1] // Q81_BYTES, ncols, _ptr(out), nrows, nthreads)
+    return out
+
+
+def ref_vec_dot_q6k(sb: np.ndarray, q8: np.ndarray, iqs: int) -> float:
+    """Reference vec_dot_q6_K_q8_1 on one super-block (210 B) and its 8 q8_1 blocks."""
+    sb = np.ascontiguousarray(sb, dtype=np.uint8)
+    q8 = np.ascontiguousarray(q8, dtype=np.uint8)
+    return float(ref_lib().ref_vec_dot_q6_K_q8_1(_ptr(sb), _ptr(q8), 0, iqs))
 
 
 def ref_vec_dot(sb: np.ndarray, q8: np.ndarray, iqs: int) -> float:

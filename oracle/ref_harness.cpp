@@ -1,4 +1,5 @@
-// ref_harness.cpp -- runs the REFERENCE's own Q4_K x q8_1 dot product on the CPU.
+// ref_harness.cpp -- runs the REFERENCE's own Q4_K x q8_1 and Q6_K x q8_1 dot
+// products on the CPU.
 //
 // TEST INFRASTRUCTURE ONLY.  Compiled by oracle/Makefile together with the
 // reference's unmodified kernels/vecdotq.cuh (included from where it lies in
@@ -20,22 +21,36 @@ float ref_vec_dot_q4_K_q8_1(const void *vbq, const void *bq8_1, int kbx, int iqs
     return vec_dot_q4_K_q8_1(vbq, (const block_q8_1 *)bq8_1, kbx, iqs);
 }
 
-// One output value the way upstream mul_mat_vec_q<Q4_K, ncols_dst, false>
-// forms it (kernels/mmvq.cu:150-338): nwarps*32 threads, thread tid visits
-// super-blocks kbx = tid/16, tid/16 + 2*nwarps, ... (mmvq.cu:236) with
-// kqs = 2*(tid%16) (mmvq.cu:240), accumulates tmp += vec_dot in float
-// (mmvq.cu:246), warps 1..nwarps-1 are added into warp 0 in order
+// kernels/vecdotq.cuh:867-890, called exactly as the MMVQ kernel calls it.
+float ref_vec_dot_q6_K_q8_1(const void *vbq, const void *bq8_1, int kbx, int iqs) {
+    return vec_dot_q6_K_q8_1(vbq, (const block_q8_1 *)bq8_1, kbx, iqs);
+}
+
+// One output value the way upstream mul_mat_vec_q<type, ncols_dst, false>
+// forms it (kernels/mmvq.cu:150-338): nwarps*32 threads; with qi the ints of
+// quants per super-block and vdr the ints one call consumes, thread tid
+// visits super-blocks kbx = tid/(qi/vdr), + blocks_per_iter, ... (mmvq.cu:236)
+// with blocks_per_iter = vdr*nwarps*32/qi (mmvq.cu:172) and
+// kqs = vdr*(tid%(qi/vdr)) (mmvq.cu:240), accumulates tmp += vec_dot in
+// float (mmvq.cu:246), warps 1..nwarps-1 are added into warp 0 in order
 // (mmvq.cu:293-294), then a 32-lane xor-butterfly (mmvq.cu:301).
 // nwarps = 4 for ncols_dst <= 4 and 2 for 5..8 (mmvq.cu:95-110).
-static float mmvq_value(const block_q4_K *row, const block_q8_1 *ycol, int nb, int nwarps) {
+// Q4_K: qi = QI4_K = 32, vdr = VDR_Q4_K_Q8_1_MMVQ = 2; Q6_K: qi = QI6_K = 32,
+// vdr = VDR_Q6_K_Q8_1_MMVQ = 1 (vecdotq.cuh:576); both 8 q8_1 blocks per
+// super-block (kby = 8*kbx, mmvq.cu:237).
+typedef float (*VecDot)(const void *, const block_q8_1 *, const int &, const int &);
+
+static float mmvq_value(VecDot dot, int vdr, const void *row, const block_q8_1 *ycol, int nb, int nwarps) {
+    const int qi = 32;
     const int nthreads = nwarps * 32;
-    const int blocks_per_iter = 2 * nwarps;  // vdr*nwarps*warp_size/qi = 2*nwarps*32/32
+    const int tpb = qi / vdr;                         // threads per super-block
+    const int blocks_per_iter = vdr * nwarps * 32 / qi;
     float tmp[8 * 32];
     for (int tid = 0; tid < nthreads; ++tid) {
         float t = 0.0f;
-        const int kqs = 2 * (tid % 16);
-        for (int kbx = tid / 16; kbx < nb; kbx += blocks_per_iter) {
-            t += vec_dot_q4_K_q8_1(row, &ycol[kbx * 8], kbx, kqs);
+        const int kqs = vdr * (tid % tpb);
+        for (int kbx = tid / tpb; kbx < nb; kbx += blocks_per_iter) {
+            t += dot(row, &ycol[kbx * 8], kbx, kqs);
         }
         tmp[tid] = t;
     }
@@ -53,14 +68,12 @@ static float mmvq_value(const block_q4_K *row, const block_q8_1 *ycol, int nb, i
     return lane[0];
 }
 
-// GEMV over ggml q8_1 activations with the strides of kernels/mmvq.cu:233-247,
-// :285, :337.  ncols in 1..8.
-void ref_gemv_q4k_q8_1(const void *W, int64_t nrows, int64_t K, int64_t stride_row_blocks,
-                       const void *y_q8_1, int64_t stride_col_y_blocks, int ncols,
-                       float *dst, int64_t stride_col_dst, int nthreads) {
+static void mmvq_gemv(VecDot dot, int vdr, size_t sb_bytes, const void *W, int64_t nrows, int64_t K,
+                      int64_t stride_row_blocks, const void *y_q8_1, int64_t stride_col_y_blocks, int ncols,
+                      float *dst, int64_t stride_col_dst, int nthreads) {
     const int nb = (int)(K / QK_K);
     const int nwarps = ncols <= 4 ? 4 : 2;
-    const block_q4_K *w = (const block_q4_K *)W;
+    const uint8_t *w = (const uint8_t *)W;
     const block_q8_1 *y = (const block_q8_1 *)y_q8_1;
 #ifdef _OPENMP
     if (nthreads <= 0) nthreads = omp_get_max_threads();
@@ -68,11 +81,28 @@ void ref_gemv_q4k_q8_1(const void *W, int64_t nrows, int64_t K, int64_t stride_r
 #endif
     for (int64_t r = 0; r < nrows; ++r) {
         for (int j = 0; j < ncols; ++j) {
-            dst[(int64_t)j * stride_col_dst + r] =
-                mmvq_value(w + r * stride_row_blocks, y + (int64_t)j * stride_col_y_blocks, nb, nwarps);
+            dst[(int64_t)j * stride_col_dst + r] = mmvq_value(dot, vdr, w + r * stride_row_blocks * sb_bytes,
+                                                              y + (int64_t)j * stride_col_y_blocks, nb, nwarps);
         }
     }
     (void)nthreads;
+}
+
+// GEMV over ggml q8_1 activations with the strides of kernels/mmvq.cu:233-247,
+// :285, :337.  ncols in 1..8.
+void ref_gemv_q4k_q8_1(const void *W, int64_t nrows, int64_t K, int64_t stride_row_blocks,
+                       const void *y_q8_1, int64_t stride_col_y_blocks, int ncols,
+                       float *dst, int64_t stride_col_dst, int nthreads) {
+    mmvq_gemv(vec_dot_q4_K_q8_1, VDR_Q4_K_Q8_1_MMVQ, sizeof(block_q4_K), W, nrows, K, stride_row_blocks, y_q8_1,
+              stride_col_y_blocks, ncols, dst, stride_col_dst, nthreads);
+}
+
+// The same for Q6_K rows (mul_mat_vec_q<GGML_TYPE_Q6_K, ...>).
+void ref_gemv_q6k_q8_1(const void *W, int64_t nrows, int64_t K, int64_t stride_row_blocks,
+                       const void *y_q8_1, int64_t stride_col_y_blocks, int ncols,
+                       float *dst, int64_t stride_col_dst, int nthreads) {
+    mmvq_gemv(vec_dot_q6_K_q8_1, VDR_Q6_K_Q8_1_MMVQ, sizeof(block_q6_K), W, nrows, K, stride_row_blocks, y_q8_1,
+              stride_col_y_blocks, ncols, dst, stride_col_dst, nthreads);
 }
 
 int ref_max_threads(void) {

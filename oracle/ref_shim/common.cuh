@@ -3,9 +3,9 @@
 // Written for this project so that the reference's own dot-product code can
 // be compiled with g++ and run on the CPU as the pin for oracle/q4k_oracle.c.
 //
-// Only block_q4_K and block_q8_1 are exercised; their layouts are the format
-// contract (144 and 36 bytes, asserted below as the reference asserts them at
-// kernels/w_tile.cu:6-7).  Every other block type, table and constant exists
+// Only block_q4_K, block_q6_K and block_q8_1 are exercised; their layouts are
+// the format contract (144, 210 and 36 bytes, asserted below; the reference
+// asserts the first and last at kernels/w_tile.cu:6-7).  Every other block type, table and constant exists
 // only so that the header's other (never called) functions compile; their
 // member lists follow the member names the header uses and their values are
 // placeholders.
@@ -63,7 +63,9 @@ struct block_mxfp4 { uint8_t e; uint8_t qs[16]; };
 struct block_q2_K { uint8_t scales[16]; uint8_t qs[64]; half2 dm; };
 struct block_q3_K { uint8_t hmask[32]; uint8_t qs[64]; uint8_t scales[12]; half d; };
 struct block_q5_K { half2 dm; uint8_t scales[12]; uint8_t qh[32]; uint8_t qs[128]; };
+// Q6_K: ql[128] low nibbles, qh[64] high 2 bits, 16 int8 scales, fp16 d.
 struct block_q6_K { uint8_t ql[128]; uint8_t qh[64]; int8_t scales[16]; half d; };
+static_assert(sizeof(block_q6_K) == 210, "block_q6_K size mismatch");
 struct block_iq2_xxs { half d; uint16_t qs[32]; };
 struct block_iq2_xs { half d; uint16_t qs[32]; uint8_t scales[8]; };
 struct block_iq2_s { half d; uint8_t qs[64]; uint8_t qh[8]; uint8_t scales[8]; };

@@ -21,6 +21,12 @@ Outputs (numpy .npz, a few hundred KB in total):
                    (or T_s), a small integer that fp32 holds exactly.
   q8_1_kat.npz     hand-made q8_1 quantization cases (zeros, saturation,
                    ties, padding) with their expected blocks.
+  gemv_q6k_<name>.npz  the same as gemv_<name>.npz for Q6_K weights (210-byte
+                   super-blocks), y_ref = the reference's vec_dot_q6_K_q8_1
+                   (kernels/vecdotq.cuh:867-890, VDR 1 at :576) in MMVQ order.
+  q6k_subblock_sums.npz  exact per-16-weight sums S = sum (q6 - 32) * q8 of
+                   seeded Q6_K super-blocks, read out of the reference's dot
+                   product with d = 1, one scale = 1 and the others 0, d8 = 1.
 """
 from __future__ import annotations
 
@@ -140,6 +146,57 @@ def q8_kat():
     np.savez_compressed(HERE / "q8_1_kat.npz", x=x[:, :Kv].copy(), yq=yq, Kpad=np.int64(512))
 
 
+Q6 = 210
+
+
+def gen_w6(rng, nrows, K):
+    """Q6_K rows: ql/qh/scales bytes uniform, d = fp16(|N(0,1)|*0.01)."""
+    nb = K // QK_K
+    W = rng.integers(0, 256, size=(nrows, nb, Q6), dtype=np.uint8)
+    d = (np.abs(rng.standard_normal((nrows, nb))) * 0.01).astype(np.float16)
+    W[:, :, 208:210] = d.view(np.uint8).reshape(nrows, nb, 2)
+    return W.reshape(nrows, nb * Q6)
+
+
+def gemv_q6k_case(name, seed, nrows, K, ncols):
+    rng = np.random.default_rng(seed)
+    W = gen_w6(rng, nrows, K)
+    x = rng.standard_normal((ncols, K)).astype(np.float32)
+    yq = O.quantize_q8_1(x)
+    y_ref = O.ref_gemv_q6k_q8_1(W, K, yq)
+    np.savez_compressed(HERE / f"gemv_q6k_{name}.npz", W=W, x=x, yq=yq, y_ref=y_ref,
+                        meta=np.array([nrows, K, ncols, seed], dtype=np.int64))
+    return W.nbytes + x.nbytes
+
+
+def q6k_subblock_case(seed=11, nsb=12):
+    """S[i, s] = sum over the 16 weights of sub-block s of (q6 - 32) * q8, from the
+    reference's dot product summed over all 32 threads of a super-block
+    (iqs = 0..31, VDR 1): with d = 1, scales = one-hot at s and every q8
+    block's d8 = 1 it returns exactly that integer."""
+    rng = np.random.default_rng(seed)
+    W = gen_w6(rng, nsb, QK_K).reshape(nsb, Q6)
+    W[1, 0:192] = 0xFF  # every 6-bit value 63 (+31 after the offset)
+    W[2, 0:192] = 0x00  # every value 0 (-32)
+    x = rng.standard_normal((1, nsb * QK_K)).astype(np.float32)
+    x[0, 32:64] = 1000.0   # a saturating block
+    x[0, 64:96] = -1000.0
+    yq = O.quantize_q8_1(x, Kpad=nsb * QK_K).reshape(nsb, 8, 36).copy()
+    yq[:, :, 0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)  # d8 = 1
+    yq = yq.reshape(nsb, 8 * 36)
+    S = np.zeros((nsb, 16), np.int32)
+    for i in range(nsb):
+        for s in range(16):
+            h = W[i].copy()
+            h[192:208] = 0
+            h[192 + s] = 1
+            h[208:210] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)
+            v = sum(O.ref_vec_dot_q6k(h, yq[i], iqs) for iqs in range(32))
+            assert v == int(v)
+            S[i, s] = int(v)
+    np.savez_compressed(HERE / "q6k_subblock_sums.npz", W=W, yq=yq, S=S)
+
+
 def main():
     assert O.ref_available(), "oracle/_ref missing: run make -C oracle with the reference present"
     total = 0
@@ -152,6 +209,11 @@ def main():
     total += gemv_case("cfg1_k4096_r16_c1", 0, 16, 4096, 1, full_rows=4096)
     subblock_case()
     q8_kat()
+    # Q6_K (K a multiple of 2048, as the GPU path needs): odd row counts, batch 1..8
+    total += gemv_q6k_case("k2048_r9_c1", 21, 9, 2048, 1)
+    total += gemv_q6k_case("k4096_r17_c2", 22, 17, 4096, 2)
+    total += gemv_q6k_case("k8192_r8_c8", 23, 8, 8192, 8)
+    q6k_subblock_case()
     print("golden fixtures written; raw payload bytes", total)
 
 

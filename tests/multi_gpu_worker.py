@@ -1,11 +1,12 @@
 """One rank of the fused GEMV + all-gather check (run under torchrun, >= 2 GPUs).
 
 Every rank generates the same full matrices (same seed), computes its
-contiguous row shard with q4k_gemv_batch_allgather, and then checks that its
-own full output buffer -- filled by all ranks' kernels over NVLink -- matches
-the single-GPU GEMV of the full matrices, for several consecutive calls and
-for replays of a captured CUDA graph (the epoch handshake keeps counting).
-Exit status 0 on success.  Used by tests/test_multi_gpu.py.
+contiguous row shard with q4k_gemv_batch_allgather, waits for its peers'
+rows (q4k_gather_wait), and then checks that its own full output buffer --
+filled by all ranks' kernels over NVLink -- matches the CPU oracle's GEMV of
+the full matrices (1e-4 absolute + 1e-5 relative), for several consecutive
+calls and for replays of a captured CUDA graph (the epoch handshake keeps
+counting).  Exit status 0 on success.  Used by tests/test_multi_gpu.py.
 """
 from __future__ import annotations
 
@@ -21,6 +22,7 @@ import torch.distributed as dist
 
 sys.path.insert(0, str(Path(__file__).resolve().parent))
 from conftest import load_package  # noqa: E402
+import oracle as O  # noqa: E402  (tests/conftest.py puts oracle/ on the path; the checker only)
 
 TOL_ABS, TOL_REL = 1e-4, 1e-5
 
@@ -37,7 +39,7 @@ def main():
     g.manual_seed(77)  # identical on every rank
     fullW = [q4k.gen_q4k_torch(r, K, generator=g, device=dev) for r, K in shapes]
     xs = [torch.randn((ncols, K), device=dev, generator=g) for _, K in shapes]
-    ref = [q4k.mul_mat_vec_q(W, x) for W, x in zip(fullW, xs)]
+    ref = [torch.from_numpy(O.gemv_f32(W.cpu().numpy(), x.cpu().numpy())).to(dev) for W, x in zip(fullW, xs)]
 
     # full-output layout (same on every rank): matrix t at off[t], column stride = rows
     off, tot = [], 0
@@ -72,6 +74,7 @@ def main():
             s.synchronize()
             dist.barrier()
             q4k.gemv_batch_allgather(tasks, ncols, pg, ws, stream=s)
+            q4k.gather_wait(pg, ws, stream=s)
             s.synchronize()
             dist.barrier()
             assert ws.status(s) == 0
@@ -80,6 +83,7 @@ def main():
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=s):
             q4k.gemv_batch_allgather(tasks, ncols, pg, ws, stream=s)
+            q4k.gather_wait(pg, ws, stream=s)
         for it in range(3):
             dist.barrier()
             pg.out.fill_(float("nan"))

@@ -189,8 +189,8 @@ MISTRAL_SPECS = [(4096, 4096, 0, False), (1024, 4096, 0, False), (1024, 4096, 0,
     ([(14336, 2048, 0, True)], 1, "k_gemv_dyn (epilogue)"),    # fused, spread
 ])
 def test_kernel_choice(q4k, specs, ncols, want):
-    if "Q4K_SCHED" in __import__("os").environ:
-        pytest.skip("Q4K_SCHED overrides the measured choice")
+    if "Q4K_LIB" in __import__("os").environ:
+        pytest.skip("another build of the library (it may force one kernel)")
     assert q4k.batch_kernel(_tasks_ex(q4k, specs), ncols, num_sms=148) == want
 
 

@@ -12,10 +12,6 @@ exactly once, and every reduction sees the R shares of that group.  A
 variant whose copy cursor reads the next queue entry eagerly (as soon as it
 passes its last atom of a group) deadlocks: warp 0 then waits for an entry
 that only it publishes, which is why the kernel reads entries lazily.
-
-The second model covers k_gemv_mix (static atom ranges first, claimed groups
-after them, the first claims drawn a few atoms before warp 0's range ends),
-including warps with empty or very short static ranges.
 """
 from __future__ import annotations
 
@@ -189,192 +185,3 @@ def test_protocol_completes_every_group_once():
 def test_eager_entry_reads_deadlock():
     results = [run(*_geometry(seed), seed, eager=True) for seed in range(60)]
     assert any(r.startswith("DEADLOCK") for r in results)
-
-
-# ---------------------------------------------------------------------------
-# k_gemv_mix: a static atom range per warp first, then claimed groups.  Lane 0
-# of warp 0 draws the CTA's first kDynAhead groups at its static atom
-# ns - kStages - 3 (at once for shorter ranges) and publishes them one atom
-# later or when its own range ends; each warp's copy cursor runs from its
-# static range into the claimed groups.
-# ---------------------------------------------------------------------------
-def run_mix(G, S, grid, R, ns_list, aprs, seed):
-    rnd = random.Random(seed)
-    counter = [0]
-    reduced = {}
-    warps = []
-    for cta in range(grid):
-        sh = dict(q_group=[None] * KQ, q_bar=[Bar(1) for _ in range(KQ)], free_bar=[Bar(1), Bar(1)],
-                  red_cnt=[0, 0], part=[[None] * R for _ in range(2)],
-                  fullbar=[[Bar(1) for _ in range(KSTAGES)] for _ in range(R)])
-        for w in range(R):
-            ns = ns_list[(cta * R + w) % len(ns_list)]
-            warps.append(_mix_warp(cta, w, sh, G, S, R, ns, lambda gi: aprs[gi % len(aprs)], counter, reduced,
-                                   rnd))
-    live, waits, steps = list(range(len(warps))), {}, 0
-    while live:
-        steps += 1
-        if steps > 10 ** 7:
-            return "too many steps"
-        runnable = [i for i in live if waits.get(i) is None or waits[i]()]
-        if not runnable:
-            return f"DEADLOCK with {len(live)} warps waiting"
-        i = rnd.choice(runnable)
-        try:
-            waits[i] = next(warps[i])
-        except StopIteration:
-            live.remove(i)
-            waits.pop(i, None)
-    for g in range(S, G):
-        if reduced.get(g) != 1:
-            return f"group {g} reduced {reduced.get(g)} times"
-    return "ok"
-
-
-def _mix_warp(cta, warp, sh, G, S, R, ns, apr_of, counter, reduced, rnd):
-    producer = warp == 0
-    fb = sh['fullbar'][warp]
-    tma = []
-
-    def issue(n):
-        tma.append([n % KSTAGES, rnd.randint(0, 20)])
-
-    def tick():
-        for x in tma:
-            x[1] -= 1
-        for x in [x for x in tma if x[1] <= 0]:
-            fb[x[0]].arrive()
-            tma.remove(x)
-
-    def entry(k):
-        slot, par = k % KQ, (k // KQ) & 1
-        yield lambda: sh['q_bar'][slot].done(par)
-        return sh['q_group'][slot]
-
-    def enter(k, gi):
-        d = dict(k=k, gi=gi, need=False)
-        if gi >= 0:
-            a = apr_of(gi)
-            d['kp'], d['s1'] = warp * a // R, (warp + 1) * a // R
-        return d
-
-    def resolve(d):
-        if not d['need'] or d['gi'] < 0:
-            return d
-        gi = yield from entry(d['k'] + 1)
-        return enter(d['k'] + 1, gi)
-
-    st = dict(pend=0, filled=0, drawn=False, claiming=False)
-
-    def publish_batch(t0):
-        for e in range(KAHEAD):
-            gi = S + t0 + e
-            sh['q_group'][e] = gi if gi < G else -1
-            sh['q_bar'][e].arrive()
-        st['filled'], st['claiming'] = KAHEAD, S + t0 + KAHEAD - 1 < G
-
-    ic = dict(k=-1, gi=0, need=True)
-    cc = dict(ic)
-    issued = 0
-    while issued < KSTAGES and issued < ns:
-        issue(issued)
-        issued += 1
-    yield None  # griddepcontrol.wait
-    trig = ns - KSTAGES - 1
-    if producer and trig <= 0:
-        t0 = counter[0]
-        counter[0] += KAHEAD
-        publish_batch(t0)
-        st['drawn'], st['pend'] = True, -1
-
-    def issue_next():
-        nonlocal issued, ic
-        if issued >= ns:
-            ic = yield from resolve(ic)
-            if ic['gi'] < 0:
-                return False
-            ic['kp'] += 1
-            ic['need'] = ic['kp'] == ic['s1']
-        issue(issued)
-        issued += 1
-        return True
-
-    while issued < KSTAGES:
-        if not (yield from issue_next()):
-            break
-    done, group_k = 0, -1
-    while True:
-        if producer:
-            if not st['drawn'] and done >= trig:
-                st['pend'] = counter[0]
-                counter[0] += KAHEAD
-                st['drawn'] = True
-            elif st['drawn'] and st['pend'] >= 0 and st['filled'] == 0:
-                publish_batch(st['pend'])
-                st['pend'] = -1
-        stat = done < ns
-        if not stat:
-            if producer and st['filled'] == 0 and st['drawn']:
-                publish_batch(st['pend'])
-                st['pend'] = -1
-            cc = yield from resolve(cc)
-            if cc['gi'] < 0:
-                break
-            if producer and cc['k'] != group_k:
-                group_k = cc['k']
-                if st['claiming'] and cc['k'] >= 1:
-                    gi = S + st['pend']
-                    e = st['filled']
-                    st['filled'] += 1
-                    sh['q_group'][e % KQ] = gi if gi < G else -1
-                    sh['q_bar'][e % KQ].arrive()
-                    st['claiming'] = gi < G
-                if st['claiming']:
-                    st['pend'] = counter[0]
-                    counter[0] += 1
-        s, par = done % KSTAGES, (done // KSTAGES) & 1
-        while not fb[s].done(par):
-            tick()
-            yield None
-        yield from issue_next()
-        done += 1
-        tick()
-        if stat:
-            yield None
-            continue
-        cc['kp'] += 1
-        if cc['kp'] < cc['s1']:
-            yield None
-            continue
-        cc['need'] = True
-        b, use = cc['k'] & 1, cc['k'] >> 1
-        if use >= 1:
-            while not sh['free_bar'][b].done((use - 1) & 1):
-                tick()
-                yield None
-        sh['part'][b][warp] = cc['gi']
-        yield None
-        old = sh['red_cnt'][b]
-        sh['red_cnt'][b] += 1
-        if old == R - 1:
-            assert all(p == cc['gi'] for p in sh['part'][b])
-            reduced[cc['gi']] = reduced.get(cc['gi'], 0) + 1
-            yield None
-            sh['red_cnt'][b] = 0
-            sh['free_bar'][b].arrive()
-        yield None
-    while tma:
-        tick()
-        yield None
-
-
-def test_mixed_protocol_completes_every_dynamic_group_once():
-    for seed in range(400):
-        rnd = random.Random(seed)
-        R, grid = rnd.choice([2, 4, 7, 8]), rnd.choice([1, 2, 3, 5])
-        S = rnd.randint(0, 20)
-        G = S + rnd.randint(1, 30)
-        base = rnd.choice([0, 1, 3, 6, 12])
-        ns_list = [max(0, base + rnd.randint(-1, 1)) for _ in range(R * grid)]
-        aprs = [max(rnd.choice([R, R + 1, 2 * R, 28]), R) for _ in range(3)]
-        assert run_mix(G, S, grid, R, ns_list, aprs, seed) == "ok", (seed, R, grid, G, S, ns_list[:4], aprs)

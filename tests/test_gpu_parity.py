@@ -112,7 +112,8 @@ def test_gemv_f32_fused_vs_oracle(q4k, oracle, torch_mod, dev, nrows, K, ncols):
     assert_close(got, oracle.gemv_f32(W, x), f"{nrows}x{K} ncols={ncols}")
 
 
-@pytest.mark.parametrize("path", sorted(GOLDEN.glob("gemv_*.npz")), ids=lambda p: p.stem)
+@pytest.mark.parametrize("path", sorted(p for p in GOLDEN.glob("gemv_*.npz") if not p.stem.startswith("gemv_q6k_")),
+                         ids=lambda p: p.stem)
 def test_gemv_matches_reference_golden(q4k, torch_mod, dev, path):
     z = np.load(path)
     nrows, K, ncols, _ = (int(v) for v in z["meta"])

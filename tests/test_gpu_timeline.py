@@ -1,4 +1,4 @@
-"""The launch-timeline diagnostic (gemv-q4_k-optimization_b200/timeline.py
+"""The launch-timeline diagnostic (tests/timeline_driver.py
 over the Q4K_TIMELINE build): one small chained workload, recorded from a CUDA
 graph replay, gives a sane record for every launch."""
 from __future__ import annotations
@@ -6,6 +6,7 @@ from __future__ import annotations
 import json
 import subprocess
 import sys
+from pathlib import Path
 
 import pytest
 
@@ -15,7 +16,7 @@ pytestmark = pytest.mark.gpu
 def test_timeline_records_every_launch(q4k):
     if not q4k.TIMELINE_LIB.exists():
         pytest.skip("timeline library not built (make -C gemv-q4_k-optimization_b200 timeline)")
-    script = q4k.HERE / "timeline.py"
+    script = Path(__file__).resolve().parent / "timeline_driver.py"
     env = {"Q4K_LIB": str(q4k.TIMELINE_LIB)}
     import os
     env = {**os.environ, **env}

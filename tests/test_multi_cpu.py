@@ -85,3 +85,39 @@ def test_bad_gather_descriptors_rejected(q4k):
     g.out_peer[0] = 4096
     assert call(g) == 1  # out_peer[rank] != out_local
     assert b"gather" in L.q4k_last_error()
+
+
+def test_gather_tasks_outside_the_buffer_rejected(q4k):
+    """Every output of a gathering call is also stored into each peer's buffer at
+    the same offset, so a task whose columns reach past the full buffer (or
+    start outside it) is refused on the host, before any launch."""
+    L = q4k.lib()
+    g = q4k.Gather()
+    g.world, g.rank = 2, 0
+    g.out_local, g.epoch = 1 << 20, 2048
+    g.out_peer[0], g.out_peer[1] = 1 << 20, 1 << 24
+    g.flags_peer[0], g.flags_peer[1] = 8192, 8448
+    g.out_elems = 1000
+    tasks = (q4k.Task * 1)()
+    t = tasks[0]
+    t.W, t.x = 256, 512
+    t.nrows, t.K, t.stride_row_x, t.stride_col_x = 32, 256, 1, 256
+
+    def call(dst, stride_col_dst, ncols):
+        # no workspace: a call that passes validation stops at Q4K_EWORKSPACE,
+        # before any launch (the pointers here are not device memory)
+        t.dst, t.stride_col_dst = dst, stride_col_dst
+        return L.q4k_gemv_batch_allgather(tasks, 1, ncols, ctypes.byref(g), None, 0, None)
+
+    base = 1 << 20
+    assert call(base - 4, 32, 1) == 1                   # starts before out_local
+    assert b"gather buffer" in L.q4k_last_error()
+    assert call(base + 2, 32, 1) == 1                   # not float-aligned inside it
+    assert call(base + 4 * 969, 32, 1) == 1             # rows [969, 1001) reach past 1000
+    assert b"reach past" in L.q4k_last_error()
+    assert call(base + 4 * 500, 500, 2) == 1            # second column ends at 1032
+    assert call(base + 4 * 400, 16, 2) == 1             # stride_col_dst < nrows
+    # in range ([468, 1000)): accepted, then refused for the missing workspace
+    # (or, without a GPU, for the device set-up) -- anything but Q4K_EINVAL
+    st = call(base + 4 * 468, 500, 2)
+    assert st in (2, 5), (st, L.q4k_last_error())

@@ -142,7 +142,8 @@ def test_subblock_sums_match_reference_golden(oracle):
         assert np.array_equal(T, z["T"][i]), i
 
 
-@pytest.mark.parametrize("path", sorted(GOLDEN.glob("gemv_*.npz")), ids=lambda p: p.stem)
+@pytest.mark.parametrize("path", sorted(p for p in GOLDEN.glob("gemv_*.npz") if not p.stem.startswith("gemv_q6k_")),
+                         ids=lambda p: p.stem)
 def test_gemv_matches_reference_golden(oracle, path):
     z = np.load(path)
     nrows, K, ncols, _ = (int(v) for v in z["meta"])

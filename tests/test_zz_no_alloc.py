@@ -6,7 +6,8 @@ budget) cannot hand the library a workspace, so this entry point uses a
 scratch array built into the library.  The test calls it through the C ABI
 twice in a row -- different shapes, so the second call runs on whatever the
 first left in the shared array -- and compares each result with the regular
-workspace-taking entry point, within the tolerance of the other parity tests.
+workspace-taking entry point and with the CPU oracle, within the tolerance of
+the other parity tests.
 It lives in its own file, collected last, and needs nothing from other tests.
 """
 from __future__ import annotations
@@ -21,7 +22,7 @@ pytestmark = pytest.mark.gpu
 TOL_ABS, TOL_REL = 1e-4, 1e-5
 
 
-def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row(q4k):
+def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row(q4k, oracle):
     import torch
 
     dev = torch.device("cuda", 0)
@@ -40,6 +41,8 @@ def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row(q4k):
         torch.cuda.synchronize()
         g, w = got.cpu().numpy().astype(np.float64), want.cpu().numpy().astype(np.float64)
         assert np.all(np.abs(g - w) <= TOL_ABS + TOL_REL * np.abs(w)), f"{nrows}x{K} ncols={ncols}"
+        o = oracle.gemv_f32(W.cpu().numpy(), x.cpu().numpy()).astype(np.float64)
+        assert np.all(np.abs(g - o) <= TOL_ABS + TOL_REL * np.abs(o)), f"{nrows}x{K} ncols={ncols} vs oracle"
 
 
 def test_noalloc_rejects_calls_larger_than_its_array(q4k):

@@ -12,7 +12,10 @@ stamps every launch leaves (include/q4k_gemv.h, q4k_timeline_*):
   per ring     mean end of the workers of each ring slot of a CTA
   per CTA      mean end by CTA index (CTAs are dispatched in index order)
 
-    python gemv-q4_k-optimization_b200/timeline.py --config 2 [--ncols N] [--reverse] [--json] [--save F.npz]
+    python tests/timeline_driver.py --config 2 [--ncols N] [--reverse] [--json] [--save F.npz]
+
+A diagnostic driver kept beside the test that checks its output
+(tests/test_gpu_timeline.py); not part of the library.
 
 The reference's own tracing was Nsight plus in-kernel clock64 probes left
 commented out (w_tile.cu:76-122); this is the same question asked of the
@@ -30,8 +33,8 @@ from pathlib import Path
 
 import numpy as np
 
-HERE = Path(__file__).resolve().parent
-ROOT = HERE.parent
+ROOT = Path(__file__).resolve().parent.parent
+HERE = ROOT / "gemv-q4_k-optimization_b200"
 os.environ.setdefault("Q4K_LIB", str(HERE / "libq4k_gemv_timeline.so"))
 sys.path.insert(0, str(ROOT))
 
