@@ -1,15 +1,22 @@
 #!/usr/bin/env python
 """Q4_K x q8_1 decode-GEMV benchmark on B200.
 
-Default workload ("mistral-7b-decode-gemv-set"): one decode
-step's Q4_K GEMVs of Mistral-7B at batch 1 -- 32 layers x {q 4096x4096, k
-1024x4096, v 1024x4096, o 4096x4096, gate 14336x4096, up 14336x4096, down
-4096x14336} plus the 32000x4096 output head, synthetic seeded weights with
-the BASELINE value distributions (d, dmin = fp16(|N(0,1)|*0.01), uniform 6-bit
+Headline workload ("mistral-7b-decode-gemv-set"): one
+decode step's Q4_K GEMVs of Mistral-7B at batch 1 -- 32 layers x {q 4096x4096,
+k 1024x4096, v 1024x4096, o 4096x4096, gate 14336x4096, up 14336x4096, down
+4096x14336} plus the 32000x4096 output head, synthetic seeded weights with the
+BASELINE value distributions (d, dmin = fp16(|N(0,1)|*0.01), uniform 6-bit
 scales/mins, uniform nibbles; generated on the device) and x ~ N(0,1) (q/k/v
-share one activation, gate/up share one).  One prep + persistent GEMV launch
-pair per layer.  The 4.0 GB of weights per step exceed the 126 MB L2, so
-every step streams from HBM.  Other BASELINE configs: --config 1/3/4/5/5t.
+share one activation, gate/up share one).  One launch sequence per layer.
+The 4.0 GB of weights per step exceed the 126 MB L2, so every step streams
+from HBM.
+
+Every other BASELINE config is measured in the same run and reported under
+"per_config": at one GPU configs 1 (4096x4096), 3 (ffn_up 14336x4096 at
+ncols 1, 2, 3, 4, 8), 4 (Llama-3-70B layer), 5 (the 128256x8192 head) and 5t
+(the tiny 1024x4096 / 512x4096 pair); at N > 1 GPUs the row-sharded configs
+4 and 5.  Each entry: ms per step, us per launch, TB/s, fraction of the
+measured HBM peak and the clocks seen during its timed region.
 
 Metric: achieved algorithmic HBM bandwidth of the whole job (TB/s, all
 ranks) with bytes = rows*K*0.5625 + ncols*K*4 per distinct activation +
@@ -19,9 +26,11 @@ ncols*rows*4; also us per GEMV launch.
   python bench.py --impl reference    # the reference's CPU path, timed on the host
 
 N > 1 (torchrun, one rank per GPU): every matrix is row-sharded across the
-ranks; by default each launch also all-gathers the output rows into every
-rank's buffer over NVLink peer stores (--gather nccl: NCCL all_gather per
-launch instead).
+ranks (contiguous ceil-split, the reference's row-split mode); each launch
+stores its output rows into every rank's full output buffer over NVLink
+(--gather nccl: NCCL all_gather per launch instead).  Before timing, every
+rank checks a seeded sample of 256 gathered rows per matrix against the CPU
+oracle ("parity": "ok" | "fail").
 """
 from __future__ import annotations
 
@@ -43,7 +52,7 @@ PKG_DIR = ROOT / "gemv-q4_k-optimization_b200"
 PROFILES = ROOT / "profiles"
 METRIC = "Q4_K GEMV achieved HBM TB/s (algorithmic bytes), us per GEMV launch"
 
-# A launch group is one q4k_gemv_batch launch: (name, rows, K, activation group
+# A launch group is one batch launch: (name, rows, K, activation group
 # [, glu op]).  An entry with a glu op is a gate/up pair fused in one task
 # (two matrices of rows x K, one output: op(up.x, gate.x)).
 MISTRAL_LAYER = [("q", 4096, 4096, "attn"), ("k", 1024, 4096, "attn"), ("v", 1024, 4096, "attn"),
@@ -70,6 +79,9 @@ WORKLOADS = {
     "q6": ("mistral-7b-q6_k-head-32000x4096", [("head_q6", 32000, 4096, "x", "q6")], 16, []),
     "q6l": ("llama-3-q6_k-head-128256x8192", [("head_q6", 128256, 8192, "x", "q6")], 6, []),
 }
+# The other BASELINE configs measured beside the headline: (config, ncols).
+PER_CONFIG_1GPU = [("1", 1), ("3", 1), ("3", 2), ("3", 3), ("3", 4), ("3", 8), ("4", 1), ("5", 1), ("5t", 1)]
+PER_CONFIG_SHARDED = [("4", 1), ("5", 1)]
 
 
 def ent(e):
@@ -122,6 +134,14 @@ def load_oracle():
     return O
 
 
+def host_cores() -> int:
+    """Host threads this process may run on (affinity-aware)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -134,6 +154,8 @@ def measured_peaks():
 # clocks
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """nvidia-smi samples every 200 ms, each stamped with the host clock, so
+    that any timed window can be summarised."""
     FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -141,7 +163,7 @@ class ClockSampler:
     def __init__(self, uuid: str | None):
         self.uuid = str(uuid or "").lower()
         self.proc = None
-        self.lines: list[str] = []
+        self.rows: list[tuple[float, list[str]]] = []
         self.thread = None
 
     def start(self):
@@ -157,12 +179,15 @@ class ClockSampler:
 
     def _read(self):
         for ln in self.proc.stdout:
-            self.lines.append(ln.strip())
+            f = [c.strip() for c in ln.strip().split(",")]
+            if len(f) < 10 or (self.uuid and self.uuid not in f[1].lower()):
+                continue
+            self.rows.append((time.perf_counter(), f))
 
-    def stop(self) -> dict:
+    def stop(self):
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)  # let the sampler catch the end of the timed region
+            return
+        time.sleep(0.25)  # let the sampler catch the end of the last timed region
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -170,22 +195,24 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        rows = []
-        for ln in self.lines:
-            f = [c.strip() for c in ln.split(",")]
-            if len(f) < 10:
-                continue
-            if self.uuid and self.uuid not in f[1].lower():
-                continue
-            rows.append(f)
-        sm = [float(f[2].split()[0]) for f in rows if f[2].split()[0].replace(".", "").isdigit()]
-        smax = [float(f[3].split()[0]) for f in rows if f[3].split()[0].replace(".", "").isdigit()]
+
+    def summary(self, t0: float, t1: float, window: str) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = [f for t, f in self.rows if t0 - 0.2 <= t <= t1 + 0.2]
+
+        def num(v):
+            v = v.split()[0] if v.split() else ""
+            return float(v) if v.replace(".", "").isdigit() else None
+
+        sm = [v for v in (num(f[2]) for f in rows) if v is not None]
+        smax = [v for v in (num(f[3]) for f in rows) if v is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for f in rows for n, v in zip(names, f[6:10]) if v.lower() == "active"})
         loaded = [s for s in sm if smax and s > 0.5 * max(smax)] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None,
                 "sm_max_mhz": max(smax) if smax else None, "reasons": reasons, "samples": len(rows),
-                "window": "untimed soak of step replays (~0.8 s) + warm-up + timed steps"}
+                "window": window}
 
 
 # ---------------------------------------------------------------------------
@@ -205,30 +232,41 @@ def host_group(q4k, group, ncols, rng):
 
 def run_reference(args) -> None:
     """The reference's CPU implementation of the path (its vec_dot_q4_K_q8_1
-    compiled for the host, oracle/_ref), all host threads, one launch group
-    per step (a decoder layer for config 2)."""
+    compiled for the host, oracle/_ref), on all host cores, over the same
+    step as our arm: every launch group of the config (for config 2: 32
+    decoder layers and the output head).  One host copy of each distinct
+    launch group's weights serves all its repeats (each group far exceeds the
+    CPU caches, so the repeats stream from memory as distinct copies would)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     O = load_oracle()
     q4k = load_package()
-    name, groups = build_groups(args.config, 1)
-    group = groups[0]
     ncols = args.ncols
-    mats, xs = host_group(q4k, group, ncols, np.random.default_rng(0))
+    reps = args.layers if args.layers is not None else WORKLOADS[args.config][2]
+    name, groups = build_groups(args.config, reps)
+    rng = np.random.default_rng(0)
+    distinct = {}
+    for grp in groups:
+        key = tuple(grp)
+        if key not in distinct:
+            distinct[key] = host_group(q4k, grp, ncols, rng)
     # the reference's compiled dot product covers Q4_K; Q6_K runs on the port
-    kind = "reference" if O.ref_available() and not any(m[3] for m in mats) else "port"
-    threads = O.max_threads() if kind == "port" else O.ref_lib().ref_max_threads()
+    any_q6 = any(m[3] for mats, _ in distinct.values() for m in mats)
+    kind = "reference" if O.ref_available() and not any_q6 else "port"
+    threads = host_cores()  # explicit: torchrun sets OMP_NUM_THREADS=1 in the environment
 
     def one_step():
-        for W, K, a, is_q6 in mats:
-            yq = O.quantize_q8_1(xs[a])
-            if is_q6:
-                O.gemv_q6k_q8_1(W, K, yq, nthreads=threads)
-            elif kind == "reference":
-                O.ref_gemv_q8_1(W, K, yq, nthreads=threads)
-            else:
-                O.gemv_q8_1(W, K, yq, nthreads=threads)
+        for grp in groups:
+            mats, xs = distinct[tuple(grp)]
+            for W, K, a, is_q6 in mats:
+                yq = O.quantize_q8_1(xs[a])
+                if is_q6:
+                    O.gemv_q6k_q8_1(W, K, yq, nthreads=threads)
+                elif kind == "reference":
+                    O.ref_gemv_q8_1(W, K, yq, nthreads=threads)
+                else:
+                    O.gemv_q8_1(W, K, yq, nthreads=threads)
 
     for _ in range(args.warmup):
         one_step()
@@ -236,15 +274,18 @@ def run_reference(args) -> None:
     for _ in range(args.steps):
         one_step()
     dt = (time.perf_counter() - t0) / args.steps
-    tbs = group_bytes(group, ncols) / dt / 1e12
-    sample = (f"one launch group of {name} per step ({len(group)} Q4_K GEMVs, "
-              f"{group_bytes(group, ncols) / 1e6:.1f} MB algorithmic), q8_1 quantization included; "
+    step_bytes = sum(group_bytes(g, ncols) for g in groups)
+    tbs = step_bytes / dt / 1e12
+    sample = (f"the whole step of {name}: {len(groups)} launch groups, "
+              f"{sum(len(g) for g in groups)} GEMVs, {step_bytes / 1e9:.2f} GB algorithmic, q8_1 quantization "
+              f"included, {threads} host threads; "
               f"{'the reference vec_dot_q4_K_q8_1 in MMVQ order' if kind == 'reference' else 'the C oracle'}")
     line = {
         "impl": "reference", "metric": METRIC, "value": tbs, "unit": "TB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": name, "ncols": ncols, "sample": "one launch group per step"},
+        "config": {"workload": name, "baseline_config": args.config, "ncols": ncols,
+                   "launch_groups": len(groups), "sample": "the whole step, every launch group"},
         "cpu_baseline": {"value": tbs, "unit": "TB/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": tbs, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -252,10 +293,10 @@ def run_reference(args) -> None:
 
 
 def cpu_baseline(O, mats, group, ncols, budget_s: float = 12.0) -> dict:
-    """The oracle (all host threads) on the first launch group, repeated for ~budget_s."""
+    """The oracle (all host cores) on the first launch group, repeated for ~budget_s."""
     rng = np.random.default_rng(1)
     xs = {a: rng.standard_normal((ncols, K)).astype(np.float32) for _, _, K, a, _ in map(ent, group)}
-    threads = O.max_threads()
+    threads = host_cores()
 
     def timed(nthreads, budget):
         n, t0 = 0, time.perf_counter()
@@ -279,6 +320,323 @@ def cpu_baseline(O, mats, group, ncols, budget_s: float = 12.0) -> dict:
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+class Ctx:
+    """What every workload of one run shares: process layout, device, library."""
+
+    def __init__(self, args, torch, dist, q4k):
+        self.args, self.torch, self.dist, self.q4k = args, torch, dist, q4k
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dev = torch.device("cuda", self.local)
+        self.peer = self.world > 1 and args.gather == "peer"
+
+    def barrier(self):
+        if self.world > 1:
+            self.torch.cuda.synchronize(self.dev)
+            self.dist.barrier()
+
+    def max_over_ranks(self, vals):
+        if self.world == 1:
+            return [float(v) for v in vals]
+        t = self.torch.tensor([float(v) for v in vals], device=self.dev, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return [float(v) for v in t.tolist()]
+
+    def all_ok(self, ok: bool) -> bool:
+        if self.world == 1:
+            return ok
+        t = self.torch.tensor([1 if ok else 0], device=self.dev, dtype=self.torch.int32)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MIN)
+        return bool(int(t[0]))
+
+
+class Workload:
+    """One config's device buffers, tasks and launch sequence on this rank."""
+
+    def __init__(self, C: Ctx, cfg: str, ncols: int, reps: int | None):
+        torch, q4k = C.torch, C.q4k
+        self.C, self.cfg, self.ncols = C, cfg, ncols
+        rank, world, dev = C.rank, C.world, C.dev
+        self.reps = reps if reps is not None else WORKLOADS[cfg][2]
+        self.name, self.groups = build_groups(cfg, self.reps)
+        self.full_run = self.reps == WORKLOADS[cfg][2]
+        # weights: this rank's row shards (rank-specific stream); activations:
+        # replicated, the same on every rank (row split shares x)
+        gw = torch.Generator(device=dev)
+        gw.manual_seed(1234 + 7919 * rank + 104729 * int.from_bytes(cfg.encode(), "little") + ncols)
+        gx = torch.Generator(device=dev)
+        gx.manual_seed(4321 + ncols)
+        peer = C.peer
+        full_elems = sum(r * ncols for grp in self.groups for _, r, _, _, _ in map(ent, grp))
+        self.q6 = any(glu == "q6" for grp in self.groups for *_, glu in map(ent, grp))
+        self.fused = not self.q6 and any(glu for grp in self.groups for *_, glu in map(ent, grp))
+        if (self.fused or self.q6) and world > 1:
+            raise SystemExit(f"config {cfg} (fused epilogue / Q6_K) runs on one GPU")
+        self.pg = q4k.PeerGather(full_elems) if peer else None
+        # Every step's activations live in one device buffer and its local
+        # outputs in another, so that the end-to-end leg moves each with one copy.
+        x_tot = sum(ncols * K for grp in self.groups for K in {a: K for _, _, K, a, _ in map(ent, grp)}.values())
+        self.x_all = torch.empty((x_tot,), device=dev)
+        x_off = 0
+        y_tot = 0
+        if not peer:
+            for grp in self.groups:
+                y_tot += -(-sum(q4k.shard_rows(r, rank, world)[2] for _, r, _, _, _ in map(ent, grp)) * ncols
+                           // 64) * 64
+        self.y_all = torch.zeros((max(y_tot, 1),), device=dev)
+        y_off = 0
+        self.L = []
+        base = 0
+        for grp in self.groups:
+            xs = {}
+            for _, _, K, a, _ in map(ent, grp):
+                if a not in xs:
+                    xs[a] = self.x_all[x_off: x_off + ncols * K].view(ncols, K).normal_(generator=gx)
+                    x_off += ncols * K
+            ents = []
+            for name, rows, K, a, glu in map(ent, grp):
+                lo, hi, per = q4k.shard_rows(rows, rank, world)
+                if glu == "q6":
+                    W, Wg = q4k.gen_q6k_torch(hi - lo, K, generator=gw, device=dev), None
+                else:
+                    W = q4k.gen_q4k_torch(hi - lo, K, generator=gw, device=dev)
+                    Wg = q4k.gen_q4k_torch(hi - lo, K, generator=gw, device=dev) if glu else None
+                ents.append(dict(name=name, W=W, W_gate=Wg, glu=glu, x=xs[a], a=a, rows=rows, K=K, lo=lo,
+                                 n=hi - lo, per=per))
+            if peer:
+                # full outputs live in the shared buffer; each rank writes its rows
+                # there and the kernel stores them into every peer's buffer too
+                outs, ybuf0 = [], base
+                for e in ents:
+                    full = self.pg.out[base: base + e["rows"] * ncols].view(ncols, e["rows"])
+                    e["full"] = full
+                    outs.append(full[:, e["lo"]: e["lo"] + e["n"]])
+                    e["stride"] = e["rows"]
+                    base += e["rows"] * ncols
+                ybuf, gath = self.pg.out[ybuf0: base], None
+            else:
+                per_tot = sum(e["per"] for e in ents)
+                ybuf = self.y_all[y_off: y_off + per_tot * ncols]
+                y_off += -(-per_tot * ncols // 64) * 64
+                outs, off = [], 0
+                for e in ents:
+                    outs.append(ybuf[off: off + e["per"] * ncols].view(ncols, e["per"])[:, : e["n"]])
+                    e["stride"] = e["per"]
+                    off += e["per"] * ncols
+                gath = torch.empty((per_tot * ncols * world,), device=dev) if world > 1 else None
+            for e, o in zip(ents, outs):
+                e["out"] = o
+            if self.q6:
+                tasks = q4k.make_tasks_q6_k([e["W"] for e in ents], [e["x"] for e in ents], outs)
+                for i, e in enumerate(ents):
+                    tasks[i].stride_col_dst = e["stride"]
+            elif self.fused:
+                tasks = q4k.make_tasks_ex([dict(W=e["W"], W_gate=e["W_gate"], x=e["x"], out=o,
+                                                glu=e["glu"] or "none") for e, o in zip(ents, outs)])
+                for i, e in enumerate(ents):
+                    tasks[i].t.stride_col_dst = e["stride"]
+            else:
+                tasks = q4k.make_tasks([e["W"] for e in ents], [e["x"] for e in ents], outs)
+                for i, e in enumerate(ents):
+                    tasks[i].stride_col_dst = e["stride"]
+            self.L.append(dict(xs=xs, ents=ents, ybuf=ybuf, tasks=tasks, gath=gath))
+        wsb = (q4k.batch_ex_workspace_bytes if self.fused else
+               (lambda t, n: int(q4k.lib().q4k_batch_q6_k_workspace_bytes(t, len(t), n))) if self.q6 else
+               q4k.batch_workspace_bytes)
+        self.ws = q4k.Workspace(max(wsb(G["tasks"], ncols) for G in self.L), dev)
+        self.stream = torch.cuda.Stream(device=dev)
+        self.graph = None
+        self.use_graph = not C.args.no_graph
+
+    # -- launches ---------------------------------------------------------------
+    def gemv(self, tasks):
+        q4k, C, ws, s = self.C.q4k, self.C, self.ws, self.stream
+        if C.peer:
+            q4k.gemv_batch_allgather(tasks, self.ncols, self.pg, ws, stream=s)
+        elif self.fused:
+            q4k.gemv_batch_ex(tasks, self.ncols, ws, stream=s)
+        elif self.q6:
+            q4k.gemv_batch_q6_k(tasks, self.ncols, ws, stream=s)
+        else:
+            q4k.gemv_batch(tasks, self.ncols, ws, stream=s)
+
+    def run_step(self, ev=None):
+        C = self.C
+        for gi, G in enumerate(self.L):
+            if ev is not None:
+                ev[gi][0].record(self.stream)
+            self.gemv(G["tasks"])
+            if ev is not None:
+                ev[gi][1].record(self.stream)
+            if C.world > 1 and not C.peer:
+                C.dist.all_gather_into_tensor(G["gath"], G["ybuf"])
+        if C.peer:
+            # the step's gathered outputs are complete once this wait has run
+            C.q4k.gather_wait(self.pg, self.ws, stream=self.stream)
+
+    def capture(self):
+        torch = self.C.torch
+        if not self.use_graph:
+            return
+        try:
+            with torch.cuda.stream(self.stream):
+                self.graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self.graph, stream=self.stream):
+                    self.run_step()
+        except Exception as e:  # capture unsupported: time eagerly
+            print(f"# graph capture failed ({e!r}); timing eager launches", file=sys.stderr)
+            self.use_graph, self.graph = False, None
+
+    def replay(self):
+        torch = self.C.torch
+        with torch.cuda.stream(self.stream):  # replay() launches on the current stream
+            if self.use_graph:
+                self.graph.replay()
+            else:
+                self.run_step()
+
+    def status(self) -> int:
+        return self.ws.status(self.stream)
+
+    # -- checks -------------------------------------------------------------------
+    def parity_check(self, O, nsample: int = 256) -> dict:
+        """Row-sharded runs: a seeded sample of nsample rows of every matrix of
+        the first and the last launch group, read from this rank's gathered
+        output, against the CPU oracle on the same rows.  The sampled rows'
+        weights are assembled on every rank from their owners' shards (NCCL
+        all-reduce MAX of zero-padded bytes); the oracle is the checker only."""
+        C, torch, q4k = self.C, self.C.torch, self.C.q4k
+        worst, bad, checked = 0.0, 0, 0
+        idx_groups = sorted({0, len(self.L) - 1})
+        for gi in idx_groups:
+            G = self.L[gi]
+            for e in G["ents"]:
+                rows, K = e["rows"], e["K"]
+                rng = np.random.default_rng(rows * 31 + K + gi)
+                sel = np.sort(rng.choice(rows, size=min(nsample, rows), replace=False))
+                rb = e["W"].shape[1] if e["W"].dim() > 1 else K // 256 * 144
+                buf = torch.zeros((len(sel), rb), dtype=torch.uint8, device=C.dev)
+                mine = [(i, r - e["lo"]) for i, r in enumerate(sel) if e["lo"] <= r < e["lo"] + e["n"]]
+                if mine:
+                    ii = torch.tensor([i for i, _ in mine], device=C.dev)
+                    rr = torch.tensor([r for _, r in mine], device=C.dev)
+                    buf[ii] = e["W"][rr]
+                C.dist.all_reduce(buf, op=C.dist.ReduceOp.MAX)
+                x = e["x"].cpu().numpy()
+                want = O.gemv_f32(buf.cpu().numpy(), x).astype(np.float64)  # (ncols, nsample)
+                if C.peer:
+                    got = e["full"][:, torch.from_numpy(sel).to(C.dev)].cpu().numpy().astype(np.float64)
+                else:  # NCCL gather: rank q's slice at q * per_tot in the gathered buffer
+                    per_tot = sum(f["per"] for f in G["ents"])
+                    off = 0
+                    for f in G["ents"]:
+                        if f is e:
+                            break
+                        off += f["per"] * self.ncols
+                    gath = G["gath"].view(C.world, per_tot * self.ncols)
+                    got = np.empty((self.ncols, len(sel)))
+                    for k, r in enumerate(sel):
+                        q, lr = r // e["per"], r % e["per"]
+                        part = gath[q, off: off + e["per"] * self.ncols].view(self.ncols, e["per"])
+                        got[:, k] = part[:, lr].cpu().numpy()
+                err = np.abs(got - want)
+                tol = 1e-4 + 1e-5 * np.abs(want)
+                bad += int((err > tol).sum())
+                worst = max(worst, float((err / tol).max()))
+                checked += err.size
+        ok = C.all_ok(bad == 0)
+        return {"parity": "ok" if ok else "fail", "values_checked_per_rank": checked,
+                "worst_err_over_tol": worst, "groups_checked": idx_groups,
+                "bar": "1e-4 abs + 1e-5 rel vs the CPU oracle, 256 seeded rows per matrix"}
+
+    # -- timing -------------------------------------------------------------------
+    def time_steps(self, soak_s: float) -> dict:
+        """Soak (untimed), warm-up, then the timed steps between CUDA events on
+        the launch stream; then one step with events between the launches
+        (serialising them) for the isolated-launch time.  Max over ranks."""
+        C, torch, args = self.C, self.C.torch, self.C.args
+        dev = C.dev
+        nsoak, t_soak = 0, time.perf_counter()
+        hs = t_soak
+        while time.perf_counter() - t_soak < soak_s and nsoak < 4000:
+            for _ in range(10):
+                self.replay()
+            nsoak += 10
+            torch.cuda.synchronize(dev)
+        if C.world > 1:  # every rank replays the same number of soak steps
+            n = int(C.max_over_ranks([nsoak])[0])
+            for _ in range(n - nsoak):
+                self.replay()
+        C.barrier()
+        for _ in range(args.warmup):
+            self.replay()
+        torch.cuda.synchronize(dev)
+        C.barrier()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        h0 = time.perf_counter()
+        t_start.record(self.stream)
+        for _ in range(args.steps):
+            self.replay()
+        t_end.record(self.stream)
+        torch.cuda.synchronize(dev)
+        h1 = time.perf_counter()
+        C.barrier()
+        ms = t_start.elapsed_time(t_end) / args.steps
+        # isolated launches (events between launches serialize them); every
+        # rank enters together
+        C.barrier()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in self.L]
+        with torch.cuda.stream(self.stream):
+            self.run_step(ev)
+        torch.cuda.synchronize(dev)
+        st = self.status()
+        nrep = len(self.groups) - len(WORKLOADS[self.cfg][3])  # the repeated group only
+        iso_ms = float(np.mean([a.elapsed_time(b) for a, b in ev[: max(1, nrep)]]))
+        ms, iso_ms, bad = C.max_over_ranks([ms, iso_ms, 1 if st != 0 else 0])
+        if bad:
+            raise SystemExit(f"device status word reports an error after the timed steps (config {self.cfg})")
+        return {"ms": ms, "iso_ms": iso_ms, "hs": hs, "h0": h0, "h1": h1}
+
+    def step_bytes(self) -> int:
+        return sum(group_bytes(G, self.ncols, self.C.world) for G in self.groups)
+
+    def kernels(self):
+        q4k = self.C.q4k
+        try:
+            if self.q6:
+                return "k_gemv (Q6_K)"
+            if self.C.peer:
+                return "k_gemv (gather epilogue)"
+            return sorted({q4k.batch_kernel(G["tasks"], self.ncols) for G in self.L})
+        except Exception as e:  # a report, never a reason to lose the measurement
+            return f"unknown ({e!r})"
+
+    def free(self):
+        C = self.C
+        self.graph = None
+        C.torch.cuda.synchronize(C.dev)
+        C.barrier()
+        if self.pg is not None:
+            self.pg.close()
+            self.pg = None
+        self.L = []
+        self.ws = None
+        C.torch.cuda.empty_cache()
+
+
+def summarize(W: Workload, t: dict, peak: float) -> dict:
+    world = W.C.world
+    total = W.step_bytes()
+    nl = len(W.groups)
+    return {"workload": W.name, "ncols": W.ncols, "launch_groups": nl, "ms_per_step": t["ms"],
+            "us_per_launch": t["ms"] * 1e3 / nl, "us_per_launch_isolated": t["iso_ms"] * 1e3,
+            "tbs": total / (t["ms"] * 1e-3) / 1e12,
+            "frac": total / world / (t["ms"] * 1e-3) / 1e9 / peak,
+            "bytes_per_step": total, "gemv_kernels": W.kernels(), "window": (t["hs"], t["h1"])}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -294,6 +652,7 @@ def main():
                     help="N > 1: fused peer-store all-gather in the GEMV (default) or NCCL all_gather per launch")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true", help="measure the headline config only")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -304,228 +663,57 @@ def main():
     import torch
     import torch.distributed as dist
 
-    rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=120))
     q4k = load_package()
     q4k.lib()
-    ncols = args.ncols
-    reps = args.layers if args.layers is not None else WORKLOADS[args.config][2]
-    wname, groups = build_groups(args.config, reps)
-    full_run = args.layers is None or args.layers == WORKLOADS[args.config][2]
-
-    # ---- weights (row shards), activations, outputs -------------------------
-    g = torch.Generator(device=dev)
-    g.manual_seed(1234 + rank)
-    peer = world > 1 and args.gather == "peer"
-    full_elems = sum(r * ncols for grp in groups for _, r, _, _, _ in map(ent, grp))
-    q6 = any(glu == "q6" for grp in groups for *_, glu in map(ent, grp))
-    fused = not q6 and any(glu for grp in groups for *_, glu in map(ent, grp))
-    if (fused or q6) and world > 1:
-        raise SystemExit(f"config {args.config} (fused epilogue / Q6_K) runs on one GPU")
-    pg = q4k.PeerGather(full_elems) if peer else None
-    # Every step's activations live in one device buffer and its local outputs
-    # in another, so that the end-to-end leg moves each with one copy.
-    x_tot = sum(ncols * K for grp in groups for K in {a: K for _, _, K, a, _ in map(ent, grp)}.values())
-    x_all = torch.empty((x_tot,), device=dev)
-    x_off = 0
-    y_tot = 0
-    if not peer:
-        for grp in groups:
-            y_tot += -(-sum(q4k.shard_rows(r, rank, world)[2] for _, r, _, _, _ in map(ent, grp)) * ncols // 64) * 64
-    y_all = torch.zeros((max(y_tot, 1),), device=dev)
-    y_off = 0
-    L = []
-    base = 0
-    for grp in groups:
-        xs = {}
-        for _, _, K, a, _ in map(ent, grp):
-            if a not in xs:
-                xs[a] = x_all[x_off: x_off + ncols * K].view(ncols, K).normal_(generator=g)
-                x_off += ncols * K
-        ents = []
-        for name, rows, K, a, glu in map(ent, grp):
-            lo, hi, per = q4k.shard_rows(rows, rank, world)
-            if glu == "q6":
-                W, Wg = q4k.gen_q6k_torch(hi - lo, K, generator=g, device=dev), None
-            else:
-                W = q4k.gen_q4k_torch(hi - lo, K, generator=g, device=dev)
-                Wg = q4k.gen_q4k_torch(hi - lo, K, generator=g, device=dev) if glu else None
-            ents.append(dict(name=name, W=W, W_gate=Wg, glu=glu, x=xs[a], rows=rows, K=K, lo=lo, n=hi - lo,
-                             per=per))
-        if peer:
-            # full outputs live in the shared buffer; each rank writes its rows
-            # there and the kernel stores them into every peer's buffer too
-            outs, ybuf0 = [], base
-            for e in ents:
-                full = pg.out[base: base + e["rows"] * ncols].view(ncols, e["rows"])
-                outs.append(full[:, e["lo"]: e["lo"] + e["n"]])
-                e["stride"] = e["rows"]
-                base += e["rows"] * ncols
-            ybuf, gath = pg.out[ybuf0: base], None
-        else:
-            per_tot = sum(e["per"] for e in ents)
-            ybuf = y_all[y_off: y_off + per_tot * ncols]
-            y_off += -(-per_tot * ncols // 64) * 64
-            outs, off = [], 0
-            for e in ents:
-                outs.append(ybuf[off: off + e["per"] * ncols].view(ncols, e["per"])[:, : e["n"]])
-                e["stride"] = e["per"]
-                off += e["per"] * ncols
-            gath = torch.empty((per_tot * ncols * world,), device=dev) if world > 1 else None
-        if q6:
-            tasks = q4k.make_tasks_q6_k([e["W"] for e in ents], [e["x"] for e in ents], outs)
-            for i, e in enumerate(ents):
-                tasks[i].stride_col_dst = e["stride"]
-        elif fused:
-            tasks = q4k.make_tasks_ex([dict(W=e["W"], W_gate=e["W_gate"], x=e["x"], out=o,
-                                            glu=e["glu"] or "none") for e, o in zip(ents, outs)])
-            for i, e in enumerate(ents):
-                tasks[i].t.stride_col_dst = e["stride"]
-        else:
-            tasks = q4k.make_tasks([e["W"] for e in ents], [e["x"] for e in ents], outs)
-            for i, e in enumerate(ents):
-                tasks[i].stride_col_dst = e["stride"]
-        L.append(dict(xs=xs, ents=ents, ybuf=ybuf, tasks=tasks, gath=gath))
-
-    wsb = (q4k.batch_ex_workspace_bytes if fused else
-           (lambda t, n: int(q4k.lib().q4k_batch_q6_k_workspace_bytes(t, len(t), n))) if q6 else
-           q4k.batch_workspace_bytes)
-    ws = q4k.Workspace(max(wsb(G["tasks"], ncols) for G in L), dev)
-    stream = torch.cuda.Stream(device=dev)
-
-    def gemv(tasks):
-        if peer:
-            q4k.gemv_batch_allgather(tasks, ncols, pg, ws, stream=stream)
-        elif fused:
-            q4k.gemv_batch_ex(tasks, ncols, ws, stream=stream)
-        elif q6:
-            q4k.gemv_batch_q6_k(tasks, ncols, ws, stream=stream)
-        else:
-            q4k.gemv_batch(tasks, ncols, ws, stream=stream)
-
-    def run_step(ev=None):
-        for gi, G in enumerate(L):
-            if ev is not None:
-                ev[gi][0].record(stream)
-            gemv(G["tasks"])
-            if ev is not None:
-                ev[gi][1].record(stream)
-            if world > 1 and not peer:
-                dist.all_gather_into_tensor(G["gath"], G["ybuf"])
-
-    # ---- one untimed step: checks the device status word before timing ------
-    with torch.cuda.stream(stream):
-        run_step()
-    stream.synchronize()
-    assert ws.status(stream) == 0, "device status word reports an error"
-
-    # ---- capture the step: launches chained back to back (no events between
-    # them, which would break the programmatic-dependency overlap) -----------
-    use_graph = not args.no_graph
-    step_graph = None
-    if use_graph:
-        try:
-            with torch.cuda.stream(stream):
-                step_graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(step_graph, stream=stream):
-                    run_step()
-        except Exception as e:  # capture unsupported: time eagerly
-            print(f"# graph capture failed ({e!r}); timing eager launches", file=sys.stderr)
-            use_graph, step_graph = False, None
-
-    def replay():
-        with torch.cuda.stream(stream):  # replay() launches on the current stream
-            if use_graph:
-                step_graph.replay()
-            else:
-                run_step()
+    C = Ctx(args, torch, dist, q4k)
+    rank = C.rank
+    peak, peak_kind = measured_peaks()
+    O = load_oracle() if (world > 1 or (rank == 0 and not args.no_cpu_baseline)) else None
 
     uuid = None
     try:
-        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        uuid = str(torch.cuda.get_device_properties(C.dev).uuid)
     except AttributeError:
         pass
     sampler = ClockSampler(uuid) if rank == 0 else None
-
-    # Clock samples (every 200 ms) need load around the short timed region:
-    # the sampler runs from an untimed soak of step replays (~0.8 s) through
-    # the warm-up and the timed steps.  Every rank replays the same number of
-    # soak steps (rank 0's count).
     if sampler:
         sampler.start()
-    nsoak, t_soak = 0, time.perf_counter()
-    while time.perf_counter() - t_soak < 0.8 and nsoak < 4000:
-        for _ in range(10):
-            replay()
-        nsoak += 10
-        torch.cuda.synchronize(dev)
-    if world > 1:
-        t = torch.tensor([nsoak], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        for _ in range(int(t[0]) - nsoak):
-            replay()
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-    for _ in range(args.warmup):
-        replay()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    for _ in range(args.steps):
-        replay()
-    t_end.record(stream)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    clocks = sampler.stop() if sampler else None
-    ms = t_start.elapsed_time(t_end) / args.steps
 
-    # ---- isolated launches (events between launches serialize them) ---------
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in L]
-    with torch.cuda.stream(stream):
-        run_step(ev)
-    torch.cuda.synchronize(dev)
-    nrep = len(groups) - len(WORKLOADS[args.config][3])  # the repeated group only
-    iso_ms = float(np.mean([a.elapsed_time(b) for a, b in ev[: max(1, nrep)]]))
-    if world > 1:
-        t = torch.tensor([ms, iso_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, iso_ms = float(t[0]), float(t[1])
-
-    step_total = sum(group_bytes(G, ncols, world) for G in groups)
-    value = step_total / (ms * 1e-3) / 1e12
-    peak, peak_kind = measured_peaks()
-    nlaunch = len(groups)
-    launch_us = ms * 1e3 / nlaunch
-    # Every launch of the timed step is k_gemv (with its programmatic-dependent
-    # prep): its average duration in the chained step is step time / launches;
-    # achieved bandwidth per rank = the rank's step bytes / step time.
+    # ---- headline ------------------------------------------------------------
+    W = Workload(C, args.config, args.ncols, args.layers)
+    with torch.cuda.stream(W.stream):
+        W.run_step()  # one untimed step: checks the device status word before timing
+    W.stream.synchronize()
+    if int(C.max_over_ranks([1 if W.status() != 0 else 0])[0]):
+        raise SystemExit("device status word reports an error")
+    parity = W.parity_check(O) if world > 1 else None
+    W.capture()
+    t = W.time_steps(soak_s=0.8)
+    head = summarize(W, t, peak)
+    ms = t["ms"]
+    ncols = args.ncols
+    step_total = W.step_bytes()
+    nlaunch = len(W.groups)
     achieved = step_total / world / (ms * 1e-3) / 1e9
-    g0 = groups[0]
     if world == 1:
-        launch_bytes = group_bytes(g0, ncols)
+        launch_bytes = group_bytes(W.groups[0], ncols)
     else:  # this rank's share of the first launch group
-        launch_bytes = (sum(wbytes(e["n"], e["K"], e["glu"]) + ncols * e["n"] * 4 for e in L[0]["ents"]) +
-                        sum(ncols * x.shape[1] * 4 for x in L[0]["xs"].values()))
+        launch_bytes = (sum(wbytes(e["n"], e["K"], e["glu"]) + ncols * e["n"] * 4 for e in W.L[0]["ents"]) +
+                        sum(ncols * x.shape[1] * 4 for x in W.L[0]["xs"].values()))
 
-    # ---- e2e: public C-ABI calls with host buffers ------------------------------
+    # ---- e2e: public C-ABI calls with host buffers ---------------------------
     e2e = None
     if not args.no_e2e:
-        xs_all = [x_all]
-        ys_all = [pg.out] if peer else [y_all]
+        xs_all = [W.x_all]
+        ys_all = [W.pg.out] if C.peer else [W.y_all]
         h_x = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in xs_all]
         for h, d in zip(h_x, xs_all):
             h.copy_(d)
@@ -534,97 +722,125 @@ def main():
         d2h = sum(h.numel() * 4 for h in h_y)
 
         def e2e_step():
-            with torch.cuda.stream(stream):
+            with torch.cuda.stream(W.stream):
                 for h, d in zip(h_x, xs_all):
                     d.copy_(h, non_blocking=True)
-                run_step()
+                W.run_step()
                 for h, d in zip(h_y, ys_all):
                     h.copy_(d, non_blocking=True)
 
         for _ in range(args.warmup):
             e2e_step()
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
+        C.barrier()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
+        a.record(W.stream)
         for _ in range(args.steps):
             e2e_step()
-        b.record(stream)
-        torch.cuda.synchronize(dev)
-        e_ms = a.elapsed_time(b) / args.steps
-        if world > 1:
-            t = torch.tensor([e_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = float(t[0])
+        b.record(W.stream)
+        torch.cuda.synchronize(C.dev)
+        e_ms = C.max_over_ranks([a.elapsed_time(b) / args.steps])[0]
         e2e = {"value": step_total / (e_ms * 1e-3) / 1e12, "unit": "TB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms,
-               "path": "q4k_gemv_batch C-ABI calls (ctypes), one per launch group, eager (no graph); every "
-                       "step one copy of all its activations pinned host -> device before the calls and one "
-                       "copy of all its outputs device -> pinned host after them"}
-
-    # the GEMV kernel each distinct launch group runs (the library's own choice)
-    try:
-        kernels = "k_gemv (Q6_K)" if q6 else (
-            "k_gemv (gather epilogue)" if peer else sorted({q4k.batch_kernel(G["tasks"], ncols) for G in L}))
-    except Exception as e:  # a report, never a reason to lose the measurement
-        kernels = f"unknown ({e!r})"
+               "path": "batch C-ABI calls (ctypes), one per launch group, eager (no graph); every step one copy "
+                       "of all its activations pinned host -> device before the calls and one copy of all its "
+                       "outputs device -> pinned host after them" +
+                       ("; the gather wait before the copy back" if C.peer else "")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        O = load_oracle()
+        g0 = W.groups[0]
         mats = [(M.cpu().numpy(), e["K"], a, e["glu"] == "q6")
-                for e, (_, _, _, a, _) in zip(L[0]["ents"], map(ent, g0))
+                for e, (_, _, _, a, _) in zip(W.L[0]["ents"], map(ent, g0))
                 for M in (e["W"], e["W_gate"]) if M is not None]
         cpu = cpu_baseline(O, mats, g0, ncols)
+    kernels = W.kernels()
+    wname, full_run, shapes = W.name, W.full_run, sorted({f"{r}x{K}" for grp in W.groups
+                                                          for _, r, K, _, _ in map(ent, grp)})
+    fused, peer = W.fused, C.peer
+    W.free()
+    del W
 
-    traffic = None
-    tf = PROFILES / "gemv_layer_traffic.json"
-    if tf.exists() and world == 1 and args.config == "2":
-        d = json.loads(tf.read_text())
-        if d.get("ncols") == ncols:
-            traffic = d.get("dram_bytes_per_launch")
+    # ---- the other BASELINE configs ------------------------------------------
+    per_config = {}
+    if not args.no_per_config and args.layers is None:
+        todo = PER_CONFIG_1GPU if world == 1 else PER_CONFIG_SHARDED
+        for cfg, nc in todo:
+            if cfg == args.config and nc == args.ncols:
+                continue
+            key = f"{cfg}" if cfg != "3" else f"3/ncols={nc}"
+            try:
+                Wc = Workload(C, cfg, nc, None)
+                with torch.cuda.stream(Wc.stream):
+                    Wc.run_step()
+                Wc.stream.synchronize()
+                if int(C.max_over_ranks([1 if Wc.status() != 0 else 0])[0]):
+                    raise RuntimeError("device status word reports an error")
+                par = Wc.parity_check(O) if world > 1 else None
+                Wc.capture()
+                tc = Wc.time_steps(soak_s=0.3)
+                per_config[key] = summarize(Wc, tc, peak)
+                if par is not None:
+                    per_config[key]["parity"] = par
+                Wc.free()
+                del Wc
+            except Exception as e:  # one config's failure must not lose the headline
+                per_config[key] = {"error": repr(e)[:300]}
+                torch.cuda.synchronize(C.dev)
 
+    if sampler:
+        sampler.stop()
+    win = "untimed soak of step replays + warm-up + timed steps"
+    clocks = sampler.summary(t["hs"], t["h1"], win) if sampler else None
+    for v in per_config.values():
+        w = v.pop("window", None)
+        if w is not None:
+            v["clocks"] = sampler.summary(w[0], w[1], win) if sampler else None
     if rank == 0:
-        shapes = sorted({f"{r}x{K}" for grp in groups for _, r, K, _, _ in map(ent, grp)})
+        traffic = None
+        tf = PROFILES / "gemv_layer_traffic.json"
+        if tf.exists() and world == 1 and args.config == "2":
+            d = json.loads(tf.read_text())
+            if d.get("ncols") == ncols:
+                traffic = d.get("dram_bytes_per_launch")
         line = {
-            "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": head["tbs"], "unit": "TB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded, generated on the device)",
             "config": {"workload": wname if full_run else f"{wname} (profiling subset)",
                        "baseline_config": args.config, "launch_groups": nlaunch, "shapes": shapes,
                        "ncols": ncols, "gemv_kernels": kernels,
-                       "launches": "per group: prep (q8_1 quantization) + persistent GEMV over the group's "
-                                   "matrices, chained with programmatic dependencies" + (
+                       "launches": "per group: q8_1 quantization + persistent GEMV over the group's matrices, "
+                                   "chained with programmatic dependencies" + (
                                        "; ffn gate+up as one task with the SwiGLU epilogue" if fused else ""),
                        "timing": "one CUDA graph per step, CUDA events on the launch stream around all timed steps",
                        "l2": "inputs larger than L2 (weights per step >= 3x the 126 MB L2), no flush needed",
                        "parallelism": "single GPU" if world == 1 else (
-                           f"row-shard x{world}, outputs all-gathered inside the GEMV over NVLink peer stores"
-                           if peer else f"row-shard x{world} + NCCL all-gather per launch")},
-            "us_per_call": launch_us,
-            "us_per_launch_isolated": iso_ms * 1e3,
-            "pct_hbm_peak": 100.0 * value * 1e3 / world / peak,
+                           f"row-shard x{world}, outputs stored into every rank's buffer inside the GEMV over "
+                           f"NVLink peer stores" if peer else f"row-shard x{world} + NCCL all-gather per launch")},
+            "us_per_call": ms * 1e3 / nlaunch,
+            "us_per_launch_isolated": head["us_per_launch_isolated"],
+            "pct_hbm_peak": 100.0 * achieved / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
                          "kernel": f"{', '.join(kernels) if isinstance(kernels, list) else kernels}: "
-                                   "every launch of the step, each with its programmatic-dependent prep "
-                                   "launch; achieved = step bytes per rank / step time",
+                                   "every launch of the step, each with its quantization step; "
+                                   "achieved = step bytes per rank / step time",
                          "algorithmic_bytes_per_launch": launch_bytes,
-                         "launch_isolated_gbs": launch_bytes / (iso_ms * 1e-3) / 1e9},
+                         "launch_isolated_gbs": launch_bytes / (head["us_per_launch_isolated"] * 1e-6) / 1e9},
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
-            "gpu_launches": args.steps * nlaunch * 2,
-            "graph": use_graph,
+            "gpu_launches": args.steps * nlaunch * 2 + (args.steps if peer else 0),
+            "graph": not args.no_graph,
+            "per_config": per_config,
         }
+        if parity is not None:
+            line["parity"] = parity["parity"]
+            line["parity_detail"] = parity
         print(json.dumps(line), flush=True)
 
     if world > 1:
-        step_graph = None
-        torch.cuda.synchronize(dev)
+        torch.cuda.synchronize(C.dev)
         dist.barrier()
-        if pg is not None:
-            pg.close()
         dist.destroy_process_group()
 
 
