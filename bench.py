@@ -448,11 +448,17 @@ class Workload:
         self.stream = torch.cuda.Stream(device=dev)
         self.graph = None
         self.use_graph = not C.args.no_graph
+        self.single = C.args.path == "single"
+        if self.single and not (self.fused or self.q6):
+            self.ws.init(self.stream)  # the single-launch calls need zeroed control words once
 
     # -- launches ---------------------------------------------------------------
     def gemv(self, tasks):
         q4k, C, ws, s = self.C.q4k, self.C, self.ws, self.stream
-        if C.peer:
+        if self.single and not (self.fused or self.q6):
+            # one launch per group where the tasks allow it (else two)
+            q4k.gemv_batch_persistent(tasks, self.ncols, ws, stream=s, gather=self.pg if C.peer else None)
+        elif C.peer:
             q4k.gemv_batch_allgather(tasks, self.ncols, self.pg, ws, stream=s)
         elif self.fused:
             q4k.gemv_batch_ex(tasks, self.ncols, ws, stream=s)
@@ -607,6 +613,9 @@ class Workload:
         try:
             if self.q6:
                 return "k_gemv (Q6_K)"
+            if self.single and not self.fused:
+                ks = sorted({q4k.batch_persistent_kernel(G["tasks"], self.ncols) for G in self.L})
+                return [k + (" + gather epilogue" if self.C.peer else "") for k in ks]
             if self.C.peer:
                 return "k_gemv (gather epilogue)"
             return sorted({q4k.batch_kernel(G["tasks"], self.ncols) for G in self.L})
@@ -653,6 +662,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-per-config", action="store_true", help="measure the headline config only")
+    ap.add_argument("--path", default="single", choices=["single", "two"],
+                    help="single: q4k_gemv_batch_persistent (one launch per group where the tasks allow it, "
+                         "else two); two: q4k_gemv_batch (quantization launch + GEMV launch)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -758,6 +770,7 @@ def main():
     wname, full_run, shapes = W.name, W.full_run, sorted({f"{r}x{K}" for grp in W.groups
                                                           for _, r, K, _, _ in map(ent, grp)})
     fused, peer = W.fused, C.peer
+    single_all = isinstance(kernels, list) and all("single launch" in k for k in kernels)
     W.free()
     del W
 
@@ -810,8 +823,12 @@ def main():
             "config": {"workload": wname if full_run else f"{wname} (profiling subset)",
                        "baseline_config": args.config, "launch_groups": nlaunch, "shapes": shapes,
                        "ncols": ncols, "gemv_kernels": kernels,
-                       "launches": "per group: q8_1 quantization + persistent GEMV over the group's matrices, "
-                                   "chained with programmatic dependencies" + (
+                       "path": args.path,
+                       "launches": ("per group: one persistent GEMV launch over the group's matrices whose CTAs "
+                                    "quantize the activations into shared memory (two launches where that mode "
+                                    "does not apply)" if args.path == "single" else
+                                    "per group: q8_1 quantization launch + persistent GEMV launch over the group's "
+                                    "matrices") + ", chained with programmatic dependencies" + (
                                        "; ffn gate+up as one task with the SwiGLU epilogue" if fused else ""),
                        "timing": "one CUDA graph per step, CUDA events on the launch stream around all timed steps",
                        "l2": "inputs larger than L2 (weights per step >= 3x the 126 MB L2), no flush needed",
@@ -829,7 +846,7 @@ def main():
                          "algorithmic_bytes_per_launch": launch_bytes,
                          "launch_isolated_gbs": launch_bytes / (head["us_per_launch_isolated"] * 1e-6) / 1e9},
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
-            "gpu_launches": args.steps * nlaunch * 2 + (args.steps if peer else 0),
+            "gpu_launches": args.steps * nlaunch * (1 if single_all else 2) + (args.steps if peer else 0),
             "graph": not args.no_graph,
             "per_config": per_config,
         }

@@ -142,6 +142,7 @@ def lib() -> ctypes.CDLL:
             "q4k_ipc_open": (None, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
             "q4k_ipc_close": (None, [_P]),
             "q4k_batch_ex_kernel": (_I, [TXP, _I, _I, _I]),
+            "q4k_batch_persistent_kernel": (_I, [TP, _I, _I, _I]),
             "q4k_timeline_bytes": (_SZ, []),
             "q4k_timeline_read": (None, [_P, _SZ, ctypes.POINTER(_I)]),
             "q4k_timeline_reset": (None, []),
@@ -427,7 +428,7 @@ def batch_ex_workspace_bytes(tasks, ncols: int) -> int:
 
 
 KERNEL_NAMES = {0: "k_gemv", 2: "k_gemv (epilogue)", 3: "k_gemv (two rows per lane)", 5: "k_gemv_dyn",
-                6: "k_gemv_dyn (epilogue)"}
+                6: "k_gemv_dyn (epilogue)", 7: "k_gemv (single launch)"}
 
 
 def batch_kernel(tasks, ncols: int, num_sms: int | None = None) -> str:
@@ -443,6 +444,18 @@ def batch_kernel(tasks, ncols: int, num_sms: int | None = None) -> str:
             ex[i].t = t
         tasks = ex
     k = int(lib().q4k_batch_ex_kernel(tasks, len(tasks), ncols, num_sms))
+    if k < 0:
+        _check(1)
+    return KERNEL_NAMES.get(k, str(k))
+
+
+def batch_persistent_kernel(tasks, ncols: int, num_sms: int | None = None) -> str:
+    """Name of the GEMV kernel gemv_batch_persistent runs for these q4k_task
+    tasks: "k_gemv (single launch)", or its two-launch fallback's kernel."""
+    if num_sms is None:
+        import torch
+        num_sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    k = int(lib().q4k_batch_persistent_kernel(tasks, len(tasks), ncols, num_sms))
     if k < 0:
         _check(1)
     return KERNEL_NAMES.get(k, str(k))
@@ -492,7 +505,8 @@ def mul_mat_vec_q8_1_fused(W, W_gate, yq, K: int, glu: str = "swiglu", x_bias=No
 
 
 def gemv_batch_persistent(tasks, ncols: int, ws: Workspace, stream=None, gather=None) -> None:
-    """q4k_gemv_batch in a single launch (quantization inside the GEMV grid).
+    """q4k_gemv_batch in a single launch (each CTA quantizes its activations
+    into shared memory) where the tasks allow it, else the two-launch sequence.
 
     ws is zeroed on first use (and whenever it grows); afterwards every
     completed call leaves its control words zero.  gather: a PeerGather for

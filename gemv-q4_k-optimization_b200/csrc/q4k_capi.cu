@@ -258,12 +258,103 @@ struct Plan {
 #endif
 constexpr int kSchedForce = Q4K_SCHED_FORCE;
 
+// ---- single-launch mode (activations quantized into each CTA's shared memory)
+// Plain Q4_K tasks with fp32 activations whose blocks can be read in 32-byte
+// pieces (32-byte aligned columns), at most kActSmemMaxCols columns.
+bool asm_eligible(const Job *jobs, int njobs, int ncols, const Plan &P, bool dump) {
+    if (dump || P.q6 || P.any_fused || P.mode != kModePlain || ncols > kActSmemMaxCols) return false;
+    for (int i = 0; i < njobs; ++i) {
+        const Job &j = jobs[i];
+        if (P.act_of_job[i] < 0) continue;
+        if (j.kind != kPrepF32 || j.norm || j.gate || j.x_bias || j.q6) return false;
+        if ((reinterpret_cast<uintptr_t>(j.src) & 31u) != 0 || (ncols > 1 && j.src_col_stride % 8 != 0)) return false;
+    }
+    return true;
+}
+
+int task_of_atom_host(const GemvParams &G, int64_t a) {
+    int t = 0;
+    while (t + 1 < G.ntasks && a >= G.task[t + 1].atom_base) ++t;
+    return t;
+}
+
+// Which activations each CTA's atoms read (the tasks its workers' atom ranges
+// span; a bit per activation, into G.cta_act_mask) and the largest table any
+// CTA needs (bytes).  The kernel lays its table out from these bits.
+int64_t act_smem_need(GemvParams &G, int grid, int ncols) {
+    // (worker_begin of the kernel)
+    auto wbegin = [&](int64_t w) -> int64_t {
+        if (G.tapered) {
+            const int64_t c = w / G.rings, r = w - c * G.rings;
+            return G.cta_atom0[c] + (G.cta_atom0[c + 1] - G.cta_atom0[c]) * r / G.rings;
+        }
+        return G.natoms * w / G.nworkers;
+    };
+    const int R = kActSmemRings;
+    auto bytes_of = [&](uint32_t mask) {
+        int64_t b = 0;
+        for (int a = 0; a < G.n_act; ++a)
+            if ((mask >> a) & 1u) b += static_cast<int64_t>(ncols) * G.task[G.act_task[a]].nb * kActSBBytes;
+        return b;
+    };
+    int64_t worst = 0;
+    auto begin = wbegin;
+    for (int c = 0; c < grid; ++c) {
+        uint32_t mask = 0;
+        auto add_range = [&](int64_t a0, int64_t a1) {
+            if (a1 <= a0) return;
+            const int t1 = task_of_atom_host(G, a1 - 1);
+            for (int t = task_of_atom_host(G, a0); t <= t1; ++t) mask |= 1u << G.task[t].act_id;
+        };
+        if (G.packed) {
+            // the CTA's workers are consecutive: one contiguous atom range
+            const int64_t w0 = static_cast<int64_t>(c) * R;
+            const int64_t w1 = w0 + R < G.nworkers ? w0 + R : G.nworkers;
+            if (w0 < w1) add_range(begin(w0), begin(w1));
+        } else {
+            for (int r = 0; r < R; ++r) {
+                const int64_t w = static_cast<int64_t>(r) * grid + c;
+                if (w < G.nworkers) add_range(begin(w), begin(w + 1));
+            }
+        }
+        G.cta_act_mask[c] = static_cast<uint16_t>(mask);
+        const int64_t b = bytes_of(mask);
+        if (b > worst) worst = b;
+    }
+    return worst;
+}
+
+// Per-CTA atom ranges of a packed launch (the kernel's worker_begin reads
+// them): CTA c's share has weight 1000, less for the last Q4K_TAPER_CTAS CTAs
+// (a linear ramp down to 1000 - Q4K_TAPER_PERMILLE), the atoms split in
+// proportion to the running weight.  Launches that are not packed, or with
+// more CTAs than the table holds, keep the uniform split.
+void fill_cta_table(GemvParams &G, int grid, int rings) {
+    G.tapered = 0;
+    G.rings = rings;
+    if (Q4K_TAPER_PERMILLE <= 0 || !G.packed || grid > kMaxPlanCtas || G.nworkers != int64_t{grid} * rings) return;
+    const int tc = Q4K_TAPER_CTAS < grid ? Q4K_TAPER_CTAS : grid;
+    auto weight = [&](int c) -> int64_t {
+        const int k = c - (grid - tc);  // 0 .. tc-1 in the tapered tail
+        return k < 0 ? 1000 : 1000 - int64_t{Q4K_TAPER_PERMILLE} * (k + 1) / tc;
+    };
+    int64_t total = 0;
+    for (int c = 0; c < grid; ++c) total += weight(c);
+    int64_t run = 0;
+    for (int c = 0; c <= grid; ++c) {
+        G.cta_atom0[c] = static_cast<int32_t>(G.natoms * run / total);
+        if (c < grid) run += weight(c);
+    }
+    G.tapered = 1;
+}
+
 // want_dyn: use the dynamically scheduled kernel when the launch qualifies
 // (plain or gated Q4_K tasks whose row groups give every warp of a CTA at
 // least one atom, and at least two row groups per SM); its tasks are ordered
 // by decreasing K.
 int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, Plan &P,
-              int32_t *dump_T = nullptr, bool dump = false, size_t ws_bytes = 0, bool want_dyn = false) {
+              int32_t *dump_T = nullptr, bool dump = false, size_t ws_bytes = 0, bool want_dyn = false,
+              bool want_asm = false) {
     if (njobs < 1 || njobs > kMaxTasks) return fail(Q4K_EINVAL, "ntasks=%d outside 1..%d", njobs, kMaxTasks);
     for (int i = 0; i < njobs; ++i) {
         int st = validate_job(jobs[i], ncols, i);
@@ -376,11 +467,7 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         T.apr = static_cast<int32_t>(apr);
         T.rg_base = static_cast<int32_t>(rgs);
         T.ngroups = static_cast<int32_t>(groups);
-        // The first task of each distinct activation quantizes it on the
-        // single-launch path.
-        T.act_owner = 1;
-        for (int k = 0; k < i; ++k)
-            if (P.act_of_job[k] == P.act_of_job[i]) T.act_owner = 0;
+        T.act_id = P.act_of_job[i];
         T.x = j.kind == kPrepF32 ? static_cast<const float *>(j.src) : nullptr;
         T.x_col_stride = j.src_col_stride;
         T.has_gate = j.gate ? 1 : 0;
@@ -404,12 +491,31 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.gemv.nworkers = static_cast<int32_t>(nw);
     P.gemv.packed = atoms >= 4 * max_workers ? 1 : 0;
     P.gemv.pad0_ = 0;
+    fill_cta_table(P.gemv, num_sms, rings_m(ncols, P.mode));
     // the epilogue variant keeps gate partials, the two-row one the second row's
     P.gemv.pcols = (P.any_fused || P.r2) ? 2 * ncols : ncols;
     P.gemv.dyn_groups = dyn ? static_cast<int32_t>(rgs) : 0;
     P.layout = make_layout(rgs, P.gemv.pcols, P.act_bytes, 2 * nw);
-    P.gemv.fused = 0;
-    P.gemv.ncols = ncols;
+    // distinct activations: a task that reads each
+    P.gemv.n_act = P.n_act;
+    for (int a = 0; a < kMaxTasks; ++a) P.gemv.act_task[a] = -1;
+    for (int t = 0; t < nt; ++t)
+        if (P.gemv.act_task[P.gemv.task[t].act_id] < 0) P.gemv.act_task[P.gemv.task[t].act_id] = t;
+    P.gemv.act_smem_bytes = 0;
+    if (want_asm && num_sms <= kMaxPlanCtas && asm_eligible(jobs, njobs, ncols, P, dump)) {
+        for (int a = 0; a < kMaxTasks; ++a) {
+            const int t = P.gemv.act_task[a];
+            P.gemv.act_x[a] = t >= 0 ? P.gemv.task[t].x : nullptr;
+            P.gemv.act_xcs[a] = t >= 0 ? P.gemv.task[t].x_col_stride : 0;
+            P.gemv.act_nb[a] = t >= 0 ? P.gemv.task[t].nb : 0;
+            P.gemv.task_act[a] = static_cast<int8_t>(a < nt ? P.gemv.task[a].act_id : -1);
+        }
+        const int64_t need = act_smem_need(P.gemv, num_sms, ncols);
+        if (need <= kActSmemCap) {
+            P.mode = kModeActSmem;
+            P.gemv.act_smem_bytes = static_cast<int32_t>(round_up(static_cast<size_t>(need), 128));
+        }
+    }
     if (ws == nullptr) return Q4K_OK;
     if (ws_bytes < P.layout.total)
         return fail(Q4K_EWORKSPACE, "workspace of %zu bytes < %zu required", ws_bytes, P.layout.total);
@@ -576,9 +682,10 @@ int timeline_attach(Plan &P) {
 #endif
 
 
-// fused: one launch that quantizes the activations itself (fp32 jobs only;
-// the workspace header and counters must be zero on entry, which every
-// completed call leaves them).
+// fused: run the batch as one launch that quantizes the activations itself
+// (kModeActSmem) where the tasks allow it, else as the two-launch sequence;
+// the workspace's status word, gather count and split counters must be zero
+// on entry, which every completed call leaves them.
 int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes, cudaStream_t s,
         int32_t *dump_S = nullptr, int32_t *dump_T = nullptr, const q4k_gather *gather = nullptr,
         bool fused = false) {
@@ -601,7 +708,7 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
     // The device's plan (its SM count fixes the workers and the layout); the
     // workspace size is checked before any pointer into it is formed.
     st = make_plan(jobs, njobs, ncols, static_cast<uint8_t *>(workspace), num_sms, P, dump_T, dump, ws_bytes,
-                   !fused && !gathering && kSchedForce != 1);
+                   !fused && !gathering && kSchedForce != 1, fused);
     if (st != Q4K_OK) return st;
     P.gemv.dump_S = dump_S;
     P.gemv.gworld = 1;
@@ -621,14 +728,7 @@ int run(const Job *jobs, int njobs, int ncols, void *workspace, size_t ws_bytes,
 #if Q4K_TIMELINE
     if ((st = timeline_attach(P)) != Q4K_OK) return st;
 #endif
-    if (fused) {
-        uint8_t *w8 = static_cast<uint8_t *>(workspace);
-        P.gemv.fused = 1;
-        // its own line, apart from the status word
-        P.gemv.bar_arrive = reinterpret_cast<unsigned long long *>(w8 + 128);
-    } else if ((e = launch_prep(P.prep, s)) != cudaSuccess) {
-        return cuda_fail(e, "prep launch");
-    }
+    if (P.mode != kModeActSmem && (e = launch_prep(P.prep, s)) != cudaSuccess) return cuda_fail(e, "prep launch");
     const int mode = P.mode;
     if ((e = launch_gemv(P.gemv, ncols, mode, num_sms, s)) != cudaSuccess)
         return cuda_fail(e, "gemv launch");
@@ -858,6 +958,26 @@ int q4k_batch_ex_kernel(const q4k_task_ex *tasks, int ntasks, int ncols, int num
                       Q4K_KERNEL_STATIC_TWO_ROW == kModeR2 && Q4K_KERNEL_DYNAMIC == kModeDynPlain &&
                       Q4K_KERNEL_DYNAMIC_GATED == kModeDynGated,
                   "kernel ids");
+    return P.mode;
+}
+
+int q4k_batch_persistent_kernel(const q4k_task *tasks, int ntasks, int ncols, int num_sms) {
+    if (!tasks || ntasks < 1 || ntasks > kMaxTasks) {
+        fail(Q4K_EINVAL, "ntasks=%d outside 1..16", ntasks);
+        return -1;
+    }
+    if (num_sms < 1 || num_sms > 4096) {
+        fail(Q4K_EINVAL, "num_sms=%d outside 1..4096", num_sms);
+        return -1;
+    }
+    Job jobs[kMaxTasks];
+    for (int i = 0; i < ntasks; ++i)
+        jobs[i] = {tasks[i].W, tasks[i].x, tasks[i].dst, tasks[i].nrows, tasks[i].K,
+                   tasks[i].stride_row_x, tasks[i].stride_col_x, tasks[i].stride_col_dst, kPrepF32};
+    Plan P;
+    // the decision run() makes for q4k_gemv_batch_persistent
+    if (make_plan(jobs, ntasks, ncols, nullptr, num_sms, P, nullptr, false, 0, false, true) != Q4K_OK) return -1;
+    static_assert(Q4K_KERNEL_SINGLE_LAUNCH == kModeActSmem, "kernel ids");
     return P.mode;
 }
 

@@ -167,6 +167,18 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm,
 __device__ __forceinline__ void prefetch_l2(const void *p) {
     asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
 }
+// L2 evict-last policy (data read again soon: activations among the weight stream).
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// Non-binding bulk L2 prefetch of [p, p + bytes) (16-byte aligned, bytes a
+// multiple of 16), kept with the evict-last policy.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *p, uint32_t bytes, uint64_t policy) {
+    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(p), "r"(bytes), "l"(policy)
+                 : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }

@@ -80,6 +80,9 @@ static_assert(warps_for(8) * 32 <= 1024, "block too large");
 // lane (one activation load serves both rows).  kModeQ6: Q6_K weights.
 // kModeDynPlain / kModeDynGated: the plain and gated arithmetic in the
 // dynamically scheduled kernel (k_gemv_dyn: whole row groups per CTA).
+// kModeActSmem: the plain arithmetic and partition in one launch: every CTA
+// quantizes the activations its atoms need straight into shared memory
+// (no separate quantization launch), ring stages carry weights only.
 enum GemvMode : int {
     kModePlain = 0,
     kModeDump = 1,
@@ -87,7 +90,8 @@ enum GemvMode : int {
     kModeR2 = 3,
     kModeQ6 = 4,
     kModeDynPlain = 5,
-    kModeDynGated = 6
+    kModeDynGated = 6,
+    kModeActSmem = 7
 };
 #ifndef Q4K_R2_MIN
 #define Q4K_R2_MIN 3
@@ -138,21 +142,52 @@ constexpr int kDynAhead = 3;
 __host__ __device__ constexpr bool is_dyn(int mode) {
     return mode == kModeDynPlain || mode == kModeDynGated;
 }
+// Single-launch mode: up to kActSmemMaxCols columns; shared memory beyond the
+// rings (8 warps x kStages x one weight stage) holds the CTA's activation
+// records, at most kActSmemCap bytes (the rest of the 227 KB, less a reserve
+// for the kernel's static shared memory).
+constexpr int kActSmemMaxCols = 2;
+constexpr int kActSmemRings = kMaxWarps;
+constexpr int kActSmemStatic = 2048;
+constexpr int kActSmemCap = kSmemLimit - kActSmemRings * kStages * kWStageBytes - kActSmemStatic;
+constexpr int kMaxPlanCtas = 256;  // launches of more CTAs (SMs) run the two-launch sequence
+// Work taper of packed launches: the last Q4K_TAPER_CTAS CTAs (dispatched
+// last: with programmatic dependencies a grid's CTAs start in index order as
+// the previous grid's CTAs leave their SMs) get linearly fewer atoms, down to
+// (1000 - Q4K_TAPER_PERMILLE) / 1000 of a full share for the last one.
+#ifndef Q4K_TAPER_PERMILLE
+#define Q4K_TAPER_PERMILLE 0
+#endif
+#ifndef Q4K_TAPER_CTAS
+#define Q4K_TAPER_CTAS 48
+#endif
+static_assert(kActSmemCap > 0, "no room for activations beside the rings");
 __host__ __device__ constexpr int stage_bytes_m(int ncols, int mode) {
-    return mode == kModeQ6 ? q6_stage_bytes(ncols) : stage_bytes(ncols);
+    return mode == kModeQ6 ? q6_stage_bytes(ncols) : mode == kModeActSmem ? kWStageBytes : stage_bytes(ncols);
 }
 __host__ __device__ constexpr int rings_m(int ncols, int mode) {
-    return mode == kModeQ6 ? rings_q6(ncols) : is_dyn(mode) ? rings_dyn(ncols, mode == kModeDynGated) : rings_for(ncols);
+    return mode == kModeQ6         ? rings_q6(ncols)
+           : is_dyn(mode)          ? rings_dyn(ncols, mode == kModeDynGated)
+           : mode == kModeActSmem  ? kActSmemRings
+                                   : rings_for(ncols);
 }
 __host__ __device__ constexpr int warps_m(int ncols, int mode) {
-    return mode == kModeQ6 ? rings_q6(ncols) : is_dyn(mode) ? rings_dyn(ncols, mode == kModeDynGated) : warps_for(ncols);
+    return mode == kModeQ6         ? rings_q6(ncols)
+           : is_dyn(mode)          ? rings_dyn(ncols, mode == kModeDynGated)
+           : mode == kModeActSmem  ? kActSmemRings
+                                   : warps_for(ncols);
 }
+// The single-launch mode keeps the plain kernel's partition (same rings per
+// CTA), so both paths give bit-identical results.
+static_assert(rings_for(1) == kActSmemRings && rings_for(2) == kActSmemRings && split_for(2) == 1,
+              "single-launch partition differs from the two-launch one");
 __host__ __device__ constexpr int smem_m(int ncols, int mode) {
     return rings_m(ncols, mode) * kStages * stage_bytes_m(ncols, mode);
 }
 
 // Device status codes (match q4k_status).
 constexpr int kStatusOk = 0;
+constexpr int kStatusBadPlan = 1;  // a launch plan the kernel refused (Q4K_EINVAL)
 constexpr int kStatusTimeout = 3;
 // Bounded waits: a bulk copy that has not landed after this long is an error.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
@@ -182,7 +217,7 @@ struct TaskDesc {
     int32_t apr;             // atoms per row group = ceil(nb / kKS)
     int32_t rg_base;         // global row-group index of row group 0
     int32_t ngroups;         // row groups = ceil(nrows / 32)
-    int32_t act_owner;       // single-launch path: 1 if this task quantizes its activation
+    int32_t act_id;          // index of this task's distinct activation
     // single-launch path: the fp32 activation this task's q8a records come from
     const float *x;
     int64_t x_col_stride;    // floats between activation columns
@@ -228,11 +263,27 @@ struct GemvParams {
     uint32_t *gepoch;                // this rank's epoch word (persists across calls)
     uint32_t *gdone;                 // CTAs finished (workspace; zero at kernel start)
     GatherWait gwait;                // single-launch path: wait for the previous gather before reading x
-    // Single-launch path (fused quantization + grid barrier): sync words in an
-    // initialised workspace that every launch leaves as it found them.
-    int32_t fused;
-    int32_t ncols;
-    unsigned long long *bar_arrive;  // grid-barrier arrivals, counts up by gridDim.x per launch
+    // Single-launch path: the distinct activations (a task that reads each,
+    // its fp32 columns, column stride and super-blocks), which of them each
+    // CTA's atoms read (a bit per activation, computed on the host), each
+    // task's activation, and the shared-memory bytes every CTA has for the
+    // q8a records.  Flat tables, so that a CTA's plan reads few parameter lines.
+    int32_t n_act;
+    int32_t act_smem_bytes;
+    int32_t act_task[kMaxTasks];
+    const float *act_x[kMaxTasks];
+    int64_t act_xcs[kMaxTasks];
+    int32_t act_nb[kMaxTasks];
+    int8_t task_act[kMaxTasks];
+    uint16_t cta_act_mask[kMaxPlanCtas];
+    // Packed launches with a per-CTA split (tapered = 1): CTA c's workers
+    // cover atoms [cta_atom0[c], cta_atom0[c + 1]), split evenly among its
+    // `rings` workers.  The host sets the shares (the CTAs dispatched last,
+    // which start last, get fewer atoms); tapered = 0: every worker gets
+    // natoms / nworkers.
+    int32_t tapered;
+    int32_t rings;
+    int32_t cta_atom0[kMaxPlanCtas + 1];
     int32_t *dyn_claim;              // dynamically scheduled launches: group tickets (zero at kernel start)
     unsigned long long *tl;          // launch timeline records (Q4K_TIMELINE builds; else nullptr)
     int32_t tl_slot;

@@ -273,12 +273,28 @@ __device__ __forceinline__ void advance(const GemvParams &P, AtomCursor &c) {
     }
 }
 
-// First atom of worker w under the uniform partition of natoms over nworkers.
+// First atom of worker w: uniform partition of natoms over nworkers, or the
+// per-CTA table of a tapered launch (CTA c = w / rings, its range split
+// evenly among its rings).
 __device__ __forceinline__ int64_t worker_begin(const GemvParams &P, int64_t w) {
+    if (P.tapered) {
+        const int64_t c = w / P.rings, r = w - c * P.rings;
+        const int64_t a0 = P.cta_atom0[c];
+        return a0 + (P.cta_atom0[c + 1] - a0) * r / P.rings;
+    }
     return P.natoms * w / P.nworkers;
 }
-// Worker whose range holds atom a.
+// Worker whose range holds atom a (the largest w with worker_begin(w) <= a).
 __device__ __forceinline__ int64_t worker_of(const GemvParams &P, int64_t a) {
+    if (P.tapered) {
+        const int64_t G = P.nworkers / P.rings;
+        int64_t c = a * G / P.natoms;  // near the answer: walk to it
+        if (c > G - 1) c = G - 1;
+        while (c > 0 && P.cta_atom0[c] > a) --c;
+        while (c + 1 < G && P.cta_atom0[c + 1] <= a) ++c;
+        const int64_t a0 = P.cta_atom0[c], n = P.cta_atom0[c + 1] - a0;
+        return c * P.rings + ((a - a0 + 1) * P.rings - 1) / n;
+    }
     return ((a + 1) * P.nworkers - 1) / P.natoms;
 }
 
@@ -327,7 +343,8 @@ __device__ __forceinline__ void issue_weights(const GemvParams &P, const AtomCur
         } else {
             const int kb0 = c.kp * kKS;
             const int nsb = min(kKS, T.nb - kb0);
-            mbar_expect_tx(bar, static_cast<uint32_t>(nsb * (kBoxBytes + NC * kActSBBytes)));
+            // (the single-launch mode's stages carry weights only)
+            mbar_expect_tx(bar, static_cast<uint32_t>(nsb * (kBoxBytes + (MODE == kModeActSmem ? 0 : NC * kActSBBytes))));
 #pragma unroll
             for (int i = 0; i < kKS; ++i)
                 if (i < nsb) Q4K_TMA(stage + i * kBoxBytes, &P.tmap[c.t], (kb0 + i) * 36, c.g * 32, bar);
@@ -342,6 +359,7 @@ __device__ __forceinline__ void issue_weights(const GemvParams &P, const AtomCur
 template <int NC, int MODE>
 __device__ __forceinline__ void issue_acts(const GemvParams &P, const AtomCursor &c, uint32_t stage,
                                            uint32_t bar, int lane) {
+    if constexpr (MODE == kModeActSmem) return;  // records already in shared memory
     const TaskDesc &T = P.task[c.t];
     if constexpr (MODE == kModeQ6) {
         // the 8 records of the atom's super-blocks, per column, at a 336-byte pitch
@@ -378,8 +396,8 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, unsign
 // (weights at p) against NC activation records (act, column stride acs).
 // acc[j] holds a packed pair of partial sums for column j.
 template <int NC, bool DUMP>
-__device__ __forceinline__ void pair_dot(uint32_t p, uint32_t act, int c, float d, float nd23, float dmin,
-                                         float pm23, uint32_t scw, uint32_t mw, uint64_t (&acc)[NC],
+__device__ __forceinline__ void pair_dot(uint32_t p, uint32_t act, uint32_t acs, int c, float d, float nd23,
+                                         float dmin, float pm23, uint32_t scw, uint32_t mw, uint64_t (&acc)[NC],
                                          int32_t *dumpS, int64_t dump_col_stride) {
     const int b0 = (c & 1) * 2;
     // d*sc and -dmin*m of sub-blocks 2c, 2c+1: (byte + 2^23)*x - 2^23*x == byte*x, one rounding
@@ -398,7 +416,7 @@ __device__ __forceinline__ void pair_dot(uint32_t p, uint32_t act, int c, float 
     const uint64_t magic2 = f2_pack(-kMagicF, -kMagicF);
 #pragma unroll
     for (int j = 0; j < NC; ++j) {
-        const uint32_t aj = act + j * (kKS * kActSBBytes);
+        const uint32_t aj = act + j * acs;
         const uint4 qe0 = lds128(aj + 64 * c);
         const uint4 qe1 = lds128(aj + 64 * c + 16);
         const uint4 qo0 = lds128(aj + 64 * c + 32);
@@ -425,10 +443,11 @@ __device__ __forceinline__ void pair_dot(uint32_t p, uint32_t act, int c, float 
 }
 
 // One super-block of one row: weights at p, the activation records of its
-// NC columns at act.  Semantics of kernels/vecdotq.cuh:461-483, :775-819.
+// NC columns at act, acs bytes apart.  Semantics of kernels/vecdotq.cuh:461-483,
+// :775-819.
 template <int NC, bool DUMP>
-__device__ __forceinline__ void sb_dot(uint32_t p, uint32_t act, uint64_t (&acc)[NC], int32_t *dumpS,
-                                       int64_t dump_col_stride) {
+__device__ __forceinline__ void sb_dot(uint32_t p, uint32_t act, uint32_t acs, uint64_t (&acc)[NC],
+                                       int32_t *dumpS, int64_t dump_col_stride) {
     const uint4 h = lds128(p);
     const float2 dm = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
     const float d = dm.x, dmin = dm.y;
@@ -442,13 +461,13 @@ __device__ __forceinline__ void sb_dot(uint32_t p, uint32_t act, uint64_t (&acc)
     if constexpr (NC <= 2) {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-            pair_dot<NC, DUMP>(p, act, c, d, nd23, dmin, pm23, c < 2 ? sc03 : sc47, c < 2 ? m03 : m47, acc,
-                               dumpS, dump_col_stride);
+            pair_dot<NC, DUMP>(p, act, acs, c, d, nd23, dmin, pm23, c < 2 ? sc03 : sc47, c < 2 ? m03 : m47,
+                               acc, dumpS, dump_col_stride);
     } else {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c)
-            pair_dot<NC, DUMP>(p, act, c, d, nd23, dmin, pm23, c < 2 ? sc03 : sc47, c < 2 ? m03 : m47, acc,
-                               dumpS, dump_col_stride);
+            pair_dot<NC, DUMP>(p, act, acs, c, d, nd23, dmin, pm23, c < 2 ? sc03 : sc47, c < 2 ? m03 : m47,
+                               acc, dumpS, dump_col_stride);
     }
 }
 
@@ -694,9 +713,18 @@ __device__ __forceinline__ void add_sb(RowAcc<NCW> &acc, const uint64_t (&sb)[NC
     }
 }
 
+// Where the single-launch mode keeps a CTA's activation records: the base of
+// the shared-memory region after the rings and, per task, its byte offset
+// there (column j of super-block kb at base + off + j * nb * 320 + kb * 320).
+struct ActView {
+    uint32_t base;
+    const int *task_off;
+};
+
 template <int NCW, int NC, int MODE>
 __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCursor &c, uint32_t stage, int lane,
-                                             int j0, RowAcc<NCW> &acc, RowAcc<NCW> &gacc, RowAccD<NCW> &dacc) {
+                                             int j0, RowAcc<NCW> &acc, RowAcc<NCW> &gacc, RowAccD<NCW> &dacc,
+                                             const ActView &AV) {
     const TaskDesc &T = P.task[c.t];
     if constexpr (MODE == kModeQ6) {
         // row lane & 7 of the group, super-blocks 2q and 2q+1 (q = lane >> 3)
@@ -722,17 +750,23 @@ __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCurs
     const int rows = min(32, T.nrows - c.g * 32);
     if (lane >= rows) return;
     constexpr bool DUMP = MODE == kModeDump;
-    const uint32_t act = stage + Stage<NC, MODE>::kActOff + j0 * (kKS * kActSBBytes);
+    constexpr bool ASM = MODE == kModeActSmem;
+    // records of the atom's super-blocks: in the ring stage (copied per atom),
+    // or in the CTA's activation table (single-launch mode)
+    const uint32_t acs = ASM ? static_cast<uint32_t>(T.nb) * kActSBBytes : kKS * kActSBBytes;
+    const uint32_t act = ASM ? AV.base + static_cast<uint32_t>(AV.task_off[c.t]) + j0 * acs +
+                                   static_cast<uint32_t>(c.kp * kKS) * kActSBBytes
+                             : stage + Stage<NC, MODE>::kActOff + j0 * acs;
     if constexpr (MODE == kModeGated) {
         if (T.has_gate) {
             uint64_t sb[NCW];
 #pragma unroll
             for (int j = 0; j < NCW; ++j) sb[j] = 0ull;
-            sb_dot<NCW, false>(stage + lane * kPitch, act, sb, nullptr, 0);
+            sb_dot<NCW, false>(stage + lane * kPitch, act, kKS * kActSBBytes, sb, nullptr, 0);
             add_sb(acc, sb);
 #pragma unroll
             for (int j = 0; j < NCW; ++j) sb[j] = 0ull;
-            sb_dot<NCW, false>(stage + kBoxBytes + lane * kPitch, act, sb, nullptr, 0);
+            sb_dot<NCW, false>(stage + kBoxBytes + lane * kPitch, act, kKS * kActSBBytes, sb, nullptr, 0);
             add_sb(gacc, sb);
             return;
         }
@@ -752,7 +786,7 @@ __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCurs
             uint64_t sb[NCW];
 #pragma unroll
             for (int j = 0; j < NCW; ++j) sb[j] = 0ull;
-            sb_dot<NCW, DUMP>(stage + i * kBoxBytes + lane * kPitch, act + i * kActSBBytes, sb, dS, dcs);
+            sb_dot<NCW, DUMP>(stage + i * kBoxBytes + lane * kPitch, act + i * kActSBBytes, acs, sb, dS, dcs);
             add_sb(acc, sb);
         }
     }
@@ -931,18 +965,51 @@ struct WorkerPipe {
 // any earlier grid: the weights are read-only).
 // (A column-split partner only follows the cursors: issue == false.)
 template <int NC, int MODE>
+// In the single-launch mode only the first stage is issued here; the others
+// follow once the CTA's activation loads are in flight (issue_rest_prologue),
+// so that a CTA starting after the previous grid has completed does not queue
+// its activations behind a whole ring of weights.
 __device__ __forceinline__ void worker_prologue(const GemvParams &P, WorkerPipe &W, int lane,
                                                 const uint32_t (&bar)[kStages], bool issue) {
     constexpr int kSB = Stage<NC, MODE>::kBytes;
+    constexpr int kNow = MODE == kModeActSmem ? 1 : kStages;
     W.icur = locate_atom(P, W.a0);
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
         W.pro[s] = W.icur;
         if (s < W.n) {
-            if (issue) issue_weights<NC, MODE>(P, W.icur, W.ring + s * kSB, bar[s], lane);
+            if (issue && s < kNow) issue_weights<NC, MODE>(P, W.icur, W.ring + s * kSB, bar[s], lane);
             advance(P, W.icur);
         }
     }
+}
+
+template <int NC, int MODE>
+__device__ __forceinline__ void issue_rest_prologue(const GemvParams &P, const WorkerPipe &W, int lane,
+                                                    const uint32_t (&bar)[kStages]) {
+    constexpr int kSB = Stage<NC, MODE>::kBytes;
+#pragma unroll
+    for (int s = 1; s < kStages; ++s)
+        if (s < W.n) issue_weights<NC, MODE>(P, W.pro[s], W.ring + s * kSB, bar[s], lane);
+}
+
+// Start-up: touch every kernel-parameter line the prologue and the plan read
+// (one thread per task, in parallel), and ask for the tasks' tensor maps, so
+// that the walk over the task table that follows does not take one
+// constant-cache miss after another.
+__device__ __forceinline__ void warm_params(const GemvParams &P) {
+    const int t = threadIdx.x;
+    uint64_t v = 0;
+    if (t < P.ntasks) {
+        const TaskDesc &T = P.task[t];
+        v = reinterpret_cast<uint64_t>(T.W) ^ static_cast<uint64_t>(T.atom_base) ^
+            static_cast<uint64_t>(T.bias_col_stride) ^ static_cast<uint64_t>(T.apr);
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&P.tmap[t]) : "memory");
+    } else if (t == 32) {
+        v = static_cast<uint64_t>(P.natoms) ^ static_cast<uint64_t>(P.nworkers) ^
+            static_cast<uint64_t>(P.act_nb[0]) ^ static_cast<uint64_t>(P.cta_act_mask[blockIdx.x % kMaxPlanCtas]);
+    }
+    asm volatile("" ::"l"(v));  // keep the loads
 }
 
 // The rest of one worker's range, once the activations are ready: stream its
@@ -955,7 +1022,7 @@ template <int NC, int NCW, int MODE>
 __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, int64_t worker, int lane, int j0,
                                             bool issuer, const uint32_t (&full)[kStages],
                                             const uint32_t (&empty)[kStages], int64_t cta_w0, int64_t cta_w1,
-                                            int *cta_cnt) {
+                                            int *cta_cnt, const ActView &AV) {
     constexpr int kSB = Stage<NC, MODE>::kBytes;
     constexpr bool kShared = split_for(NC) > 1;
     const int n = W.n;
@@ -994,7 +1061,7 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
         }
         bool ok = wait_phase(full[s], parity, kWaitLimitNs);
         if (ok) {
-            compute_atom<NCW, NC, MODE>(P, cur, ring + s * kSB, lane, j0, acc, gacc, dacc);
+            compute_atom<NCW, NC, MODE>(P, cur, ring + s * kSB, lane, j0, acc, gacc, dacc, AV);
             __syncwarp();
             if constexpr (kShared) {
                 if (lane == 0) mbar_arrive(empty[s]);
@@ -1030,64 +1097,181 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
     }
 }
 
-// Single-launch path, before the main loop: every warp of the grid quantizes
-// a share of the activation blocks of the tasks that own an activation (the
-// same arithmetic as k_prep); a grid barrier then makes the q8a records of
-// all CTAs visible before any activation copy is issued.
-__device__ __forceinline__ void fused_quantize(const GemvParams &P) {
+// ---- single-launch mode: activations quantized into shared memory ----------
+// Which distinct activations a CTA's atoms read, and where their q8a records
+// go in its shared memory.  The host sizes the region with the same rule
+// (act_smem_need in the C ABI), so both agree on every CTA's need.
+struct ActPlan {
+    int n;                     // activations this CTA needs
+    int act[kMaxTasks];        // their ids, increasing
+    int off[kMaxTasks];        // byte offset of each in the region
+    int blk0[kMaxTasks + 1];   // prefix sums of their q8_1 blocks (ncols * nb * 8 each)
+    int task_off[kMaxTasks];   // per task: offset of its activation (-1: not needed)
+    int bytes;                 // region bytes used
+};
+
+// Task holding global atom a (a < natoms).
+__device__ __forceinline__ int task_of_atom(const GemvParams &P, int64_t a) {
+    int t = 0;
+    while (t + 1 < P.ntasks && a >= P.task[t + 1].atom_base) ++t;
+    return t;
+}
+
+// Laid out by lane 0 of one warp from the host's tables: the CTA's bit set of
+// activations (cta_act_mask, the same rule as act_smem_need in the C ABI:
+// the tasks its workers' atom ranges span), their super-block counts and the
+// tasks' activation ids -- a few parameter lines, read once.
+template <int NC>
+__device__ void act_plan_cta(const GemvParams &P, ActPlan &A) {
+    const uint32_t mask = P.cta_act_mask[blockIdx.x];
+    int nb[kMaxTasks], ta[kMaxTasks];
+#pragma unroll
+    for (int a = 0; a < kMaxTasks; ++a) {
+        nb[a] = P.act_nb[a];
+        ta[a] = P.task_act[a];
+    }
+    int off = 0, n = 0, blk = 0;
+    int off_of[kMaxTasks];
+    A.blk0[0] = 0;
+#pragma unroll
+    for (int a = 0; a < kMaxTasks; ++a) {
+        off_of[a] = -1;
+        if (!((mask >> a) & 1u)) continue;
+        A.act[n] = a;
+        A.off[n] = off;
+        off_of[a] = off;
+        off += NC * nb[a] * kActSBBytes;
+        blk += NC * nb[a] * 8;
+        A.blk0[++n] = blk;
+    }
+    A.n = n;
+    A.bytes = off;
+#pragma unroll
+    for (int t = 0; t < kMaxTasks; ++t) A.task_off[t] = ta[t] >= 0 ? off_of[ta[t]] : -1;
+}
+
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+// 32 bytes (one L2 sector) from a 32-byte aligned address, cached in L2 only.
+__device__ __forceinline__ void ldg_cg_f8(const float *p, float (&v)[8]) {
+    asm volatile("ld.global.cg.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+                 : "l"(p));
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+__device__ __forceinline__ void sts32f(uint32_t a, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+
+// One half of a q8_1 block per lane: lanes 2i and 2i+1 take values [0, 16)
+// and [16, 32) of a block (32-byte aligned: each lane reads two whole L2
+// sectors, so every sector is requested once per CTA) and write them into its q8a
+// record slot (sub-block s of the record at rec).  Semantics of
+// quantize_value / write_q8a, bit for bit: d = amax/127 (IEEE division),
+// q = amax == 0 ? 0 : roundf(x/d), d8 = float(half(d)), T = sum of q.
+// The quotient x/d is formed as t = x * r with r ~ 1/d (approximate
+// reciprocal plus one Newton step, so |t - x/d| < 2^-15 for |x/d| <= 127.x):
+// where t is not within 2^-14 of a half-integer, x/d rounded to nearest lies
+// on the same side of every half-integer as t, so roundf(x/d) = rint(t),
+// formed with the 1.5 * 2^23 addition (the integer lands in the low mantissa
+// bits; its low byte is the int8 quant).  The loop over the values has no
+// branch (so their chains interleave); values near a half-integer (about 1
+// in 8000), or whose scale is zero or subnormal, are marked and recomputed
+// with the IEEE division afterwards.  Both lanes of a pair must execute this
+// (the amax and T exchanges); store = false computes without writing.
+template <typename F>
+__device__ __forceinline__ void quantize_half_block(const float *src, uint32_t rec, int s, int half, bool store,
+                                                    bool first, F &&after_loads) {
+    float v[16], v1[8];
+    ldg_cg_f8(src, reinterpret_cast<float(&)[8]>(v[0]));
+    ldg_cg_f8(src + 8, v1);
+    if (first) after_loads();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[8 + i] = v1[i];
+    float m8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m8[i] = fmaxf(fabsf(v[i]), fabsf(v[i + 8]));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m8[i] = fmaxf(m8[i], m8[i + 4]);
+    float amax = fmaxf(fmaxf(m8[0], m8[2]), fmaxf(m8[1], m8[3]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    const float d = amax / 127.0f;  // IEEE division (no fast-math in this build)
+    const __half dh = __float2half_rn(d);
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    int T = 0;
+    if (amax != 0.0f) {
+        float r = rcp_approx_ftz(d);
+        r = __fmaf_rn(__fmaf_rn(-d, r, 1.0f), r, r);
+        constexpr float kMagic = 12582912.0f;               // 1.5 * 2^23
+        constexpr float kNearTie = 0.5f - 6.103515625e-05f;  // 0.5 - 2^-14
+        uint32_t qb[16];
+        uint32_t redo = 0u;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float t = __fmul_rn(v[i], r);
+            const float m = __fadd_rn(t, kMagic);
+            const float rt = __fsub_rn(m, kMagic);
+            qb[i] = __float_as_uint(m);  // low byte: rint(t) as int8
+            redo |= (fabsf(__fsub_rn(t, rt)) < kNearTie ? 0u : 1u) << i;
+        }
+        if (redo != 0u) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                if ((redo >> i) & 1u) qb[i] = static_cast<uint32_t>(static_cast<int>(roundf(v[i] / d)));
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            w[k] = __byte_perm(__byte_perm(qb[4 * k], qb[4 * k + 1], 0x0040u),
+                               __byte_perm(qb[4 * k + 2], qb[4 * k + 3], 0x0040u), 0x5410u);
+            T = dp4a_ss(w[k], 0x01010101u, T);
+        }
+    }
+    T += __shfl_xor_sync(0xffffffffu, T, 1);
+    if (!store) return;
+    sts128(rec + 32 * s + 16 * half, w[0], w[1], w[2], w[3]);
+    if (half == 0) {
+        const float d8 = __half2float(dh);
+        const uint32_t meta = rec + kActMetaOff + 16 * (s >> 1) + 4 * (s & 1);
+        sts32f(meta, (s & 1) ? d8 * 0.0625f : d8);
+        sts32f(meta + 8, d8 * static_cast<float>(T));
+    }
+}
+
+// All q8_1 blocks of the CTA's activations, half a block per lane, every
+// warp of the CTA: lane l of warp w takes half-block (w + k * warps) * 32 + l.
+// after_loads() runs once per warp, right after the warp's first loads are
+// issued (or at once if it has none).
+template <int NC, typename F>
+__device__ __forceinline__ void quantize_acts_smem(const GemvParams &P, const ActPlan &A, uint32_t base,
+                                                   F &&after_loads) {
     const int lane = threadIdx.x & 31;
-    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-    const int64_t wid = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    int64_t base = 0;
-    for (int t = 0; t < P.ntasks; ++t) {
-        const TaskDesc &T = P.task[t];
-        if (!T.act_owner) continue;
-        const int nblk = T.nb * 8;
-        const int64_t items = static_cast<int64_t>(P.ncols) * nblk;
-        // warp wid takes items wid - base, wid - base + nw, ... of this task
-        int64_t first = wid - base;
-        if (first < 0) first += ((-first + nw - 1) / nw) * nw;
-        for (int64_t it = first; it < items; it += nw) {
-            const int col = static_cast<int>(it / nblk);
-            const int b = static_cast<int>(it - static_cast<int64_t>(col) * nblk);
-            int q;
-            __half dh;
-            quantize_value(T.x[col * T.x_col_stride + b * 32 + lane], q, dh);
-            write_q8a(const_cast<uint8_t *>(T.act) + col * T.act_col_stride, b, lane, q, dh, nullptr);
-        }
-        base += items;
+    const int nwarps = blockDim.x >> 5;
+    const int total = 2 * A.blk0[A.n];  // half-blocks (even)
+    bool pending = true;
+    for (int chunk = threadIdx.x >> 5; chunk * 32 < total; chunk += nwarps) {
+        const int gh0 = chunk * 32 + lane;
+        const bool store = gh0 < total;
+        const int gh = store ? gh0 : total - 2 + (lane & 1);  // pairs stay pairs
+        const int gb = gh >> 1;
+        int i = 0;
+        while (gb >= A.blk0[i + 1]) ++i;
+        const int a = A.act[i];
+        const int nb = P.act_nb[a];
+        const int nbl = nb * 8;
+        const int rem = gb - A.blk0[i];
+        const int j = rem / nbl;
+        const int b = rem - j * nbl;
+        const uint32_t rec = base + static_cast<uint32_t>(A.off[i] + (j * nb + (b >> 3)) * kActSBBytes);
+        quantize_half_block(P.act_x[a] + j * P.act_xcs[a] + b * 32 + 16 * (gh & 1), rec, b & 7, gh & 1, store,
+                            pending, after_loads);
+        pending = false;
     }
-}
-
-// Grid-wide barrier over all CTAs of this launch (one CTA per SM, all
-// resident).  The arrival counter only counts up, by gridDim.x per launch, so
-// it needs no reset: a CTA reads it after griddepcontrol.wait (the previous
-// launch's arrivals are complete, this launch's are fewer than gridDim.x),
-// which fixes this launch's target, the next multiple of gridDim.x.  The
-// arrival is a release reduction by one thread after bar.sync (publishing the
-// CTA's stores) and the waiters acquire the counter; the wait is bounded.
-__device__ __forceinline__ unsigned long long barrier_target(const GemvParams &P) {
-    const unsigned long long v0 = ld_relaxed_gpu_u64(P.bar_arrive);
-    return v0 - v0 % gridDim.x + gridDim.x;
-}
-
-__device__ __forceinline__ void grid_barrier_arrive(const GemvParams &P) {
-    __syncthreads();
-    if (threadIdx.x == 0) red_add_release_gpu_u64(P.bar_arrive, 1ull);
-}
-
-__device__ __forceinline__ void grid_barrier_wait(const GemvParams &P, unsigned long long target) {
-    if (threadIdx.x == 0) {
-        const uint64_t t0 = globaltimer_ns();
-        for (uint32_t it = 0;; ++it) {
-            if (ld_acquire_gpu_u64(P.bar_arrive) >= target) break;
-            if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
-                atomicExch(P.status, kStatusTimeout);
-                break;
-            }
-        }
-    }
-    __syncthreads();
+    if (pending) after_loads();
 }
 
 // Fused all-gather epilogue (producer side): after every CTA of this grid has
@@ -1132,6 +1316,9 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
     __shared__ __align__(8) uint64_t full_bars[kR][kStages];
     __shared__ __align__(8) uint64_t empty_bars[kR][kStages];
     __shared__ int cta_cnt[kR];  // arrivals at row groups split between this CTA's workers
+    constexpr bool ASM = MODE == kModeActSmem;
+    __shared__ ActPlan act_plan[1];  // single-launch mode only
+    __shared__ int plan_ok;
 
 #if Q4K_TIMELINE
     const uint64_t tl_start = globaltimer_ns();
@@ -1142,6 +1329,7 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int rid = warp / kSplit;           // ring = worker slot in this CTA
+    if constexpr (MODE == kModeActSmem) warm_params(P);
     const int half = warp - rid * kSplit;    // 0: issuer, columns [0, kNC0); 1: columns [kNC0, NC)
     if (threadIdx.x < kR) {
         cta_cnt[threadIdx.x] = 0;
@@ -1178,34 +1366,77 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
     // or the previous single-launch GEMV) finishes; griddepcontrol.wait
     // returns once it has completed.
     if (active) worker_prologue<NC, MODE>(P, W, lane, full, issuer);
+    if constexpr (ASM) {
+        // this CTA's activation table (after the weight copies are out); a
+        // plan the region cannot hold (the host sizes it with the same rule)
+        // is refused, never overrun
+        if (threadIdx.x == 0) {
+            act_plan_cta<NC>(P, act_plan[0]);
+            plan_ok = blockIdx.x < kMaxPlanCtas && act_plan[0].bytes <= P.act_smem_bytes;
+            // Ask L2 for the activation columns while the previous grid runs: a
+            // prefetch binds no value (if that grid writes x, the loads after
+            // the wait still see its stores; L2 is the point of coherence).
+            const uint64_t pol = l2_evict_last_policy();
+            const ActPlan &A = act_plan[0];
+            for (int i = 0; i < A.n; ++i) {
+                const int a = A.act[i];
+                for (int j = 0; j < NC; ++j)
+                    bulk_prefetch_l2(P.act_x[a] + j * P.act_xcs[a], static_cast<uint32_t>(P.act_nb[a]) * kQK * 4u,
+                                     pol);
+            }
+        }
+    }
+#if Q4K_TIMELINE
+    const uint64_t tl_plan = globaltimer_ns();
+#endif
     pdl_wait();
 #if Q4K_TIMELINE
     const uint64_t tl_wait = globaltimer_ns();
 #endif
-    if (P.fused) {
-        // Single launch: quantize this CTA's share of the activations, then a
-        // grid barrier before any activation copy.  (Issuing the weights after
-        // the arrival instead measured slower: the copies no longer overlap
-        // the previous grid's tail.)
-        unsigned long long target = 0;
-        if (threadIdx.x == 0) {
-            target = barrier_target(P);
-            if (blockIdx.x == 0) *P.status = kStatusOk;
-            if (P.gworld > 1) gather_wait_flags(P.gwait);  // x may be a gathered output
+    const ActView AV{smem_addr(smem) + static_cast<uint32_t>(kR * kStages * kSB), ASM ? act_plan[0].task_off : nullptr};
+#if Q4K_TIMELINE
+    uint64_t tl_d[3] = {0, 0, 0};  // single-launch mode: after the plan barrier, before / after quantizing
+#endif
+    if constexpr (ASM) {
+        // Single launch: the activations are read after the previous grid on
+        // the stream has completed (it may have written them), quantized by
+        // every warp of the CTA into its activation table, then used by all.
+        __syncthreads();  // the plan
+#if Q4K_TIMELINE
+        tl_d[0] = globaltimer_ns();
+#endif
+        if (!plan_ok) {
+            if (threadIdx.x == 0) atomicExch(P.status, kStatusBadPlan);
+            // let this warp's weight copy (the first stage only, so far) land
+            // (bounded) before leaving
+            if (active && issuer && W.n > 0) wait_phase(full[0], 0u, kDrainLimitNs);
+            return;
         }
+        if (threadIdx.x == 0 && blockIdx.x == 0) *P.status = kStatusOk;
+        if (P.gworld > 1) {
+            if (threadIdx.x == 0) gather_wait_flags(P.gwait);  // x may be a gathered output
+            __syncthreads();
+        }
+#if Q4K_TIMELINE
+        tl_d[1] = globaltimer_ns();
+#endif
+        quantize_acts_smem<NC>(P, act_plan[0], AV.base, [&]() {
+            if (active && issuer) issue_rest_prologue<NC, MODE>(P, W, lane, full);
+        });
+#if Q4K_TIMELINE
+        tl_d[2] = globaltimer_ns();
+#endif
         __syncthreads();
-        fused_quantize(P);
-        fence_proxy_async_global();  // this thread's q8a stores, before other CTAs' bulk copies
-        grid_barrier_arrive(P);
-        grid_barrier_wait(P, target);
-        fence_proxy_async_global();  // the q8a records are read by bulk copies next
     }
+#if Q4K_TIMELINE
+    const uint64_t tl_quant = globaltimer_ns();
+#endif
     if (active) {
         if (issuer) {
-            worker_main<NC, kNC0, MODE>(P, W, worker, lane, 0, true, full, empty, cta_w0, cta_w1, cta_cnt);
+            worker_main<NC, kNC0, MODE>(P, W, worker, lane, 0, true, full, empty, cta_w0, cta_w1, cta_cnt, AV);
         } else if constexpr (kSplit > 1) {
             worker_main<NC, NC - kNC0, MODE>(P, W, worker, lane, kNC0, false, full, empty, cta_w0, cta_w1,
-                                             cta_cnt);
+                                             cta_cnt, AV);
         }
     }
 #if Q4K_TIMELINE
@@ -1220,8 +1451,19 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
         o[3] = active ? static_cast<unsigned long long>(W.n) : 0ull;
         o[4] = smid;
         o[5] = static_cast<unsigned long long>(worker);
-        o[6] = active ? static_cast<unsigned long long>(W.a0) : 0ull;
-        o[7] = active ? static_cast<unsigned long long>(W.a1) : 0ull;
+        // single-launch mode: when the activation table was planned and when
+        // its quantization ended; else the worker's atom range
+        o[6] = ASM ? tl_quant : active ? static_cast<unsigned long long>(W.a0) : 0ull;
+        o[7] = ASM ? tl_plan : active ? static_cast<unsigned long long>(W.a1) : 0ull;
+        if (ASM && warp + 8 < 16) {
+            // the phases of the quantization, in the record of warp + 8 (word 3
+            // stays 0: not a worker record)
+            unsigned long long *d = o + 8 * 8;
+            d[0] = tl_d[0];
+            d[1] = tl_d[1];
+            d[2] = tl_d[2];
+            d[3] = 0;
+        }
     }
 #endif
     if (!DUMP && P.gworld > 1) gather_epilogue(P);
@@ -1415,7 +1657,7 @@ __global__ void __launch_bounds__(rings_dyn(NC, BASE == kModeGated) * 32, 1)
         const int s = done % kStages;
         ok = wait_phase(full[s], static_cast<uint32_t>((done / kStages) & 1), kWaitLimitNs);
         if (!ok) break;
-        compute_atom<NC, NC, BASE>(P, cc.c, ring + s * kSB, lane, 0, acc, gacc, dacc);
+        compute_atom<NC, NC, BASE>(P, cc.c, ring + s * kSB, lane, 0, acc, gacc, dacc, ActView{0u, nullptr});
         __syncwarp();
         dyn_resolve<R>(P, ic, q_group, q_bar, warp, ok);
         if (!ok) break;
@@ -1561,6 +1803,25 @@ void *gemv_fn_dyn(int ncols) {
     }
 }
 
+// The single-launch variant exists for ncols <= kActSmemMaxCols only.
+cudaError_t set_attrs_asm() {
+    cudaError_t e;
+    static_assert(kActSmemMaxCols == 2, "instantiate the single-launch variant for every width");
+    constexpr int kMax = kSmemLimit - kActSmemStatic;
+    if ((e = cudaFuncSetAttribute(k_gemv<1, kModeActSmem>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax)) !=
+        cudaSuccess)
+        return e;
+    return cudaFuncSetAttribute(k_gemv<2, kModeActSmem>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+}
+
+void *gemv_fn_asm(int ncols) {
+    switch (ncols) {
+        case 1: return reinterpret_cast<void *>(k_gemv<1, kModeActSmem>);
+        case 2: return reinterpret_cast<void *>(k_gemv<2, kModeActSmem>);
+        default: return nullptr;
+    }
+}
+
 // The two-row variant exists for ncols >= kR2Min only.
 cudaError_t set_attrs_r2() {
     cudaError_t e;
@@ -1616,6 +1877,7 @@ cudaError_t device_setup(int *num_sms) {
         if ((e = set_attrs_all<kModeQ6>()) != cudaSuccess) return e;
         if ((e = set_attrs_dyn<kModePlain>()) != cudaSuccess) return e;
         if ((e = set_attrs_dyn<kModeGated>()) != cudaSuccess) return e;
+        if ((e = set_attrs_asm()) != cudaSuccess) return e;
         st.ready = true;
     }
     *num_sms = st.num_sms;
@@ -1665,12 +1927,15 @@ cudaError_t launch_gemv(const GemvParams &p, int ncols, int mode, int grid, cuda
                : mode == kModeQ6    ? gemv_fn<kModeQ6>(ncols)
                : mode == kModeDynPlain ? gemv_fn_dyn<kModePlain>(ncols)
                : mode == kModeDynGated ? gemv_fn_dyn<kModeGated>(ncols)
+               : mode == kModeActSmem  ? gemv_fn_asm(ncols)
                                     : gemv_fn<kModePlain>(ncols);
     if (fn == nullptr) return cudaErrorInvalidValue;
+    if (mode == kModeActSmem && (p.act_smem_bytes < 0 || p.act_smem_bytes > kActSmemCap))
+        return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
     cfg.blockDim = dim3(warps_m(ncols, mode) * 32);
-    cfg.dynamicSmemBytes = smem_m(ncols, mode);
+    cfg.dynamicSmemBytes = smem_m(ncols, mode) + (mode == kModeActSmem ? p.act_smem_bytes : 0);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

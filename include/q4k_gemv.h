@@ -297,20 +297,23 @@ Q4K_API int q4k_gather_wait(const q4k_gather *gather, void *workspace, size_t wo
 /* The calls above issue two launches (activation quantization, then the
  * GEMV) and accept a workspace with arbitrary contents, as ggml's pool hands
  * it out.  A caller that keeps one workspace per stream can save the first
- * launch: q4k_gemv_batch_persistent quantizes the activations inside the GEMV
- * launch (all warps of the grid, then a grid-wide barrier) and needs the same
- * workspace size (q4k_batch_workspace_bytes).  It requires the workspace's
- * control words to be in a known state on entry: zero the workspace once with
+ * launch: q4k_gemv_batch_persistent runs the batch as ONE launch in which
+ * every CTA quantizes the activations its rows need straight into its shared
+ * memory (the same q8_1 semantics, bit for bit) and reads them from there;
+ * the weights start streaming before the previous launch on the stream has
+ * finished.  It applies to plain Q4_K tasks with fp32 activations whose
+ * columns start 32-byte aligned, ncols <= 2, and launches where no CTA needs
+ * more than 81 KB of activation records (e.g. a whole Mistral-7B or
+ * Llama-3-70B decoder layer at ncols 1); other calls run the two-launch
+ * sequence.  Results are identical to q4k_gemv_batch's static kernel.  It
+ * needs the same workspace size (q4k_batch_workspace_bytes) and its control
+ * words in a known state on entry: zero the workspace once with
  * q4k_workspace_init before the first call; every call that completes leaves
  * them valid again (the two-launch calls may use the same workspace in
  * between).  After a call reports Q4K_ETIMEOUT (q4k_workspace_status) call
  * q4k_workspace_init again.  gather may be NULL (no all-gather) or a
- * descriptor as for q4k_gemv_batch_allgather.  Results are identical to
- * q4k_gemv_batch.  All CTAs of the launch (one per SM) must be resident at
- * once; a GPU shared with other work can delay that, in which case the
- * barrier's bounded wait ends with Q4K_ETIMEOUT.  On B200, chained inside a
- * CUDA graph, it measured slightly slower than the two-launch calls, whose
- * quantization launch overlaps the previous GEMV's tail. */
+ * descriptor as for q4k_gemv_batch_allgather; the launch then waits for the
+ * previous gathering call's rows before it reads its activations. */
 Q4K_API int q4k_workspace_init(void *workspace, size_t workspace_bytes, q4k_stream_t stream);
 Q4K_API int q4k_gemv_batch_persistent(const q4k_task *tasks, int ntasks, int ncols, const q4k_gather *gather,
                                       void *workspace, size_t workspace_bytes, q4k_stream_t stream);
@@ -356,7 +359,12 @@ Q4K_API size_t q4k_noalloc_scratch_bytes(void);
 #define Q4K_KERNEL_STATIC_TWO_ROW 3  /* the same, two rows per lane (ncols >= 3) */
 #define Q4K_KERNEL_DYNAMIC 5         /* whole row groups per CTA from a ticket queue */
 #define Q4K_KERNEL_DYNAMIC_GATED 6   /* the same with the bias / GLU epilogue */
+#define Q4K_KERNEL_SINGLE_LAUNCH 7   /* static partition, activations quantized in the GEMV launch */
 Q4K_API int q4k_batch_ex_kernel(const q4k_task_ex *tasks, int ntasks, int ncols, int num_sms);
+/* The same question for q4k_gemv_batch_persistent: Q4K_KERNEL_SINGLE_LAUNCH
+ * when the tasks run as one launch, else the kernel of its two-launch
+ * fallback (its gather argument does not change the answer). */
+Q4K_API int q4k_batch_persistent_kernel(const q4k_task *tasks, int ntasks, int ncols, int num_sms);
 
 /* Per-sub-block integer sums as the kernels form them, for bit-exact parity
  * checks (the GEMV kernel runs in a dump mode and writes no dst):
@@ -385,7 +393,9 @@ Q4K_API int q4k_workspace_status(const void *workspace, int *device_status, q4k_
  *         {start, wait return, end, atoms of the worker (0: idle), SM id,
  *          worker index, first atom, end atom}; the dynamically scheduled
  *          kernel records atoms done in word 3, 0 in word 6 and its last
- *          queue entry in word 7
+ *          queue entry in word 7; the single-launch mode records in words 6
+ *          and 7 when its activations were quantized and when the CTA had
+ *          planned its activation table
  *   prep  u64[slot][Q4K_TIMELINE_PREP_CTAS][4] = {start, wait return, end, 1}
  * q4k_timeline_bytes() is the size of both regions (GEMV first); it returns 0
  * and the other two Q4K_EINVAL in a library built without the option.  Each

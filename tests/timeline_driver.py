@@ -61,30 +61,49 @@ def build_step(q4k, bench, torch, cfg: str, ncols: int, reverse: bool, dev):
     return launches
 
 
-def summarize(G, Pr, n):
-    """Per-launch and aggregate figures (us) from the records of slots 0..n-1."""
+def summarize(G, Pr, n, single=False):
+    """Per-launch and aggregate figures (us) from the records of slots 0..n-1.
+    single: launches of the single-launch mode (no quantization launch; words
+    6 and 7 of a warp's record hold its quantization end and plan time)."""
     per = []
     for i in range(n):
         cta, warp = np.nonzero(G[i][:, :, 3] > 0)
         w = G[i][cta, warp]
         p = Pr[i][Pr[i][:, 3] == 1]
-        if len(w) == 0 or len(p) == 0:
+        if len(w) == 0 or (len(p) == 0 and not single):
             raise SystemExit(f"launch {i}: no records (was the timeline library loaded?)")
         rel = w[:, 1].min()
-        per.append(dict(prep_release=p[:, 1].min(), prep_end=p[:, 2].max(), gemv_release=rel,
-                        gemv_end=w[:, 2].max(), ends=np.sort(w[:, 2] - rel) / 1e3,
-                        end=(w[:, 2] - rel) / 1e3, cta=cta, warp=warp))
+        d = dict(gemv_release=rel, gemv_end=w[:, 2].max(), ends=np.sort(w[:, 2] - rel) / 1e3,
+                 end=(w[:, 2] - rel) / 1e3, cta=cta, warp=warp, start_min=w[:, 0].min())
+        if single:
+            d.update(quant=(w[:, 6] - w[:, 1]) / 1e3, plan=(w[:, 7] - w[:, 0]) / 1e3)
+            # phases in the records of warp + 8: plan barrier, status barrier, quantizer end
+            dd = G[i][cta, warp + 8] if warp.max() < 8 else None
+            if dd is not None and dd[:, 0].min() > 0:
+                d.update(ph_sync1=(dd[:, 0] - w[:, 1]) / 1e3, ph_sync2=(dd[:, 1] - dd[:, 0]) / 1e3,
+                         ph_quant=(dd[:, 2] - dd[:, 1]) / 1e3, ph_sync3=(w[:, 6] - dd[:, 2]) / 1e3)
+        else:
+            d.update(prep_release=p[:, 1].min(), prep_end=p[:, 2].max())
+        per.append(d)
     rows = []
     for i in range(1, n):
         a, b = per[i - 1], per[i]
-        rows.append(dict(
-            launch=i,
-            period=(b["gemv_end"] - a["gemv_end"]) / 1e3,
-            prev_end_to_prep_release=(b["prep_release"] - a["gemv_end"]) / 1e3,
-            prep_run=(b["prep_end"] - b["prep_release"]) / 1e3,
-            prep_end_to_gemv_release=(b["gemv_release"] - b["prep_end"]) / 1e3,
-            end_p10=float(np.percentile(b["ends"], 10)), end_p50=float(np.percentile(b["ends"], 50)),
-            end_p90=float(np.percentile(b["ends"], 90)), end_max=float(b["ends"][-1])))
+        r = dict(launch=i, period=(b["gemv_end"] - a["gemv_end"]) / 1e3)
+        if single:
+            r.update(prev_end_to_release=(b["gemv_release"] - a["gemv_end"]) / 1e3,
+                     quant_p50=float(np.percentile(b["quant"], 50)), quant_max=float(b["quant"].max()),
+                     plan_max=float(b["plan"].max()))
+            for k in ("ph_sync1", "ph_sync2", "ph_quant", "ph_sync3"):
+                if k in b:
+                    r[k + "_p50"] = float(np.percentile(b[k], 50))
+                    r[k + "_max"] = float(b[k].max())
+        else:
+            r.update(prev_end_to_prep_release=(b["prep_release"] - a["gemv_end"]) / 1e3,
+                     prep_run=(b["prep_end"] - b["prep_release"]) / 1e3,
+                     prep_end_to_gemv_release=(b["gemv_release"] - b["prep_end"]) / 1e3)
+        r.update(end_p10=float(np.percentile(b["ends"], 10)), end_p50=float(np.percentile(b["ends"], 50)),
+                 end_p90=float(np.percentile(b["ends"], 90)), end_max=float(b["ends"][-1]))
+        rows.append(r)
     keys = [k for k in rows[0] if k != "launch"]
     mean = {k: float(np.mean([r[k] for r in rows])) for k in keys}
     # worker end times by warp (ring slot of the CTA) and by CTA index, launches 1..n-1
@@ -108,6 +127,8 @@ def main():
     ap.add_argument("--replays", type=int, default=3)
     ap.add_argument("--json", action="store_true", help="print one JSON line instead of tables")
     ap.add_argument("--save", default=None, help="also write the raw records of the step (.npz)")
+    ap.add_argument("--single", action="store_true",
+                    help="q4k_gemv_batch_persistent (single-launch mode) instead of the two-launch calls")
     args = ap.parse_args()
 
     import torch
@@ -123,9 +144,15 @@ def main():
     ws = q4k.Workspace(max(q4k.batch_workspace_bytes(L["tasks"], args.ncols) for L in launches), dev)
     stream = torch.cuda.Stream(device=dev)
 
+    if args.single:
+        ws.init(stream)
+
     def step():
         for L in launches:
-            q4k.gemv_batch(L["tasks"], args.ncols, ws, stream=stream)
+            if args.single:
+                q4k.gemv_batch_persistent(L["tasks"], args.ncols, ws, stream=stream)
+            else:
+                q4k.gemv_batch(L["tasks"], args.ncols, ws, stream=stream)
 
     for _ in range(3):
         step()
@@ -141,8 +168,9 @@ def main():
     n = len(launches)
     if args.save:
         np.savez_compressed(args.save, gemv=G[:n], prep=Pr[:n])
-    rows, mean, ring, cta = summarize(G, Pr, n)
-    out = {"config": args.config, "ncols": args.ncols, "reverse": args.reverse, "launches": n,
+    rows, mean, ring, cta = summarize(G, Pr, n, args.single)
+    out = {"config": args.config, "ncols": args.ncols, "reverse": args.reverse, "single": args.single,
+           "launches": n,
            "mean_us": {k: round(v, 3) for k, v in mean.items()},
            "ring_mean_end_us": {k: round(v, 3) for k, v in ring.items()},
            "cta_mean_end_us": {k: round(v, 3) for k, v in cta.items()}}
@@ -150,11 +178,9 @@ def main():
         print(json.dumps(out))
         return
     print(f"config {args.config}, ncols {args.ncols}, {n} launches per step, graph replay; us")
-    print("launch  period  GEMVend->prepRel  prepRun  prepEnd->GEMVrel  worker end after release: p10 p50 p90 max")
+    print("launch  " + "  ".join(k for k in rows[0] if k != "launch"))
     for r in rows:
-        print(f"{r['launch']:6d} {r['period']:7.2f} {r['prev_end_to_prep_release']:17.2f} {r['prep_run']:8.2f} "
-              f"{r['prep_end_to_gemv_release']:17.2f}   {r['end_p10']:6.2f} {r['end_p50']:6.2f} "
-              f"{r['end_p90']:6.2f} {r['end_max']:6.2f}")
+        print(f"{r['launch']:6d} " + "  ".join(f"{v:7.2f}" for k, v in r.items() if k != "launch"))
     print("mean   " + "  ".join(f"{k} {v:.2f}" for k, v in mean.items()))
     print("mean worker end by ring slot: " + "  ".join(f"{k}:{v:.2f}" for k, v in ring.items()))
     print("mean worker end by CTA index: " + "  ".join(f"{k}:{v:.2f}" for k, v in cta.items()))
