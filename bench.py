@@ -662,6 +662,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-per-config", action="store_true", help="measure the headline config only")
+    ap.add_argument("--soak-s", type=float, default=0.8,
+                    help="untimed replays before the warm-up, seconds (clock sampling window; 0 for profiling runs)")
     ap.add_argument("--path", default="single", choices=["single", "two"],
                     help="single: q4k_gemv_batch_persistent (one launch per group where the tasks allow it, "
                          "else two); two: q4k_gemv_batch (quantization launch + GEMV launch)")
@@ -708,7 +710,7 @@ def main():
         raise SystemExit("device status word reports an error")
     parity = W.parity_check(O) if world > 1 else None
     W.capture()
-    t = W.time_steps(soak_s=0.8)
+    t = W.time_steps(soak_s=args.soak_s)
     head = summarize(W, t, peak)
     ms = t["ms"]
     ncols = args.ncols
@@ -791,7 +793,7 @@ def main():
                     raise RuntimeError("device status word reports an error")
                 par = Wc.parity_check(O) if world > 1 else None
                 Wc.capture()
-                tc = Wc.time_steps(soak_s=0.3)
+                tc = Wc.time_steps(soak_s=min(0.3, args.soak_s))
                 per_config[key] = summarize(Wc, tc, peak)
                 if par is not None:
                     per_config[key]["parity"] = par

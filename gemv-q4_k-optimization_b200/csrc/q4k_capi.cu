@@ -283,13 +283,7 @@ int task_of_atom_host(const GemvParams &G, int64_t a) {
 // CTA needs (bytes).  The kernel lays its table out from these bits.
 int64_t act_smem_need(GemvParams &G, int grid, int ncols) {
     // (worker_begin of the kernel)
-    auto wbegin = [&](int64_t w) -> int64_t {
-        if (G.tapered) {
-            const int64_t c = w / G.rings, r = w - c * G.rings;
-            return G.cta_atom0[c] + (G.cta_atom0[c + 1] - G.cta_atom0[c]) * r / G.rings;
-        }
-        return G.natoms * w / G.nworkers;
-    };
+    auto wbegin = [&](int64_t w) -> int64_t { return G.natoms * w / G.nworkers; };
     const int R = kActSmemRings;
     auto bytes_of = [&](uint32_t mask) {
         int64_t b = 0;
@@ -322,30 +316,6 @@ int64_t act_smem_need(GemvParams &G, int grid, int ncols) {
         if (b > worst) worst = b;
     }
     return worst;
-}
-
-// Per-CTA atom ranges of a packed launch (the kernel's worker_begin reads
-// them): CTA c's share has weight 1000, less for the last Q4K_TAPER_CTAS CTAs
-// (a linear ramp down to 1000 - Q4K_TAPER_PERMILLE), the atoms split in
-// proportion to the running weight.  Launches that are not packed, or with
-// more CTAs than the table holds, keep the uniform split.
-void fill_cta_table(GemvParams &G, int grid, int rings) {
-    G.tapered = 0;
-    G.rings = rings;
-    if (Q4K_TAPER_PERMILLE <= 0 || !G.packed || grid > kMaxPlanCtas || G.nworkers != int64_t{grid} * rings) return;
-    const int tc = Q4K_TAPER_CTAS < grid ? Q4K_TAPER_CTAS : grid;
-    auto weight = [&](int c) -> int64_t {
-        const int k = c - (grid - tc);  // 0 .. tc-1 in the tapered tail
-        return k < 0 ? 1000 : 1000 - int64_t{Q4K_TAPER_PERMILLE} * (k + 1) / tc;
-    };
-    int64_t total = 0;
-    for (int c = 0; c < grid; ++c) total += weight(c);
-    int64_t run = 0;
-    for (int c = 0; c <= grid; ++c) {
-        G.cta_atom0[c] = static_cast<int32_t>(G.natoms * run / total);
-        if (c < grid) run += weight(c);
-    }
-    G.tapered = 1;
 }
 
 // want_dyn: use the dynamically scheduled kernel when the launch qualifies
@@ -491,7 +461,6 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.gemv.nworkers = static_cast<int32_t>(nw);
     P.gemv.packed = atoms >= 4 * max_workers ? 1 : 0;
     P.gemv.pad0_ = 0;
-    fill_cta_table(P.gemv, num_sms, rings_m(ncols, P.mode));
     // the epilogue variant keeps gate partials, the two-row one the second row's
     P.gemv.pcols = (P.any_fused || P.r2) ? 2 * ncols : ncols;
     P.gemv.dyn_groups = dyn ? static_cast<int32_t>(rgs) : 0;

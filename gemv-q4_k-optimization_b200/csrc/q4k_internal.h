@@ -151,16 +151,6 @@ constexpr int kActSmemRings = kMaxWarps;
 constexpr int kActSmemStatic = 2048;
 constexpr int kActSmemCap = kSmemLimit - kActSmemRings * kStages * kWStageBytes - kActSmemStatic;
 constexpr int kMaxPlanCtas = 256;  // launches of more CTAs (SMs) run the two-launch sequence
-// Work taper of packed launches: the last Q4K_TAPER_CTAS CTAs (dispatched
-// last: with programmatic dependencies a grid's CTAs start in index order as
-// the previous grid's CTAs leave their SMs) get linearly fewer atoms, down to
-// (1000 - Q4K_TAPER_PERMILLE) / 1000 of a full share for the last one.
-#ifndef Q4K_TAPER_PERMILLE
-#define Q4K_TAPER_PERMILLE 0
-#endif
-#ifndef Q4K_TAPER_CTAS
-#define Q4K_TAPER_CTAS 48
-#endif
 static_assert(kActSmemCap > 0, "no room for activations beside the rings");
 __host__ __device__ constexpr int stage_bytes_m(int ncols, int mode) {
     return mode == kModeQ6 ? q6_stage_bytes(ncols) : mode == kModeActSmem ? kWStageBytes : stage_bytes(ncols);
@@ -276,14 +266,6 @@ struct GemvParams {
     int32_t act_nb[kMaxTasks];
     int8_t task_act[kMaxTasks];
     uint16_t cta_act_mask[kMaxPlanCtas];
-    // Packed launches with a per-CTA split (tapered = 1): CTA c's workers
-    // cover atoms [cta_atom0[c], cta_atom0[c + 1]), split evenly among its
-    // `rings` workers.  The host sets the shares (the CTAs dispatched last,
-    // which start last, get fewer atoms); tapered = 0: every worker gets
-    // natoms / nworkers.
-    int32_t tapered;
-    int32_t rings;
-    int32_t cta_atom0[kMaxPlanCtas + 1];
     int32_t *dyn_claim;              // dynamically scheduled launches: group tickets (zero at kernel start)
     unsigned long long *tl;          // launch timeline records (Q4K_TIMELINE builds; else nullptr)
     int32_t tl_slot;

@@ -273,28 +273,44 @@ __device__ __forceinline__ void advance(const GemvParams &P, AtomCursor &c) {
     }
 }
 
-// First atom of worker w: uniform partition of natoms over nworkers, or the
-// per-CTA table of a tapered launch (CTA c = w / rings, its range split
-// evenly among its rings).
-__device__ __forceinline__ int64_t worker_begin(const GemvParams &P, int64_t w) {
-    if (P.tapered) {
-        const int64_t c = w / P.rings, r = w - c * P.rings;
-        const int64_t a0 = P.cta_atom0[c];
-        return a0 + (P.cta_atom0[c + 1] - a0) * r / P.rings;
+// The atom before c (never called on atom 0).
+__device__ __forceinline__ void retreat(const GemvParams &P, AtomCursor &c) {
+    if (c.kp > 0) {
+        --c.kp;
+        return;
     }
+    if (c.g > 0) {
+        --c.g;
+    } else {
+        --c.t;
+        c.g = P.task[c.t].ngroups - 1;
+    }
+    c.kp = P.task[c.t].apr - 1;
+}
+
+// Odd workers walk their atom range backwards, so that both sides of every
+// worker boundary read it at about the same time (both first or both last):
+// the tensor-map copies promote each 144-byte row piece to whole 256-byte L2
+// lines, and a line shared by two workers' ranges is then read from DRAM once
+// instead of twice (the second reader used to come a whole range later, long
+// after the line had been evicted).
+#ifndef Q4K_ALTERNATE_WALK
+#define Q4K_ALTERNATE_WALK 1
+#endif
+__device__ __forceinline__ bool walks_back(int64_t worker) { return Q4K_ALTERNATE_WALK && (worker & 1) != 0; }
+__device__ __forceinline__ void step(const GemvParams &P, AtomCursor &c, bool back) {
+    if (back)
+        retreat(P, c);
+    else
+        advance(P, c);
+}
+
+// First atom of worker w under the uniform partition of natoms over nworkers.
+__device__ __forceinline__ int64_t worker_begin(const GemvParams &P, int64_t w) {
     return P.natoms * w / P.nworkers;
 }
-// Worker whose range holds atom a (the largest w with worker_begin(w) <= a).
+// Worker whose range holds atom a.
 __device__ __forceinline__ int64_t worker_of(const GemvParams &P, int64_t a) {
-    if (P.tapered) {
-        const int64_t G = P.nworkers / P.rings;
-        int64_t c = a * G / P.natoms;  // near the answer: walk to it
-        if (c > G - 1) c = G - 1;
-        while (c > 0 && P.cta_atom0[c] > a) --c;
-        while (c + 1 < G && P.cta_atom0[c + 1] <= a) ++c;
-        const int64_t a0 = P.cta_atom0[c], n = P.cta_atom0[c + 1] - a0;
-        return c * P.rings + ((a - a0 + 1) * P.rings - 1) / n;
-    }
     return ((a + 1) * P.nworkers - 1) / P.natoms;
 }
 
@@ -956,6 +972,7 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
 struct WorkerPipe {
     int64_t a0, a1;
     int n;
+    bool back;                  // walks its range from a1 - 1 down to a0
     uint32_t ring;
     AtomCursor icur;            // next atom to issue
     AtomCursor pro[kStages];    // the prologue atoms
@@ -973,13 +990,13 @@ __device__ __forceinline__ void worker_prologue(const GemvParams &P, WorkerPipe 
                                                 const uint32_t (&bar)[kStages], bool issue) {
     constexpr int kSB = Stage<NC, MODE>::kBytes;
     constexpr int kNow = MODE == kModeActSmem ? 1 : kStages;
-    W.icur = locate_atom(P, W.a0);
+    W.icur = locate_atom(P, W.back ? W.a1 - 1 : W.a0);
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
         W.pro[s] = W.icur;
         if (s < W.n) {
             if (issue && s < kNow) issue_weights<NC, MODE>(P, W.icur, W.ring + s * kSB, bar[s], lane);
-            advance(P, W.icur);
+            if (s + 1 < W.n) step(P, W.icur, W.back);
         }
     }
 }
@@ -1072,7 +1089,7 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
                     fence_proxy_async_smem();
                     issue_weights<NC, MODE>(P, icur, ring + s * kSB, full[s], lane);
                     issue_acts<NC, MODE>(P, icur, ring + s * kSB, full[s], lane);
-                    advance(P, icur);
+                    if (i + kStages + 1 < n) step(P, icur, W.back);
                 }
             }
         }
@@ -1088,7 +1105,7 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
             }
             return;
         }
-        advance(P, cur);
+        if (i + 1 < n) step(P, cur, W.back);
     }
     if (open_t >= 0) {
         AtomCursor o{open_t, open_g, 0};
@@ -1360,6 +1377,7 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
         W.a0 = worker_begin(P, worker);
         W.a1 = worker_begin(P, worker + 1);
         W.n = static_cast<int>(W.a1 - W.a0);
+        W.back = walks_back(worker);
         W.ring = smem_addr(smem) + static_cast<uint32_t>(rid * kStages * kSB);
     }
     // Weights stream while the previous grid on the stream (the prep launch,
