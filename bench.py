@@ -354,7 +354,7 @@ class Ctx:
 class Workload:
     """One config's device buffers, tasks and launch sequence on this rank."""
 
-    def __init__(self, C: Ctx, cfg: str, ncols: int, reps: int | None):
+    def __init__(self, C: Ctx, cfg: str, ncols: int, reps: int | None, pg=None):
         torch, q4k = C.torch, C.q4k
         self.C, self.cfg, self.ncols = C, cfg, ncols
         rank, world, dev = C.rank, C.world, C.dev
@@ -373,7 +373,16 @@ class Workload:
         self.fused = not self.q6 and any(glu for grp in self.groups for *_, glu in map(ent, grp))
         if (self.fused or self.q6) and world > 1:
             raise SystemExit(f"config {cfg} (fused epilogue / Q6_K) runs on one GPU")
-        self.pg = q4k.PeerGather(full_elems) if peer else None
+        # row-sharded runs share one gather buffer (allocated once per run)
+        self.pg = pg if peer else None
+        self.full_elems = full_elems
+        if peer:
+            if pg is None or pg.out.numel() < full_elems:
+                raise SystemExit("the gather buffer is smaller than this workload's outputs")
+            # every rank's buffer starts as NaN (no value left from an earlier
+            # workload can pass the parity check); all ranks fill before any launches
+            pg.out[:full_elems].fill_(float("nan"))
+            C.barrier()
         # Every step's activations live in one device buffer and its local
         # outputs in another, so that the end-to-end leg moves each with one copy.
         x_tot = sum(ncols * K for grp in self.groups for K in {a: K for _, _, K, a, _ in map(ent, grp)}.values())
@@ -514,6 +523,8 @@ class Workload:
         all-reduce MAX of zero-padded bytes); the oracle is the checker only."""
         C, torch, q4k = self.C, self.C.torch, self.C.q4k
         worst, bad, checked = 0.0, 0, 0
+        bad_by_owner = [0] * C.world
+        examples = []
         idx_groups = sorted({0, len(self.L) - 1})
         for gi in idx_groups:
             G = self.L[gi]
@@ -548,12 +559,26 @@ class Workload:
                         got[:, k] = part[:, lr].cpu().numpy()
                 err = np.abs(got - want)
                 tol = 1e-4 + 1e-5 * np.abs(want)
-                bad += int((err > tol).sum())
-                worst = max(worst, float((err / tol).max()))
+                nbad = err > tol  # NaN (never written) counts as bad
+                nbad |= ~np.isfinite(got)
+                bad += int(nbad.sum())
+                worst = max(worst, float(np.nanmax(np.where(np.isfinite(got), err / tol, np.inf))))
                 checked += err.size
+                for j, k in zip(*np.nonzero(nbad)):
+                    owner = int(sel[k] // e["per"])
+                    bad_by_owner[min(owner, C.world - 1)] += 1
+                    if len(examples) < 6:
+                        examples.append({"group": gi, "matrix": e["name"], "row": int(sel[k]), "col": int(j),
+                                         "owner": owner, "got": float(got[j, k]), "want": float(want[j, k])})
         ok = C.all_ok(bad == 0)
+        mine = {"rank": C.rank, "bad": bad, "bad_by_owner_rank": bad_by_owner, "worst_err_over_tol": worst,
+                "examples": examples}
+        ranks = [mine]
+        if C.world > 1:
+            ranks = [None] * C.world
+            C.dist.all_gather_object(ranks, mine)
         return {"parity": "ok" if ok else "fail", "values_checked_per_rank": checked,
-                "worst_err_over_tol": worst, "groups_checked": idx_groups,
+                "groups_checked": idx_groups, "ranks": ranks,
                 "bar": "1e-4 abs + 1e-5 rel vs the CPU oracle, 256 seeded rows per matrix"}
 
     # -- timing -------------------------------------------------------------------
@@ -627,9 +652,7 @@ class Workload:
         self.graph = None
         C.torch.cuda.synchronize(C.dev)
         C.barrier()
-        if self.pg is not None:
-            self.pg.close()
-            self.pg = None
+        self.pg = None  # (the run's gather buffer outlives the workload)
         self.L = []
         self.ws = None
         C.torch.cuda.empty_cache()
@@ -701,8 +724,21 @@ def main():
     if sampler:
         sampler.start()
 
+    # ---- one gather buffer for every row-sharded workload of the run ---------
+    todo = []
+    if not args.no_per_config and args.layers is None:
+        todo = [(cfg, nc) for cfg, nc in (PER_CONFIG_1GPU if world == 1 else PER_CONFIG_SHARDED)
+                if not (cfg == args.config and nc == args.ncols)]
+    pg = None
+    if C.peer:
+        def outs(cfg, nc, reps):
+            _, grps = build_groups(cfg, reps if reps is not None else WORKLOADS[cfg][2])
+            return sum(r * nc for grp in grps for _, r, _, _, _ in map(ent, grp))
+        pg = q4k.PeerGather(max([outs(args.config, args.ncols, args.layers)] +
+                                [outs(cfg, nc, None) for cfg, nc in todo]))
+
     # ---- headline ------------------------------------------------------------
-    W = Workload(C, args.config, args.ncols, args.layers)
+    W = Workload(C, args.config, args.ncols, args.layers, pg)
     with torch.cuda.stream(W.stream):
         W.run_step()  # one untimed step: checks the device status word before timing
     W.stream.synchronize()
@@ -727,7 +763,7 @@ def main():
     e2e = None
     if not args.no_e2e:
         xs_all = [W.x_all]
-        ys_all = [W.pg.out] if C.peer else [W.y_all]
+        ys_all = [W.pg.out[:W.full_elems]] if C.peer else [W.y_all]
         h_x = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in xs_all]
         for h, d in zip(h_x, xs_all):
             h.copy_(d)
@@ -778,14 +814,11 @@ def main():
 
     # ---- the other BASELINE configs ------------------------------------------
     per_config = {}
-    if not args.no_per_config and args.layers is None:
-        todo = PER_CONFIG_1GPU if world == 1 else PER_CONFIG_SHARDED
+    if todo:
         for cfg, nc in todo:
-            if cfg == args.config and nc == args.ncols:
-                continue
             key = f"{cfg}" if cfg != "3" else f"3/ncols={nc}"
             try:
-                Wc = Workload(C, cfg, nc, None)
+                Wc = Workload(C, cfg, nc, None, pg)
                 with torch.cuda.stream(Wc.stream):
                     Wc.run_step()
                 Wc.stream.synchronize()
@@ -860,6 +893,8 @@ def main():
     if world > 1:
         torch.cuda.synchronize(C.dev)
         dist.barrier()
+        if pg is not None:
+            pg.close()
         dist.destroy_process_group()
 
 

@@ -707,10 +707,16 @@ class PeerGather:
         dist.barrier()
 
     def close(self):
+        """Unmap the peers' buffers, wait until every rank has done the same
+        (collective), then free this rank's own buffers: no rank frees memory
+        that another still has mapped."""
+        import torch.distributed as dist
         L = lib()
         for p in self._opened:
             L.q4k_ipc_close(p)
         self._opened = []
+        if dist.is_initialized():
+            dist.barrier()
         for p in self._own:
             L.q4k_ipc_free(p)
         self._own = []
