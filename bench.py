@@ -588,17 +588,30 @@ class Workload:
         (serialising them) for the isolated-launch time.  Max over ranks."""
         C, torch, args = self.C, self.C.torch, self.C.args
         dev = C.dev
-        nsoak, t_soak = 0, time.perf_counter()
-        hs = t_soak
-        while time.perf_counter() - t_soak < soak_s and nsoak < 4000:
-            for _ in range(10):
-                self.replay()
-            nsoak += 10
+        hs = time.perf_counter()
+        if C.world == 1:
+            nsoak, t_soak = 0, hs
+            while time.perf_counter() - t_soak < soak_s and nsoak < 4000:
+                for _ in range(10):
+                    self.replay()
+                nsoak += 10
+                torch.cuda.synchronize(dev)
+        elif soak_s > 0:
+            # Every rank must replay exactly as many steps as the others: each
+            # gathering launch waits (bounded) for its peers' previous launch,
+            # so a rank that ran one step more would wait for launches that
+            # never come.  The count comes from one timed step, max over ranks.
+            C.barrier()
+            t0 = time.perf_counter()
+            self.replay()
             torch.cuda.synchronize(dev)
-        if C.world > 1:  # every rank replays the same number of soak steps
-            n = int(C.max_over_ranks([nsoak])[0])
-            for _ in range(n - nsoak):
+            t_one = C.max_over_ranks([time.perf_counter() - t0])[0]
+            n = int(min(4000, max(1, soak_s / max(t_one, 1e-6))))
+            for i in range(n):
                 self.replay()
+                if i % 10 == 9:
+                    torch.cuda.synchronize(dev)
+            torch.cuda.synchronize(dev)
         C.barrier()
         for _ in range(args.warmup):
             self.replay()
