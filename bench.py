@@ -376,13 +376,8 @@ class Workload:
         # row-sharded runs share one gather buffer (allocated once per run)
         self.pg = pg if peer else None
         self.full_elems = full_elems
-        if peer:
-            if pg is None or pg.out.numel() < full_elems:
-                raise SystemExit("the gather buffer is smaller than this workload's outputs")
-            # every rank's buffer starts as NaN (no value left from an earlier
-            # workload can pass the parity check); all ranks fill before any launches
-            pg.out[:full_elems].fill_(float("nan"))
-            C.barrier()
+        if peer and (pg is None or pg.out.numel() < full_elems):
+            raise SystemExit("the gather buffer is smaller than this workload's outputs")
         # Every step's activations live in one device buffer and its local
         # outputs in another, so that the end-to-end leg moves each with one copy.
         x_tot = sum(ncols * K for grp in self.groups for K in {a: K for _, _, K, a, _ in map(ent, grp)}.values())
@@ -455,6 +450,15 @@ class Workload:
                q4k.batch_workspace_bytes)
         self.ws = q4k.Workspace(max(wsb(G["tasks"], ncols) for G in self.L), dev)
         self.stream = torch.cuda.Stream(device=dev)
+        if peer:
+            # every rank's buffer starts as NaN, so that no value left from an
+            # earlier workload can pass the parity check
+            pg.out[:full_elems].fill_(float("nan"))
+        # The weights and activations were generated on the default stream; the
+        # launches run on self.stream: everything generated (and, row-sharded,
+        # every rank's fill) is complete before any launch.
+        torch.cuda.synchronize(dev)
+        C.barrier()
         self.graph = None
         self.use_graph = not C.args.no_graph
         self.single = C.args.path == "single"
@@ -700,15 +704,18 @@ def main():
     ap.add_argument("--no-per-config", action="store_true", help="measure the headline config only")
     ap.add_argument("--soak-s", type=float, default=0.8,
                     help="untimed replays before the warm-up, seconds (clock sampling window; 0 for profiling runs)")
-    ap.add_argument("--path", default="single", choices=["single", "two"],
+    ap.add_argument("--path", default="auto", choices=["auto", "single", "two"],
                     help="single: q4k_gemv_batch_persistent (one launch per group where the tasks allow it, "
-                         "else two); two: q4k_gemv_batch (quantization launch + GEMV launch)")
+                         "else two); two: q4k_gemv_batch (quantization launch + GEMV launch); auto (default): "
+                         "the one measured faster for the headline, two at one GPU, single row-sharded")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
         return
+    if args.path == "auto":
+        args.path = "two" if args.gpus == 1 else "single"
 
     import torch
     import torch.distributed as dist
