@@ -360,8 +360,9 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         }
         P.act_of_job[i] = found;
     }
-    // kernel variant: the epilogue one for a gate or bias; else, from kR2Min
-    // columns on, 64-row groups with two rows per lane
+    // kernel variant: the epilogue one for a gate or bias (a gated task's row
+    // groups run over its main matrix, then its gate matrix); else, from
+    // kR2Min columns on, 64-row groups with two rows per lane
     P.any_fused = false;
     for (int i = 0; i < njobs; ++i)
         if (P.act_of_job[i] >= 0 && (jobs[i].gate || jobs[i].x_bias)) P.any_fused = true;
@@ -373,14 +374,14 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.r2 = !P.q6 && !dump && !P.any_fused && ncols >= kR2Min && split_for(ncols) == 1;
     P.mode = dump ? kModeDump : P.any_fused ? kModeGated : P.q6 ? kModeQ6 : P.r2 ? kModeR2 : kModePlain;
     if (want_dyn && !dump && !P.q6) {
-        const bool gated = P.mode == kModeGated;
+        const bool gated = P.any_fused;
         const int R = rings_dyn(ncols, gated);
         int64_t G = 0, natoms = 0;
         bool fits = true;
         for (int i = 0; i < njobs; ++i) {
             if (P.act_of_job[i] < 0) continue;
             const int64_t nb = jobs[i].K / Q4K_QK_K;
-            const int64_t apr = (gated && jobs[i].gate) ? nb : (nb + kKS - 1) / kKS;
+            const int64_t apr = (jobs[i].gate ? 2 : 1) * ((nb + kKS - 1) / kKS);
             if (apr < R) fits = false;
             G += (jobs[i].nrows + 31) / 32;
             natoms += (jobs[i].nrows + 31) / 32 * apr;
@@ -422,9 +423,10 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         if (P.act_of_job[i] < 0) continue;
         const int64_t groups = (j.nrows + group_rows - 1) / group_rows;
         const int64_t nb = j.K / Q4K_QK_K;
-        // a gated or two-row atom is one super-block position (of both
-        // matrices / of 64 rows); a plain one kKS super-blocks of 32 rows
-        const int64_t apr = P.q6 ? nb / kQ6AtomSB : (j.gate || P.r2) ? nb : (nb + kKS - 1) / kKS;
+        // a two-row atom is one super-block of 64 rows, a plain one kKS
+        // super-blocks of 32 rows (a gated task: those of both matrices)
+        const int64_t half = (nb + kKS - 1) / kKS;
+        const int64_t apr = P.q6 ? nb / kQ6AtomSB : P.r2 ? nb : j.gate ? 2 * half : half;
         TaskDesc &T = P.gemv.task[nt++];
         T.W = static_cast<const uint8_t *>(j.W);
         T.dst = j.dst;
@@ -442,7 +444,7 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
         T.x_col_stride = j.src_col_stride;
         T.has_gate = j.gate ? 1 : 0;
         T.gate_map = j.gate ? ngated : -1;
-        T.pad2_ = 0;
+        T.half = j.gate ? static_cast<int32_t>(half) : 0;
         if (j.gate && ++ngated > kMaxGated)
             return fail(Q4K_EINVAL, "more than %d tasks with a fused gate in one launch", kMaxGated);
         T.glu_op = j.glu_op;
@@ -456,15 +458,26 @@ int make_plan(const Job *jobs, int njobs, int ncols, uint8_t *ws, int num_sms, P
     P.any_work = atoms > 0;
     P.gemv.ntasks = nt;
     P.gemv.natoms = atoms;
-    const int64_t max_workers = static_cast<int64_t>(num_sms) * rings_m(ncols, P.mode);
+    // Partition units: the CTAs (one per SM) in the balanced partition of
+    // the epilogue variant; single warps otherwise (CTA-contiguous ranges for
+    // large problems, consecutive workers on different SMs for small ones).
+    // The dynamic kernel hands out row groups instead.
+    // Every unit holds at least one atom (the count of a split row group's
+    // contributors is the span of their units); CTAs past nworkers idle.
+    const bool queue = is_queue(P.mode);
+    const int64_t max_workers = static_cast<int64_t>(num_sms) * (queue ? 1 : rings_m(ncols, P.mode));
     const int64_t nw = atoms < max_workers ? atoms : max_workers;
     P.gemv.nworkers = static_cast<int32_t>(nw);
-    P.gemv.packed = atoms >= 4 * max_workers ? 1 : 0;
+    P.gemv.packed = !queue && atoms >= 4 * max_workers ? 1 : 0;
     P.gemv.pad0_ = 0;
-    // the epilogue variant keeps gate partials, the two-row one the second row's
+    // partial slots hold the gate sums beside the main ones (a launch with a
+    // gate), or the second row's (two-row launches)
     P.gemv.pcols = (P.any_fused || P.r2) ? 2 * ncols : ncols;
     P.gemv.dyn_groups = dyn ? static_cast<int32_t>(rgs) : 0;
-    P.layout = make_layout(rgs, P.gemv.pcols, P.act_bytes, 2 * nw);
+    // two partial slots per unit; the dynamic kernel keeps its row groups
+    // inside one CTA and needs none (so the sizing plan, made for the static
+    // kernel with an upper bound on the SMs, covers whichever kernel runs)
+    P.layout = make_layout(rgs, P.gemv.pcols, P.act_bytes, dyn ? 0 : 2 * nw);
     // distinct activations: a task that reads each
     P.gemv.n_act = P.n_act;
     for (int a = 0; a < kMaxTasks; ++a) P.gemv.act_task[a] = -1;

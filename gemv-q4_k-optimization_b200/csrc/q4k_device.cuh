@@ -122,6 +122,23 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
+// Shared-memory words for hand-offs between the warps of a CTA.
+__device__ __forceinline__ int ld_acquire_cta_s32(uint32_t a) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_volatile_s32(uint32_t a) {
+    int v;
+    asm volatile("ld.volatile.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_cta_s32(uint32_t a, int v) {
+    asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_volatile_s32(uint32_t a, int v) {
+    asm volatile("st.volatile.shared::cta.b32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(

@@ -75,11 +75,13 @@ __host__ __device__ constexpr int smem_bytes(int ncols) { return rings_for(ncols
 static_assert(rings_for(8) >= 4, "ring too large for 8 columns");
 static_assert(warps_for(8) * 32 <= 1024, "block too large");
 
-// Kernel variants: plain, debug dump of the sub-block sums, fused epilogues.
-// kModeR2: plain tasks at ncols >= kR2Min, 64-row groups with two rows per
-// lane (one activation load serves both rows).  kModeQ6: Q6_K weights.
-// kModeDynPlain / kModeDynGated: the plain and gated arithmetic in the
-// dynamically scheduled kernel (k_gemv_dyn: whole row groups per CTA).
+// Kernel variants: plain, debug dump of the sub-block sums; kModeGated:
+// launches with a fused task (a bias or a gate: the epilogue code lives only
+// in this variant and kModeDynGated).  kModeR2: plain Q4_K tasks at ncols >=
+// kR2Min, 64-row groups with two rows per lane (one activation load serves
+// both rows).  kModeQ6: Q6_K weights.  kModeDynPlain / kModeDynGated: the
+// dynamically scheduled kernel (k_gemv_dyn: whole row groups per CTA),
+// without / with a fused task.
 // kModeActSmem: the plain arithmetic and partition in one launch: every CTA
 // quantizes the activations its atoms need straight into shared memory
 // (no separate quantization launch), ring stages carry weights only.
@@ -142,6 +144,53 @@ constexpr int kDynAhead = 3;
 __host__ __device__ constexpr bool is_dyn(int mode) {
     return mode == kModeDynPlain || mode == kModeDynGated;
 }
+// ---- balanced partition (k_gemv, launches with a fused task) -----------------
+// CTA c of G owns the contiguous atom range [natoms*c/G, natoms*(c+1)/G).  Its
+// R compute warps take the range's atoms in order from a shared-memory
+// counter, each through its own kStages-deep ring, and leave every atom's
+// sums (ncols floats per lane) in one of q_slots result slots; one more warp
+// folds the slots in atom order into the row groups' sums, and another
+// applies the epilogue and writes the rows.  Shared memory: the rings, the
+// slots, the group ring.
+constexpr int kQueueStatic = 2048;  // reserve for the kernel's static shared memory
+// (launches with a fused task; the others keep per-warp ranges: measured
+// faster in a chain of launches, where the next launch's CTAs already start
+// on the SMs that finish early)
+__host__ __device__ constexpr bool is_queue(int mode) { return mode == kModeGated; }
+__host__ __device__ constexpr int q_slot_bytes(int ncols, int /*mode*/) { return 32 * 4 * ncols; }
+// Result slots: as many as fit well (the fold may fall behind the compute
+// warps for a while without stalling them), at least two per compute warp.
+__host__ __device__ constexpr int q_slots(int ncols, int mode) {
+    return q_slot_bytes(ncols, mode) <= 128   ? 128
+           : q_slot_bytes(ncols, mode) <= 256 ? 64
+           : q_slot_bytes(ncols, mode) <= 512 ? 32
+                                              : 16;
+}
+// Row groups handed from the folding warp to the flushing warp (which
+// writes them out, or does the cross-CTA hand-off of a group shared with a
+// neighbouring CTA): a ring of kGroupRing entries of 2 * ncols floats per
+// lane (the main and the second sums).
+constexpr int kGroupRing = 4;
+__host__ __device__ constexpr int q_group_bytes(int ncols) { return kGroupRing * 2 * ncols * 128; }
+__host__ __device__ constexpr int q_aux_bytes(int ncols, int mode) {
+    return q_slots(ncols, mode) * q_slot_bytes(ncols, mode) + q_group_bytes(ncols);
+}
+// activation records per column in a ring stage: a two-row atom covers one
+// super-block, the others kKS (ring geometry of the static kernel's variants)
+__host__ __device__ constexpr int q_col_pitch(int mode) { return (mode == kModeR2 ? 1 : kKS) * kActSBBytes; }
+__host__ __device__ constexpr int round128(int b) { return (b + 127) / 128 * 128; }
+__host__ __device__ constexpr int q_stage_bytes(int ncols, int mode) {
+    return mode == kModeActSmem ? kWStageBytes : round128(kWStageBytes + ncols * q_col_pitch(mode));
+}
+__host__ __device__ constexpr int q_rings(int ncols, int mode) {
+    int r = kMaxWarps;
+    while (r > 1 && r * kStages * q_stage_bytes(ncols, mode) + (is_queue(mode) ? q_aux_bytes(ncols, mode) : 0) >
+                        kSmemLimit - kQueueStatic)
+        --r;
+    return r;
+}
+static_assert(q_rings(8, kModeR2) == kMaxWarps && q_rings(2, kModePlain) == kMaxWarps, "rings per CTA");
+static_assert(q_rings(8, kModeGated) >= 6, "epilogue variant: ring too small for 8 columns");
 // Single-launch mode: up to kActSmemMaxCols columns; shared memory beyond the
 // rings (8 warps x kStages x one weight stage) holds the CTA's activation
 // records, at most kActSmemCap bytes (the rest of the 227 KB, less a reserve
@@ -153,26 +202,26 @@ constexpr int kActSmemCap = kSmemLimit - kActSmemRings * kStages * kWStageBytes 
 constexpr int kMaxPlanCtas = 256;  // launches of more CTAs (SMs) run the two-launch sequence
 static_assert(kActSmemCap > 0, "no room for activations beside the rings");
 __host__ __device__ constexpr int stage_bytes_m(int ncols, int mode) {
-    return mode == kModeQ6 ? q6_stage_bytes(ncols) : mode == kModeActSmem ? kWStageBytes : stage_bytes(ncols);
+    return mode == kModeQ6 ? q6_stage_bytes(ncols) : is_dyn(mode) ? stage_bytes(ncols) : q_stage_bytes(ncols, mode);
 }
 __host__ __device__ constexpr int rings_m(int ncols, int mode) {
     return mode == kModeQ6         ? rings_q6(ncols)
            : is_dyn(mode)          ? rings_dyn(ncols, mode == kModeDynGated)
            : mode == kModeActSmem  ? kActSmemRings
-                                   : rings_for(ncols);
+                                   : q_rings(ncols, mode);
 }
+// threads per CTA / 32: the epilogue variant adds the folding and the flushing warp
 __host__ __device__ constexpr int warps_m(int ncols, int mode) {
-    return mode == kModeQ6         ? rings_q6(ncols)
-           : is_dyn(mode)          ? rings_dyn(ncols, mode == kModeDynGated)
-           : mode == kModeActSmem  ? kActSmemRings
-                                   : warps_for(ncols);
+    return rings_m(ncols, mode) + (is_queue(mode) ? 2 : 0);
 }
 // The single-launch mode keeps the plain kernel's partition (same rings per
 // CTA), so both paths give bit-identical results.
-static_assert(rings_for(1) == kActSmemRings && rings_for(2) == kActSmemRings && split_for(2) == 1,
+static_assert(q_rings(1, kModePlain) == kActSmemRings && q_rings(2, kModePlain) == kActSmemRings &&
+                  split_for(2) == 1,
               "single-launch partition differs from the two-launch one");
 __host__ __device__ constexpr int smem_m(int ncols, int mode) {
-    return rings_m(ncols, mode) * kStages * stage_bytes_m(ncols, mode);
+    return rings_m(ncols, mode) * kStages * stage_bytes_m(ncols, mode) +
+           (is_queue(mode) ? q_aux_bytes(ncols, mode) : 0);
 }
 
 // Device status codes (match q4k_status).
@@ -204,7 +253,7 @@ struct TaskDesc {
     int64_t atom_base;       // first global atom of this task
     int32_t nrows;
     int32_t nb;              // super-blocks per row
-    int32_t apr;             // atoms per row group = ceil(nb / kKS)
+    int32_t apr;             // atoms per row group: ceil(nb / kKS), twice that with a gate
     int32_t rg_base;         // global row-group index of row group 0
     int32_t ngroups;         // row groups = ceil(nrows / 32)
     int32_t act_id;          // index of this task's distinct activation
@@ -212,12 +261,16 @@ struct TaskDesc {
     const float *x;
     int64_t x_col_stride;    // floats between activation columns
     // Fused epilogue (kernels/mmvq.cu:182-227, :309-338): with a gate matrix
-    // (tensor map tmap_gate[gate_map]) an atom holds one super-block of each
-    // matrix (apr = nb) and the output is glu(W.x + x_bias, Wg.x + gate_bias).
+    // (tensor map tmap_gate[gate_map]) a row group runs over both matrices in
+    // turn: its first `half` atoms are the main matrix's, the next `half` the
+    // gate's (apr = 2 * half, half = ceil(nb / kKS)), summed apart, and the
+    // output is glu(W.x + x_bias, Wg.x + gate_bias).  Atoms stay the plain
+    // ones (32 rows x kKS super-blocks of one matrix), with the plain
+    // arithmetic.
     int32_t has_gate;
     int32_t glu_op;          // GluOp
     int32_t gate_map;
-    int32_t pad2_;
+    int32_t half;            // atoms per row group of each matrix (0 without a gate)
     const float *x_bias;     // per output row, or nullptr
     const float *gate_bias;  // per output row, or nullptr (only with a gate)
     int64_t bias_col_stride; // floats between bias columns (0: one column for all)
@@ -231,14 +284,15 @@ struct GemvParams {
     CUtensorMap tmap_gate[kMaxGated];   // gate matrices of the tasks with a fused gate
     TaskDesc task[kMaxTasks];
     int32_t ntasks;
-    int32_t nworkers;        // active workers (<= gridDim.x * rings_for(ncols), <= natoms)
-    int32_t packed;          // 1: worker = cta * rings + ring (CTA-contiguous ranges);
+    int32_t nworkers;        // partition units, each with >= 1 atom (<= natoms): CTAs
+                             // (<= gridDim.x, balanced partition) or warps (<= gridDim.x * rings)
+    int32_t packed;          // warps: 1: worker = cta * rings + ring (CTA-contiguous ranges);
                              // 0: worker = ring * gridDim.x + cta (small problems spread over SMs)
     int32_t pad0_;
     int64_t natoms;
     int32_t *counters;       // one per global row group, zero at kernel start
     float *partials;         // [nworkers][2][pcols][32]
-    int32_t pcols;           // columns per partial slot: ncols, or 2*ncols when a task has a gate
+    int32_t pcols;           // columns per partial slot: ncols, or 2*ncols (a task with a gate, two-row launches)
     int32_t dyn_groups;      // dynamically scheduled launches: row groups of all tasks
     int32_t *status;
     int32_t *dump_S;         // debug: sub-block sums (nullptr in the product path)

@@ -263,6 +263,20 @@ __device__ __forceinline__ AtomCursor locate_atom(const GemvParams &P, int64_t a
     return c;
 }
 
+// The same, searching from task t (a task near atom a: the previous one of a
+// monotonic walk).
+__device__ __forceinline__ AtomCursor locate_atom_from(const GemvParams &P, int64_t a, int t) {
+    while (t + 1 < P.ntasks && a >= P.task[t + 1].atom_base) ++t;
+    while (t > 0 && a < P.task[t].atom_base) --t;
+    const int local = static_cast<int>(a - P.task[t].atom_base);
+    const int apr = P.task[t].apr;
+    AtomCursor c;
+    c.t = t;
+    c.g = local / apr;
+    c.kp = local - c.g * apr;
+    return c;
+}
+
 __device__ __forceinline__ void advance(const GemvParams &P, AtomCursor &c) {
     if (++c.kp == P.task[c.t].apr) {
         c.kp = 0;
@@ -332,7 +346,6 @@ static_assert(sizeof(GemvParams) <= 32764, "kernel parameters exceed the 32 KB l
 template <int NC, int MODE>
 __device__ __forceinline__ void issue_weights(const GemvParams &P, const AtomCursor &c, uint32_t stage,
                                               uint32_t bar, int lane) {
-    constexpr bool GATED = MODE == kModeGated;
     const TaskDesc &T = P.task[c.t];
     if (lane == 0) {
 #if Q4K_WEIGHT_EVICT_FIRST
@@ -350,20 +363,17 @@ __device__ __forceinline__ void issue_weights(const GemvParams &P, const AtomCur
             mbar_expect_tx(bar, static_cast<uint32_t>(2 * kBoxBytes + NC * kActSBBytes));
             Q4K_TMA(stage, &P.tmap[c.t], c.kp * 36, c.g * 64, bar);
             Q4K_TMA(stage + kBoxBytes, &P.tmap[c.t], c.kp * 36, c.g * 64 + 32, bar);
-        } else if (GATED && T.has_gate) {
-            // one super-block position of both matrices: box 0 main, box 1 gate
-            static_assert(kKS >= 2, "a gated atom needs two boxes per stage");
-            mbar_expect_tx(bar, static_cast<uint32_t>(2 * kBoxBytes + NC * kActSBBytes));
-            Q4K_TMA(stage, &P.tmap[c.t], c.kp * 36, c.g * 32, bar);
-            Q4K_TMA(stage + kBoxBytes, &P.tmap_gate[T.gate_map], c.kp * 36, c.g * 32, bar);
         } else {
-            const int kb0 = c.kp * kKS;
+            // a gated task's second half of atoms reads the gate matrix
+            const bool second = MODE == kModeGated && T.has_gate && c.kp >= T.half;
+            const CUtensorMap *tm = second ? &P.tmap_gate[T.gate_map] : &P.tmap[c.t];
+            const int kb0 = (second ? c.kp - T.half : c.kp) * kKS;
             const int nsb = min(kKS, T.nb - kb0);
             // (the single-launch mode's stages carry weights only)
             mbar_expect_tx(bar, static_cast<uint32_t>(nsb * (kBoxBytes + (MODE == kModeActSmem ? 0 : NC * kActSBBytes))));
 #pragma unroll
             for (int i = 0; i < kKS; ++i)
-                if (i < nsb) Q4K_TMA(stage + i * kBoxBytes, &P.tmap[c.t], (kb0 + i) * 36, c.g * 32, bar);
+                if (i < nsb) Q4K_TMA(stage + i * kBoxBytes, tm, (kb0 + i) * 36, c.g * 32, bar);
         }
 #undef Q4K_TMA
     }
@@ -388,12 +398,14 @@ __device__ __forceinline__ void issue_acts(const GemvParams &P, const AtomCursor
         }
         return;
     }
-    const bool gated = MODE == kModeR2 || (MODE == kModeGated && T.has_gate);  // one record per atom
-    const int kb0 = gated ? c.kp : c.kp * kKS;
-    const int nsb = gated ? 1 : min(kKS, T.nb - kb0);
+    // a two-row atom is one super-block (one record); a gated task's second
+    // half of atoms reads the same records as its first
+    const int kq = (MODE == kModeGated && T.has_gate && c.kp >= T.half) ? c.kp - T.half : c.kp;
+    const int kb0 = MODE == kModeR2 ? kq : kq * kKS;
+    const int nsb = MODE == kModeR2 ? 1 : min(kKS, T.nb - kb0);
     if (lane < NC) {
         const uint8_t *src = T.act + lane * T.act_col_stride + static_cast<int64_t>(kb0) * kActSBBytes;
-        bulk_g2s(stage + Stage<NC, MODE>::kActOff + lane * (kKS * kActSBBytes), src,
+        bulk_g2s(stage + Stage<NC, MODE>::kActOff + lane * q_col_pitch(MODE), src,
                  static_cast<uint32_t>(nsb * kActSBBytes), bar);
     }
 }
@@ -405,6 +417,18 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, unsign
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+    }
+}
+
+// Bounded wait until the shared-memory word at a reaches want (written by
+// another warp of the CTA); backs off with nanosleep.  false after kWaitLimitNs.
+__device__ __forceinline__ bool wait_word_geq(uint32_t a, int want) {
+    if (ld_volatile_s32(a) >= want) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        __nanosleep(it < 16 ? 32 : 128);
+        if (ld_volatile_s32(a) >= want) return true;
+        if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
     }
 }
 
@@ -580,7 +604,7 @@ __device__ __forceinline__ void pair_dot2(uint32_t pA, uint32_t pB, uint32_t act
     const uint64_t magic2 = f2_pack(-kMagicF, -kMagicF);
 #pragma unroll
     for (int j = 0; j < NC; ++j) {
-        const uint32_t aj = act + j * (kKS * kActSBBytes);
+        const uint32_t aj = act + j * q_col_pitch(kModeR2);
         const uint4 qe0 = lds128(aj + 64 * c);
         const uint4 qe1 = lds128(aj + 64 * c + 16);
         const uint4 qo0 = lds128(aj + 64 * c + 32);
@@ -737,6 +761,11 @@ struct ActView {
     const int *task_off;
 };
 
+// One atom of the per-warp and dynamically scheduled kernels, added into the
+// lane's running row sums: Q6_K into dacc; two-row atoms row 64g + lane into
+// acc and 64g + 32 + lane into gacc; else per super-block into acc, or gacc
+// for a gated task's second half of atoms (the gate matrix).  Columns
+// [j0, j0 + NCW).
 template <int NCW, int NC, int MODE>
 __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCursor &c, uint32_t stage, int lane,
                                              int j0, RowAcc<NCW> &acc, RowAcc<NCW> &gacc, RowAccD<NCW> &dacc,
@@ -750,10 +779,10 @@ __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCurs
         q6_sb<NCW, false>(rowa + (2 * q) * kQ6Bytes, acts + (2 * q) * kQ6RecPitch, dacc);
         q6_sb<NCW, true>(rowa + (2 * q + 1) * kQ6Bytes, acts + (2 * q + 1) * kQ6RecPitch, dacc);
         return;
-    }
-    if constexpr (MODE == kModeR2) {
+    } else if constexpr (MODE == kModeR2) {
         // 64-row group: lane holds rows 64g + lane (box 0) and 64g + 32 + lane
-        // (box 1) of super-block c.kp; rows past the end are zero-filled.
+        // (box 1) of super-block c.kp, summed into acc and gacc; rows past
+        // the end are zero-filled by the copy
         uint64_t sbA[NCW], sbB[NCW];
 #pragma unroll
         for (int j = 0; j < NCW; ++j) sbA[j] = sbB[j] = 0ull;
@@ -761,61 +790,74 @@ __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCurs
                      sbB);
         add_sb(acc, sbA);
         add_sb(gacc, sbB);
-        return;
-    }
-    const int rows = min(32, T.nrows - c.g * 32);
-    if (lane >= rows) return;
-    constexpr bool DUMP = MODE == kModeDump;
-    constexpr bool ASM = MODE == kModeActSmem;
-    // records of the atom's super-blocks: in the ring stage (copied per atom),
-    // or in the CTA's activation table (single-launch mode)
-    const uint32_t acs = ASM ? static_cast<uint32_t>(T.nb) * kActSBBytes : kKS * kActSBBytes;
-    const uint32_t act = ASM ? AV.base + static_cast<uint32_t>(AV.task_off[c.t]) + j0 * acs +
-                                   static_cast<uint32_t>(c.kp * kKS) * kActSBBytes
-                             : stage + Stage<NC, MODE>::kActOff + j0 * acs;
-    if constexpr (MODE == kModeGated) {
-        if (T.has_gate) {
-            uint64_t sb[NCW];
-#pragma unroll
-            for (int j = 0; j < NCW; ++j) sb[j] = 0ull;
-            sb_dot<NCW, false>(stage + lane * kPitch, act, kKS * kActSBBytes, sb, nullptr, 0);
-            add_sb(acc, sb);
-#pragma unroll
-            for (int j = 0; j < NCW; ++j) sb[j] = 0ull;
-            sb_dot<NCW, false>(stage + kBoxBytes + lane * kPitch, act, kKS * kActSBBytes, sb, nullptr, 0);
-            add_sb(gacc, sb);
-            return;
-        }
-    }
-    const int kb0 = c.kp * kKS;
-    const int nsb = min(kKS, T.nb - kb0);
-    const int row = c.g * 32 + lane;
-#pragma unroll
-    for (int i = 0; i < kKS; ++i) {
-        if (i < nsb) {
-            int32_t *dS = nullptr;
-            int64_t dcs = 0;
-            if constexpr (DUMP) {
-                dcs = static_cast<int64_t>(T.nrows) * T.nb * 8;
-                dS = P.dump_S + j0 * dcs + static_cast<int64_t>(row) * T.nb * 8 + (kb0 + i) * 8;
+    } else {
+        constexpr bool DUMP = MODE == kModeDump;
+        constexpr bool ASM = MODE == kModeActSmem;
+        if constexpr (ASM) {
+            // the CTA's activation table must hold this task's activation (the
+            // host's bits follow the kernel's partition): never read at offset -1
+            if (AV.task_off[c.t] < 0) {
+                if (lane == 0) atomicExch(P.status, kStatusBadPlan);
+                return;
             }
-            uint64_t sb[NCW];
+        }
+        const int rows = min(32, T.nrows - c.g * 32);
+        if (lane >= rows) return;
+        // a gated task's second half of atoms (the dynamic kernel's launches
+        // with a fused task): the gate matrix, summed into gacc
+        const bool second = MODE == kModeGated && T.has_gate && c.kp >= T.half;
+        const int kb0 = (second ? c.kp - T.half : c.kp) * kKS;
+        // records of the atom's super-blocks: in the ring stage (copied per
+        // atom), or in the CTA's activation table (single-launch mode)
+        const uint32_t acs = ASM ? static_cast<uint32_t>(T.nb) * kActSBBytes : q_col_pitch(MODE);
+        const uint32_t act = ASM ? AV.base + static_cast<uint32_t>(AV.task_off[c.t]) + j0 * acs +
+                                       static_cast<uint32_t>(kb0) * kActSBBytes
+                                 : stage + Stage<NC, MODE>::kActOff + j0 * acs;
+        const int nsb = min(kKS, T.nb - kb0);
+        const int row = c.g * 32 + lane;
 #pragma unroll
-            for (int j = 0; j < NCW; ++j) sb[j] = 0ull;
-            sb_dot<NCW, DUMP>(stage + i * kBoxBytes + lane * kPitch, act + i * kActSBBytes, acs, sb, dS, dcs);
-            add_sb(acc, sb);
+        for (int i = 0; i < kKS; ++i) {
+            if (i < nsb) {
+                int32_t *dS = nullptr;
+                int64_t dcs = 0;
+                if constexpr (DUMP) {
+                    dcs = static_cast<int64_t>(T.nrows) * T.nb * 8;
+                    dS = P.dump_S + j0 * dcs + static_cast<int64_t>(row) * T.nb * 8 + (kb0 + i) * 8;
+                }
+                uint64_t sb[NCW];
+#pragma unroll
+                for (int j = 0; j < NCW; ++j) sb[j] = 0ull;
+                sb_dot<NCW, DUMP>(stage + i * kBoxBytes + lane * kPitch, act + i * kActSBBytes, acs, sb, dS, dcs);
+                if (second)
+                    add_sb(gacc, sb);
+                else
+                    add_sb(acc, sb);
+            }
         }
     }
 }
 
+// A task's output fields, read from the parameters once per row group.
+struct OutDesc {
+    float *dst;
+    int64_t dcs;             // floats between output columns
+    const float *xb, *gb;    // biases (or nullptr)
+    int64_t bcs;             // floats between bias columns
+    int has_gate, glu;
+    int gworld;
+};
+__device__ __forceinline__ OutDesc out_desc(const GemvParams &P, const TaskDesc &T) {
+    return OutDesc{T.dst, T.dst_col_stride, T.x_bias, T.gate_bias, T.bias_col_stride, T.has_gate, T.glu_op, P.gworld};
+}
+
 // Store one output value; with a fused all-gather also into every peer's
 // full output buffer (same offset, plain stores over NVLink).
-__device__ __forceinline__ void store_out(const GemvParams &P, const TaskDesc &T, int j, int row, float v) {
-    float *p = T.dst + j * T.dst_col_stride + row;
+__device__ __forceinline__ void store_out(const GemvParams &P, const OutDesc &O, int j, int row, float v) {
+    float *p = O.dst + j * O.dcs + row;
     *p = v;
-    if (P.gworld > 1) {
+    if (O.gworld > 1) {
         const int64_t off = p - P.gout_local;
-        for (int q = 0; q < P.gworld; ++q)
+        for (int q = 0; q < O.gworld; ++q)
             if (q != P.grank) P.gout_peer[q][off] = v;
     }
 }
@@ -825,7 +867,10 @@ __device__ __forceinline__ void store_out(const GemvParams &P, const TaskDesc &T
 // silu(g) = g / (1 + e^-g); GEGLU: times the tanh approximation of gelu(g);
 // SWIGLU_OAI: the clamped variant (alpha 1.702, limit 7) with the roles of
 // the reference's call (gate first); MUL: times g.
-__device__ __forceinline__ float glu_out(int op, float v, float g) {
+// Kept out of line: the GLU arithmetic (expf, tanhf) runs once per output
+// row of a gated task, and inlined into every kernel variant it grew the
+// code around the hot loops (measured: the two-row kernel 8 % slower).
+__device__ __noinline__ float glu_out(int op, float v, float g) {
     switch (op) {
         case kGluSwiglu:
             return v * (g / (1.0f + expf(-g)));
@@ -843,21 +888,23 @@ __device__ __forceinline__ float glu_out(int op, float v, float g) {
     }
 }
 
-// Final value of output (row, column j): biases and the gate epilogue applied
-// (launches with a fused task only; the plain kernel stores v as it is).
-template <bool GATED>
-__device__ __forceinline__ void store_final(const GemvParams &P, const TaskDesc &T, int j, int row, float v,
+// Final value of output (row, column j): v = W.x, g = Wg.x (a task with a
+// gate), with the task's biases and gate epilogue applied (EPI: the kernel
+// variants of launches with a fused task; the others store v as it is and
+// carry no epilogue code).
+template <bool EPI>
+__device__ __forceinline__ void store_final(const GemvParams &P, const OutDesc &O, int j, int row, float v,
                                             float g) {
-    if constexpr (!GATED) {
-        store_out(P, T, j, row, v);
+    if constexpr (!EPI) {
+        store_out(P, O, j, row, v);
         return;
     }
-    if (T.x_bias != nullptr) v += T.x_bias[j * T.bias_col_stride + row];
-    if (T.has_gate) {
-        if (T.gate_bias != nullptr) g += T.gate_bias[j * T.bias_col_stride + row];
-        v = glu_out(T.glu_op, v, g);
+    if (O.xb != nullptr) v += O.xb[j * O.bcs + row];
+    if (O.has_gate) {
+        if (O.gb != nullptr) g += O.gb[j * O.bcs + row];
+        v = glu_out(O.glu, v, g);
     }
-    store_out(P, T, j, row, v);
+    store_out(P, O, j, row, v);
 }
 
 // Finish a row group this warp worked on: write it out directly if the
@@ -869,53 +916,40 @@ __device__ __forceinline__ void store_final(const GemvParams &P, const TaskDesc 
 // ordering; otherwise a device-scope acquire-release counter in the workspace
 // is used.
 template <int NCW, int NC, int MODE>
-__device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCursor &cur, const RowAcc<NCW> &acc,
-                                            const RowAcc<NCW> &gacc, const RowAccD<NCW> &dacc, int64_t worker,
-                                            int64_t a0, int64_t a1,
-                                            int lane, int j0, int64_t cta_w0, int64_t cta_w1, int *cta_cnt) {
+__device__ __forceinline__ void flush_values(const GemvParams &P, const AtomCursor &cur, const float (&v)[NCW],
+                                             const float (&gv)[NCW], int64_t worker, int64_t a0, int64_t a1, int lane,
+                                             int j0, int64_t cta_w0, int64_t cta_w1, int *cta_cnt) {
     constexpr int kSplit = split_for(NC);
     constexpr bool DUMP = MODE == kModeDump;
-    constexpr bool GATED = MODE == kModeGated;
     constexpr bool R2 = MODE == kModeR2;
+    constexpr bool Q6 = MODE == kModeQ6;
+    constexpr bool EPI = MODE == kModeGated;  // launches with a fused task
     const TaskDesc &T = P.task[cur.t];
     // second set of sums: the gate (gated task) or row 64g + 32 + lane (two-row launch)
-    const bool gated = R2 || (GATED && T.has_gate);
-    constexpr bool Q6 = MODE == kModeQ6;
-    float v[NCW], gv[NCW];
-#pragma unroll
-    for (int j = 0; j < NCW; ++j) {
-        v[j] = acc.value(j);
-        gv[j] = (GATED || R2) ? gacc.value(j) : 0.0f;
-        if constexpr (Q6) {
-            // the four lanes of a row (lane & 7) hold two super-blocks each (fp64)
-            double t = dacc.s[j];
-            t += __shfl_xor_sync(0xffffffffu, t, 8);
-            t += __shfl_xor_sync(0xffffffffu, t, 16);
-            v[j] = static_cast<float>(t);
-        }
-    }
+    const bool gated = R2 || (EPI && T.has_gate);
     const int64_t sg = T.atom_base + static_cast<int64_t>(cur.g) * T.apr;
     const int64_t eg = sg + T.apr;
     const int row = cur.g * (R2 ? 64 : Q6 ? kQ6Rows : 32) + lane;
     const bool valid = row < T.nrows && (!Q6 || lane < kQ6Rows);
     const bool valid2 = R2 && row + 32 < T.nrows;
+    const OutDesc O = out_desc(P, T);
     if (sg >= a0 && eg <= a1) {
         if (!DUMP && valid) {
 #pragma unroll
-            for (int j = 0; j < NCW; ++j) store_final<GATED>(P, T, j0 + j, row, v[j], gv[j]);
+            for (int j = 0; j < NCW; ++j) store_final<EPI>(P, O, j0 + j, row, v[j], gv[j]);
         }
         if (valid2) {
 #pragma unroll
-            for (int j = 0; j < NCW; ++j) store_out(P, T, j0 + j, row + 32, gv[j]);
+            for (int j = 0; j < NCW; ++j) store_out(P, O, j0 + j, row + 32, gv[j]);
         }
         return;
     }
     // Partial slot: [pcols][32] floats, the main sums of the NC columns and,
     // for a gated task, the gate sums after them (two-row launch: the second
-    // row's sums).
+    // row's sums).  pcols: 2 * NC in launches with a gate or two rows per lane.
     const int slot = (a0 > sg) ? 0 : 1;  // 0: group began before this worker, 1: it covers the start
-    constexpr int kPC = (GATED || R2) ? 2 * NC : NC;  // floats per partial slot and lane (host pcols alike)
-    float *mine = P.partials + ((worker * 2 + slot) * kPC + j0) * 32;
+    const int64_t pc = P.pcols;
+    float *mine = P.partials + ((worker * 2 + slot) * pc + j0) * 32;
 #pragma unroll
     for (int j = 0; j < NCW; ++j) mine[j * 32 + lane] = v[j];
     if (gated) {
@@ -944,7 +978,7 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
 #pragma unroll
     for (int j = 0; j < NC; ++j) tot[j] = gtot[j] = 0.0f;
     for (int64_t w = w1; w <= w2; ++w) {
-        const float *src = P.partials + ((w * 2 + (w == w1 ? 1 : 0)) * kPC) * 32;
+        const float *src = P.partials + ((w * 2 + (w == w1 ? 1 : 0)) * pc) * 32;
 #pragma unroll
         for (int j = 0; j < NC; ++j) tot[j] += ldcg_f32(src + j * 32 + lane);
         if (gated) {
@@ -954,11 +988,11 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
     }
     if (!DUMP && valid) {
 #pragma unroll
-        for (int j = 0; j < NC; ++j) store_final<GATED>(P, T, j, row, tot[j], gtot[j]);
+        for (int j = 0; j < NC; ++j) store_final<EPI>(P, O, j, row, tot[j], gtot[j]);
     }
     if (valid2) {
 #pragma unroll
-        for (int j = 0; j < NC; ++j) store_out(P, T, j, row + 32, gtot[j]);
+        for (int j = 0; j < NC; ++j) store_out(P, O, j, row + 32, gtot[j]);
     }
     if (lane == 0) {
         if (local)
@@ -966,6 +1000,29 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
         else
             st_relaxed_gpu(&P.counters[T.rg_base + cur.g], 0);
     }
+}
+
+// The same from a warp's running sums (Q6_K: fp64, the four lanes of a row
+// -- lane & 7 -- holding two super-blocks each).
+template <int NCW, int NC, int MODE>
+__device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCursor &cur, const RowAcc<NCW> &acc,
+                                            const RowAcc<NCW> &gacc, const RowAccD<NCW> &dacc, int64_t worker,
+                                            int64_t a0, int64_t a1,
+                                            int lane, int j0, int64_t cta_w0, int64_t cta_w1, int *cta_cnt) {
+    constexpr bool Q6 = MODE == kModeQ6;
+    float v[NCW], gv[NCW];
+#pragma unroll
+    for (int j = 0; j < NCW; ++j) {
+        v[j] = acc.value(j);
+        gv[j] = Q6 ? 0.0f : gacc.value(j);
+        if constexpr (Q6) {
+            double t = dacc.s[j];
+            t += __shfl_xor_sync(0xffffffffu, t, 8);
+            t += __shfl_xor_sync(0xffffffffu, t, 16);
+            v[j] = static_cast<float>(t);
+        }
+    }
+    flush_values<NCW, NC, MODE>(P, cur, v, gv, worker, a0, a1, lane, j0, cta_w0, cta_w1, cta_cnt);
 }
 
 // Per-warp pipeline state of one worker.
@@ -1022,6 +1079,7 @@ __device__ __forceinline__ void warm_params(const GemvParams &P) {
         v = reinterpret_cast<uint64_t>(T.W) ^ static_cast<uint64_t>(T.atom_base) ^
             static_cast<uint64_t>(T.bias_col_stride) ^ static_cast<uint64_t>(T.apr);
         asm volatile("prefetch.tensormap [%0];" ::"l"(&P.tmap[t]) : "memory");
+        if (T.has_gate) asm volatile("prefetch.tensormap [%0];" ::"l"(&P.tmap_gate[T.gate_map]) : "memory");
     } else if (t == 32) {
         v = static_cast<uint64_t>(P.natoms) ^ static_cast<uint64_t>(P.nworkers) ^
             static_cast<uint64_t>(P.act_nb[0]) ^ static_cast<uint64_t>(P.cta_act_mask[blockIdx.x % kMaxPlanCtas]);
@@ -1056,7 +1114,7 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
     RowAcc<NCW> acc, gacc;
     RowAccD<NCW> dacc;  // Q6_K launches
     acc.clear();
-    if constexpr (MODE == kModeGated || MODE == kModeR2) gacc.clear();
+    if constexpr (MODE != kModeQ6) gacc.clear();
     if constexpr (MODE == kModeQ6) dacc.clear();
     AtomCursor cur = W.pro[0];
     int open_t = -1, open_g = -1;
@@ -1073,7 +1131,7 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
             open_t = cur.t;
             open_g = cur.g;
             acc.clear();
-            if constexpr (MODE == kModeGated || MODE == kModeR2) gacc.clear();
+            if constexpr (MODE != kModeQ6) gacc.clear();
             if constexpr (MODE == kModeQ6) dacc.clear();
         }
         bool ok = wait_phase(full[s], parity, kWaitLimitNs);
@@ -1322,8 +1380,12 @@ __device__ __forceinline__ void gather_epilogue(const GemvParams &P) {
     }
 }
 
+// Per-warp static partition (every launch without a fused task): worker w
+// (one warp) owns atoms [natoms * w / nworkers, natoms * (w + 1) / nworkers)
+// and streams them through its own ring; a row group split between workers
+// is added up by its last contributor (flush_group).
 template <int NC, int MODE>
-__global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
+__device__ __forceinline__ void gemv_per_warp(const GemvParams &P) {
     constexpr bool DUMP = MODE == kModeDump;
     constexpr int kR = rings_m(NC, MODE);
     constexpr int kSplit = split_for(NC);
@@ -1473,9 +1535,9 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
         // its quantization ended; else the worker's atom range
         o[6] = ASM ? tl_quant : active ? static_cast<unsigned long long>(W.a0) : 0ull;
         o[7] = ASM ? tl_plan : active ? static_cast<unsigned long long>(W.a1) : 0ull;
-        if (ASM && warp + 8 < 16) {
+        if (ASM && warp < 6) {
             // the phases of the quantization, in the record of warp + 8 (word 3
-            // stays 0: not a worker record)
+            // stays 0: not a worker record; records 14 and 15 stay free)
             unsigned long long *d = o + 8 * 8;
             d[0] = tl_d[0];
             d[1] = tl_d[1];
@@ -1485,6 +1547,490 @@ __global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid
     }
 #endif
     if (!DUMP && P.gworld > 1) gather_epilogue(P);
+}
+
+// ---- launches with a fused task: per-CTA atom queue, fold and flush warps ----
+// kModeGated (a task with a bias or a fused gate; a gated task's row group
+// runs over its main matrix, then its gate matrix).  CTA c of G owns the
+// contiguous atom range [natoms*c/G, natoms*(c+1)/G) (walk order below).  Its
+// R compute warps take the range's atoms one at a time, in walk order, from
+// a shared-memory counter, each streaming them through its own kStages-deep
+// ring, so the warps of a CTA finish within about one atom of each other.  A
+// compute warp leaves the sums of the k-th atom of the walk (NC floats per
+// lane) in result slot k % S (S = q_slots); warp R folds the slots in walk
+// order into the row groups' compensated sums (the gate's apart) and hands
+// each completed group to warp R + 1, which applies the biases and the gate
+// epilogue and writes the rows, or deposits the CTA's share of a group that
+// spans CTAs (added up by the last CTA to arrive, in CTA order).  The result
+// does not depend on which warp computed which atom, and the epilogue code
+// stays out of the compute warps' instruction stream (inlined into the
+// per-warp kernel it measured 2-8 % slower on every launch).
+//
+// Slot hand-off through shared-memory words (cheaper than mbarrier phases
+// here, where every atom takes one each way): tag[s] = k + 1 once slot s
+// holds atom k (stored with release by lane 0 of the writing warp, after the
+// warp's stores and a warp barrier; the folding warp reads the tags of up to
+// 32 slots at once with acquire loads), and fold_done = the atoms folded so
+// far (published by the folding warp once it has used the values it loaded).
+// Atom k is written once atom k - S has been folded; the warp that holds the
+// lowest atom not yet folded can always write it, so the fold always
+// advances.  Every wait is bounded (Q4K_ETIMEOUT in the status word) and
+// backs off with nanosleep, so that waiting warps leave the issue slots to
+// the others.
+
+// Sums of one atom per lane: NC floats (the lane's row, the atom's
+// super-blocks added in fp32).  Rows past the matrix end give 0.
+template <int NC, int MODE>
+__device__ __forceinline__ void atom_sums(const GemvParams &P, const AtomCursor &c, uint32_t stage, int lane,
+                                          float (&r)[NC]) {
+#pragma unroll
+    for (int q = 0; q < NC; ++q) r[q] = 0.0f;
+    const TaskDesc &T = P.task[c.t];
+    const int rows = min(32, T.nrows - c.g * 32);
+    if (lane >= rows) return;
+    // a gated task's second half of atoms: the gate matrix (folded apart)
+    const bool second = T.has_gate && c.kp >= T.half;
+    const int kb0 = (second ? c.kp - T.half : c.kp) * kKS;
+    const uint32_t act = stage + Stage<NC, MODE>::kActOff;
+    const int nsb = min(kKS, T.nb - kb0);
+#pragma unroll
+    for (int i = 0; i < kKS; ++i) {
+        if (i < nsb) {
+            uint64_t sb[NC];
+#pragma unroll
+            for (int j = 0; j < NC; ++j) sb[j] = 0ull;
+            sb_dot<NC, false>(stage + i * kBoxBytes + lane * kPitch, act + i * kActSBBytes, q_col_pitch(MODE), sb,
+                              nullptr, 0);
+#pragma unroll
+            for (int j = 0; j < NC; ++j) {
+                const float2 v = f2_unpack(sb[j]);
+                r[j] += v.x + v.y;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ float lds32f(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+    return v;
+}
+
+template <int NC, int MODE>
+__device__ __forceinline__ void gemv_queue(const GemvParams &P) {
+    static_assert(MODE == kModeGated, "the queue kernel serves the launches with a fused task");
+    constexpr int kR = rings_m(NC, MODE);  // compute warps; warp kR folds, warp kR + 1 flushes
+    constexpr int kSB = Stage<NC, MODE>::kBytes;
+    constexpr int kQ = NC;  // floats per lane and atom
+    constexpr int kSlotB = q_slot_bytes(NC, MODE);
+    constexpr int kS = q_slots(NC, MODE);
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full_bars[kR][kStages];
+    __shared__ int slot_tag[kS];
+    __shared__ int fold_done;
+    __shared__ int claim_next;
+    // group ring (fold -> flush): entry e % kGroupRing holds the e-th group
+    // of the walk once gr_tag == e + 1; gr_taken: groups flushed; gr_total:
+    // groups sent in all (-1 until the fold ends)
+    __shared__ int gr_tag[kGroupRing], gr_t[kGroupRing], gr_g[kGroupRing];
+    __shared__ int gr_taken, gr_total;
+
+#if Q4K_TIMELINE
+    const uint64_t tl_start = globaltimer_ns();
+#endif
+    // The next launch on the stream may start now; it waits for this grid's
+    // completion before it touches the workspace.
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const bool folder = warp == kR;
+    const bool flusher = warp == kR + 1;
+    const bool computes = warp < kR;
+    if (threadIdx.x < kR) {
+#pragma unroll
+        for (int s = 0; s < kStages; ++s) mbar_init(smem_addr(&full_bars[threadIdx.x][s]), 1);
+        mbar_fence_init();
+    } else if (folder) {
+        for (int i = lane; i < kS; i += 32) slot_tag[i] = 0;
+        if (lane < kGroupRing) gr_tag[lane] = 0;
+    }
+    if (threadIdx.x == 0) {
+        claim_next = 0;
+        fold_done = 0;
+        gr_taken = 0;
+        gr_total = -1;
+    }
+    __syncthreads();
+    // (CTAs past nworkers have no atoms: nworkers <= natoms keeps every
+    // unit of the partition non-empty)
+    const bool active = blockIdx.x < P.nworkers;
+    const int64_t A0 = active ? worker_begin(P, blockIdx.x) : 0;
+    const int64_t A1 = active ? worker_begin(P, blockIdx.x + 1) : 0;
+    const int n = static_cast<int>(A1 - A0);
+    // The walk, in three pieces: [A0, e1), the range's part of a row group
+    // that began in the previous CTA's range; [s2, A1), its part of a group
+    // that continues into the next CTA's range; then [e1, s2), the groups
+    // of its own.  Both contributors of a group shared by two CTAs reach it
+    // among their first atoms, so its cross-CTA hand-off overlaps the rest
+    // of the work (and both read the L2 lines they share at about the same
+    // time), and the walk ends on a group of its own where it has one.
+    int64_t e1 = A0, s2 = A1;
+    if (n > 0) {
+        const AtomCursor b = locate_atom(P, A0);
+        if (b.kp > 0) e1 = min(A1, A0 - b.kp + P.task[b.t].apr);
+        const AtomCursor e = locate_atom(P, A1 - 1);
+        const int64_t gs = A1 - 1 - e.kp;
+        if (e.kp + 1 < P.task[e.t].apr && gs >= e1) s2 = gs;
+    }
+    const int len1 = static_cast<int>(e1 - A0), len2 = static_cast<int>(A1 - s2);
+    const uint32_t ring = smem_addr(smem) + static_cast<uint32_t>((computes ? warp : 0) * kStages * kSB);
+    const uint32_t slots = smem_addr(smem) + static_cast<uint32_t>(kR * kStages * kSB);
+    const uint32_t fullb = smem_addr(&full_bars[computes ? warp : 0][0]);  // stage s: fullb + 8 s
+    // The k-th atom of this CTA's walk, and the next claim (-1: none left).
+    auto atom_of = [&](int k) -> int64_t {
+        return k < len1 ? A0 + k : k < len1 + len2 ? s2 + (k - len1) : e1 + (k - len1 - len2);
+    };
+    auto claim = [&]() -> int {
+        int k = 0;
+        if (lane == 0) k = atomicAdd(&claim_next, 1);
+        k = __shfl_sync(0xffffffffu, k, 0);
+        return k < n ? k : -1;
+    };
+    // Compute warps: the ring's stages in the order they are consumed
+    // (st[0] next); each holds an atom (k: its place in the walk, -1: none),
+    // its position, the parity of the stage's next copy and the stage index.
+    // Rotated after every atom, so the loop stays rolled and the state in
+    // registers.
+    struct StageSt {
+        int k;
+        AtomCursor c;
+        uint32_t par;
+        int s;
+    };
+    StageSt st[kStages];
+#pragma unroll
+    for (int j = 0; j < kStages; ++j) st[j] = StageSt{-1, AtomCursor{0, 0, 0}, 0u, j};
+    if (computes) {
+        // weights stream while the previous grid on the stream finishes
+#pragma unroll
+        for (int j = 0; j < kStages; ++j) {
+            st[j].k = claim();
+            if (st[j].k >= 0) {
+                st[j].c = locate_atom_from(P, atom_of(st[j].k), j > 0 ? st[j - 1].c.t : 0);
+                issue_weights<NC, MODE>(P, st[j].c, ring + j * kSB, fullb + 8 * j, lane);
+            }
+        }
+    }
+    pdl_wait();
+#if Q4K_TIMELINE
+    const uint64_t tl_wait = globaltimer_ns();
+#endif
+    if (computes) {
+        // activation records of the prologue atoms (written by the previous grid)
+#pragma unroll
+        for (int j = 0; j < kStages; ++j)
+            if (st[j].k >= 0) issue_acts<NC, MODE>(P, st[j].c, ring + j * kSB, fullb + 8 * j, lane);
+    }
+
+    // (wait results are made warp-uniform: the warp stays converged for its
+    // shuffles and its 32 arrivals)
+    bool ok = true;
+    int count = 0;  // atoms computed (compute warps) or folded (warp kR)
+#if Q4K_TIMELINE
+    // SM cycles: compute warps waiting for a free slot / for their copies;
+    // the folding warp waiting for a filled slot / writing row groups
+    long long tl_cy[2] = {0, 0};
+#endif
+    if (computes) {
+        // claims are monotonic: the first stage without an atom ends the walk
+        while (st[0].k >= 0) {
+            const int k = st[0].k;
+            const uint32_t stage = ring + static_cast<uint32_t>(st[0].s * kSB);
+            const uint32_t bar = fullb + 8u * static_cast<uint32_t>(st[0].s);
+#if Q4K_TIMELINE
+            const long long tw0 = clock64();
+#endif
+            ok = __all_sync(0xffffffffu, wait_phase(bar, st[0].par, kWaitLimitNs));
+#if Q4K_TIMELINE
+            tl_cy[1] += clock64() - tw0;
+#endif
+            if (!ok) break;
+            st[0].par ^= 1u;
+            float r[kQ];
+            atom_sums<NC, MODE>(P, st[0].c, stage, lane, r);
+            __syncwarp();
+            // refill the stage with the next atom of the walk
+            st[0].k = claim();
+            if (st[0].k >= 0) {
+                st[0].c = locate_atom_from(P, atom_of(st[0].k), st[kStages - 1].c.t);
+                fence_proxy_async_smem();
+                issue_weights<NC, MODE>(P, st[0].c, stage, bar, lane);
+                issue_acts<NC, MODE>(P, st[0].c, stage, bar, lane);
+            }
+            // hand the sums over: slot k % kS, once atom k - kS is folded
+            const int sl = k % kS;
+#if Q4K_TIMELINE
+            const long long tf0 = clock64();
+#endif
+            if (k >= kS) ok = __all_sync(0xffffffffu, wait_word_geq(smem_addr(&fold_done), k - kS + 1));
+#if Q4K_TIMELINE
+            tl_cy[0] += clock64() - tf0;
+#endif
+            if (!ok) break;
+            const uint32_t dst = slots + static_cast<uint32_t>(sl * kSlotB + lane * 4);
+#pragma unroll
+            for (int q = 0; q < kQ; ++q) sts32f(dst + q * 128, r[q]);
+            __syncwarp();
+            if (lane == 0) st_release_cta_s32(smem_addr(&slot_tag[sl]), k + 1);  // orders the warp's stores
+            ++count;
+            // the refilled stage is consumed after the others
+            const StageSt t = st[0];
+#pragma unroll
+            for (int j = 0; j + 1 < kStages; ++j) st[j] = st[j + 1];
+            st[kStages - 1] = t;
+        }
+        if (!ok) {
+            if (lane == 0) atomicExch(P.status, kStatusTimeout);
+            // let this warp's copies in flight land (bounded) before leaving
+#pragma unroll
+            for (int j = 0; j < kStages; ++j)
+                if (st[j].k >= 0) wait_phase(fullb + 8u * static_cast<uint32_t>(st[j].s), st[j].par, kDrainLimitNs);
+        }
+    } else if (folder && n > 0) {
+        // Fold in walk order, a row group at a time: the group's atoms of this
+        // walk as their slots fill -- every filled slot in a row from the next
+        // one (the tags of up to 32 slots read at once), their loads issued
+        // kBatch at a time, their sums still added atom by atom in walk order
+        // -- then the group is written out, or its share deposited.
+        constexpr int kBatch = kQ >= 16 ? 2 : kQ >= 4 ? 4 : 8;
+        constexpr int kLook = kS < 32 ? kS : 32;
+        RowAcc<NC> acc, gacc;
+        RowAccD<NC> dacc;  // (Q6_K only)
+        acc.clear();
+        gacc.clear();
+        const uint32_t tag0 = smem_addr(&slot_tag[0]);
+        const uint32_t grv = slots + static_cast<uint32_t>(kS * kSlotB);  // group ring values
+        int sent = 0;  // groups handed to the flushing warp
+        int k = 0;
+        uint64_t t0 = 0;
+        uint32_t idle = 0;
+        // the walk's pieces: [A0, e1), [s2, A1), [e1, s2) (empty ones skipped)
+        const int64_t pa[3] = {A0, s2, e1}, pb[3] = {e1, A1, s2};
+        int piece = 0;
+        while (piece < 2 && pa[piece] == pb[piece]) ++piece;
+        int64_t a = pa[piece], pend = pb[piece];
+        AtomCursor c = locate_atom(P, a);
+        while (k < n) {
+            if (a == pend) {
+                // the next non-empty piece
+                do {
+                    ++piece;
+                } while (piece < 2 && pa[piece] == pb[piece]);
+                a = pa[piece];
+                pend = pb[piece];
+                c = locate_atom(P, a);
+            }
+            const TaskDesc &T = P.task[c.t];
+            const int m = static_cast<int>(min(static_cast<int64_t>(T.apr - c.kp), pend - a));  // in this group
+            const int gate_from = T.has_gate ? T.half : 0x7fffffff;  // kp of the first gate atom
+            for (int i = 0; i < m;) {
+                const int k0 = k + i;
+                // how many slots from k0 on are filled, in a row
+#if Q4K_TIMELINE
+                const long long tw0 = clock64();
+#endif
+                int b = 0;
+                for (;;) {
+                    const int want = min(kLook, m - i);
+                    const bool rd = lane < want &&
+                                    ld_acquire_cta_s32(tag0 + 4u * static_cast<uint32_t>((k0 + lane) % kS)) == k0 + lane + 1;
+                    const uint32_t ball = __ballot_sync(0xffffffffu, rd);
+                    b = ball == 0xffffffffu ? 32 : __ffs(~ball) - 1;
+                    if (b > 0) break;
+                    if (idle == 0) t0 = globaltimer_ns();
+                    ++idle;
+                    __nanosleep(idle < 16 ? 32 : 128);
+                    if ((idle & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+                        ok = false;
+                        break;
+                    }
+                }
+#if Q4K_TIMELINE
+                tl_cy[0] += clock64() - tw0;
+#endif
+                if (!ok) break;
+                idle = 0;
+                // every lane's loads below come after every lane's acquire above
+                __syncwarp();
+                for (int i0 = 0; i0 < b; i0 += kBatch) {
+                    const int bb = min(kBatch, b - i0);
+                    float v[kBatch][kQ];
+#pragma unroll
+                    for (int bi = 0; bi < kBatch; ++bi) {
+                        if (bi < bb) {
+                            const uint32_t src =
+                                slots + static_cast<uint32_t>(((k0 + i0 + bi) % kS) * kSlotB + lane * 4);
+#pragma unroll
+                            for (int q = 0; q < kQ; ++q) v[bi][q] = lds32f(src + q * 128);
+                        }
+                    }
+#pragma unroll
+                    for (int bi = 0; bi < kBatch; ++bi) {
+                        if (bi < bb) {
+                            const int kp = c.kp + (i + i0 + bi);
+                            if (kp >= gate_from) {
+#pragma unroll
+                                for (int j = 0; j < NC; ++j) gacc.add(j, v[bi][j]);
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < NC; ++j) acc.add(j, v[bi][j]);
+                            }
+                        }
+                    }
+                }
+                // The values are in registers and used (every lane's loads
+                // have returned): the slots may be rewritten.
+                __syncwarp();
+                if (lane == 0) st_volatile_s32(smem_addr(&fold_done), k0 + b);
+                i += b;
+                count += b;
+            }
+            if (!ok) break;
+            // hand the group to the flushing warp (entry sent % kGroupRing,
+            // once group sent - kGroupRing has been flushed)
+#if Q4K_TIMELINE
+            const long long tg0 = clock64();
+#endif
+            if (sent >= kGroupRing)
+                ok = __all_sync(0xffffffffu, wait_word_geq(smem_addr(&gr_taken), sent - kGroupRing + 1));
+#if Q4K_TIMELINE
+            tl_cy[1] += clock64() - tg0;
+#endif
+            if (!ok) break;
+            {
+                const int e = sent % kGroupRing;
+                const uint32_t dst = grv + static_cast<uint32_t>(e * 2 * NC * 128 + lane * 4);
+#pragma unroll
+                for (int j = 0; j < NC; ++j) {
+                    sts32f(dst + j * 128, acc.value(j));
+                    sts32f(dst + (NC + j) * 128, gacc.value(j));
+                }
+                if (lane == 0) {
+                    gr_t[e] = c.t;
+                    gr_g[e] = c.g;
+                }
+                __syncwarp();
+                if (lane == 0) st_release_cta_s32(smem_addr(&gr_tag[e]), sent + 1);
+                ++sent;
+            }
+            (void)dacc;
+            acc.clear();
+            gacc.clear();
+            k += m;
+            a += m;
+            if (a < pend) {
+                // the first atom of the next group of the piece
+                c.kp = T.apr - 1;
+                advance(P, c);
+            }
+        }
+        if (!ok && lane == 0) atomicExch(P.status, kStatusTimeout);
+        __syncwarp();
+        if (lane == 0) st_release_cta_s32(smem_addr(&gr_total), sent);  // (also after a timeout)
+    } else if (folder) {
+        if (lane == 0) gr_total = 0;  // no atoms: no groups
+    } else if (flusher && n > 0) {
+        // Write out the groups in the order the fold sends them: stores of
+        // the rows (with biases and the gate epilogue), or this CTA's share
+        // of a group that spans CTAs (the last CTA to arrive adds the shares
+        // in CTA order, flush_values).
+        const uint32_t grv = slots + static_cast<uint32_t>(kS * kSlotB);
+        uint64_t t0 = 0;
+        uint32_t idle = 0;
+        for (int e = 0;; ++e) {
+            const int x = e % kGroupRing;
+#if Q4K_TIMELINE
+            const long long tw0 = clock64();
+#endif
+            bool have = false, done = false;
+            for (;;) {
+                have = __all_sync(0xffffffffu, ld_acquire_cta_s32(smem_addr(&gr_tag[x])) == e + 1);
+                if (have) break;
+                const int tot = ld_volatile_s32(smem_addr(&gr_total));
+                if (tot >= 0 && e >= tot) {
+                    done = true;
+                    break;
+                }
+                if (idle == 0) t0 = globaltimer_ns();
+                ++idle;
+                __nanosleep(idle < 16 ? 32 : 128);
+                if ((idle & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+                    ok = false;
+                    break;
+                }
+            }
+#if Q4K_TIMELINE
+            tl_cy[0] += clock64() - tw0;
+#endif
+            if (!ok) {
+                if (lane == 0) atomicExch(P.status, kStatusTimeout);
+                break;
+            }
+            if (done) break;
+            idle = 0;
+            __syncwarp();
+            const uint32_t src = grv + static_cast<uint32_t>(x * 2 * NC * 128 + lane * 4);
+            float v[NC], gv[NC];
+#pragma unroll
+            for (int j = 0; j < NC; ++j) {
+                v[j] = lds32f(src + j * 128);
+                gv[j] = lds32f(src + (NC + j) * 128);
+            }
+            const AtomCursor cur{ld_volatile_s32(smem_addr(&gr_t[x])), ld_volatile_s32(smem_addr(&gr_g[x])), 0};
+            // the entry is in registers: it may be rewritten
+            __syncwarp();
+            if (lane == 0) st_volatile_s32(smem_addr(&gr_taken), e + 1);
+#if Q4K_TIMELINE
+            const long long tg0 = clock64();
+#endif
+            flush_values<NC, NC, MODE>(P, cur, v, gv, blockIdx.x, A0, A1, lane, 0, blockIdx.x, blockIdx.x, nullptr);
+#if Q4K_TIMELINE
+            tl_cy[1] += clock64() - tg0;
+#endif
+            ++count;
+        }
+    }
+#if Q4K_TIMELINE
+    // records 0..kR-1: compute warps (word 3: atoms computed); record 15: the
+    // folding warp, record 14: the flushing warp (word 3 stays 0: not worker
+    // records; word 5: atoms folded / groups written)
+    const int rec = folder ? 15 : flusher ? 14 : warp;
+    if (lane == 0 && P.tl != nullptr && blockIdx.x < Q4K_TIMELINE_CTAS) {
+        unsigned long long *o =
+            P.tl + ((static_cast<int64_t>(P.tl_slot) * Q4K_TIMELINE_CTAS + blockIdx.x) * 16 + rec) * 8;
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        o[0] = tl_start;
+        o[1] = tl_wait;
+        o[2] = globaltimer_ns();
+        o[3] = computes ? static_cast<unsigned long long>(count) : 0ull;
+        o[4] = smid;
+        o[5] = computes ? static_cast<unsigned long long>(blockIdx.x) * 16 + static_cast<unsigned long long>(warp)
+                        : static_cast<unsigned long long>(count);
+        // the wait / hand-off / write cycles above
+        o[6] = static_cast<unsigned long long>(tl_cy[0]);
+        o[7] = static_cast<unsigned long long>(tl_cy[1]);
+    }
+#endif
+    if (P.gworld > 1) gather_epilogue(P);
+}
+
+template <int NC, int MODE>
+__global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
+    if constexpr (is_queue(MODE))
+        gemv_queue<NC, MODE>(P);
+    else
+        gemv_per_warp<NC, MODE>(P);
 }
 
 // ============================================================================
@@ -1712,6 +2258,7 @@ __global__ void __launch_bounds__(rings_dyn(NC, BASE == kModeGated) * 32, 1)
             __threadfence_block();
             __syncwarp();
             const TaskDesc &T = P.task[cc.c.t];
+            const OutDesc O = out_desc(P, T);
             const int row = cc.c.g * 32 + lane;
 #pragma unroll
             for (int j = 0; j < NC; ++j) {
@@ -1721,7 +2268,7 @@ __global__ void __launch_bounds__(rings_dyn(NC, BASE == kModeGated) * 32, 1)
                     tot += part[b][w][j][lane];
                     if constexpr (GATED) gtot += part[b][w][NC + j][lane];
                 }
-                if (row < T.nrows) store_final<GATED>(P, T, j, row, tot, gtot);
+                if (row < T.nrows) store_final<GATED>(P, O, j, row, tot, gtot);
             }
             __syncwarp();
             if (lane == 0) {

@@ -355,8 +355,8 @@ Q4K_API size_t q4k_noalloc_scratch_bytes(void);
  * q4k_last_error()) for tasks the call would reject.  No counterpart in the
  * reference, which has one kernel per ncols. */
 #define Q4K_KERNEL_STATIC 0          /* statically partitioned atom stream */
-#define Q4K_KERNEL_STATIC_GATED 2    /* the same with the bias / GLU epilogue */
-#define Q4K_KERNEL_STATIC_TWO_ROW 3  /* the same, two rows per lane (ncols >= 3) */
+#define Q4K_KERNEL_STATIC_GATED 2    /* launches with a bias / GLU epilogue: per-CTA atom queue */
+#define Q4K_KERNEL_STATIC_TWO_ROW 3  /* the static kernel, two rows per lane (ncols >= 3) */
 #define Q4K_KERNEL_DYNAMIC 5         /* whole row groups per CTA from a ticket queue */
 #define Q4K_KERNEL_DYNAMIC_GATED 6   /* the same with the bias / GLU epilogue */
 #define Q4K_KERNEL_SINGLE_LAUNCH 7   /* static partition, activations quantized in the GEMV launch */

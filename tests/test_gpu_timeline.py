@@ -34,6 +34,25 @@ def test_timeline_records_every_launch(q4k):
     assert len(d["ring_mean_end_us"]) >= 1 and len(d["cta_mean_end_us"]) >= 1
 
 
+def test_timeline_fused_launch_records(q4k):
+    """Launches with a fused gate/up task run the queue variant: besides the
+    compute warps' records, each CTA's flushing warp (which writes the rows)
+    leaves one, ending after most compute warps and within the launch."""
+    if not q4k.TIMELINE_LIB.exists():
+        pytest.skip("timeline library not built (make -C gemv-q4_k-optimization_b200 timeline)")
+    import os
+    script = Path(__file__).resolve().parent / "timeline_driver.py"
+    env = {**os.environ, "Q4K_LIB": str(q4k.TIMELINE_LIB)}
+    out = subprocess.run([sys.executable, str(script), "--config", "ffn", "--json"], capture_output=True,
+                         text=True, env=env, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads(out.stdout.strip().splitlines()[-1])
+    assert d["launches"] == 16
+    m = d["mean_us"]
+    assert 1.0 < m["period"] < 200.0
+    assert m["end_p10"] <= m["fold_end_max"] < m["period"] + 5
+
+
 def test_timeline_single_launch_records(q4k):
     """The same diagnostic over the single-launch mode: every launch planned
     and quantized its activations after its release and before its warps

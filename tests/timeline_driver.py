@@ -19,9 +19,10 @@ A diagnostic driver kept beside the test that checks its output
 
 The reference's own tracing was Nsight plus in-kernel clock64 probes left
 commented out (w_tile.cu:76-122); this is the same question asked of the
-persistent launch chain.  Plain Q4_K batches only (the quantization launch
-and k_gemv); numbers are from the timeline build, whose stamps cost a few
-stores per warp.
+persistent launch chain.  Q4_K batches (the quantization launch and
+k_gemv; groups with a fused gate/up entry through q4k_gemv_batch_ex);
+numbers are from the timeline build, whose stamps cost a few stores per
+warp.
 """
 from __future__ import annotations
 
@@ -40,24 +41,29 @@ sys.path.insert(0, str(ROOT))
 
 
 def build_step(q4k, bench, torch, cfg: str, ncols: int, reverse: bool, dev):
+    """The workload's launches; a group with a fused gate/up entry becomes a
+    q4k_gemv_batch_ex launch (fused=True)."""
     _, groups = bench.build_groups(cfg, bench.WORKLOADS[cfg][2])
-    if any(glu for grp in groups for *_, glu in map(bench.ent, grp)):
-        raise SystemExit(f"config {cfg}: plain Q4_K batches only")
+    if any(glu == "q6" for grp in groups for *_, glu in map(bench.ent, grp)):
+        raise SystemExit(f"config {cfg}: Q4_K batches only")
     if reverse:
         groups = [list(reversed(g)) for g in groups]
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     launches = []
     for grp in groups:
-        xs, Ws, xl, outs = {}, [], [], []
-        for _, rows, K, a, _ in map(bench.ent, grp):
+        xs, items = {}, []
+        for _, rows, K, a, glu in map(bench.ent, grp):
             if a not in xs:
                 xs[a] = torch.randn((ncols, K), device=dev, generator=g)
-            Ws.append(q4k.gen_q4k_torch(rows, K, generator=g, device=dev))
-            xl.append(xs[a])
-            outs.append(torch.empty((ncols, rows), device=dev))
-        launches.append(dict(tasks=q4k.make_tasks(Ws, xl, outs), keep=(Ws, xs, outs),
-                             names=[e[0] for e in grp]))
+            W = q4k.gen_q4k_torch(rows, K, generator=g, device=dev)
+            Wg = q4k.gen_q4k_torch(rows, K, generator=g, device=dev) if glu else None
+            items.append(dict(W=W, W_gate=Wg, x=xs[a], out=torch.empty((ncols, rows), device=dev),
+                              glu=glu or "none"))
+        fused = any(it["W_gate"] is not None for it in items)
+        tasks = (q4k.make_tasks_ex(items) if fused else
+                 q4k.make_tasks([it["W"] for it in items], [it["x"] for it in items], [it["out"] for it in items]))
+        launches.append(dict(tasks=tasks, fused=fused, keep=(items, xs), names=[e[0] for e in grp]))
     return launches
 
 
@@ -67,21 +73,31 @@ def summarize(G, Pr, n, single=False):
     6 and 7 of a warp's record hold its quantization end and plan time)."""
     per = []
     for i in range(n):
+        # worker records: word 3 (atoms computed) > 0; records 15 and 14 of a
+        # CTA are its folding and flushing warps (word 3 = 0); the flushing
+        # warp writes the last row groups
         cta, warp = np.nonzero(G[i][:, :, 3] > 0)
         w = G[i][cta, warp]
+        fold = G[i][:, 14]
+        fold = fold[(fold[:, 0] > 0) & (fold[:, 3] == 0)]
         p = Pr[i][Pr[i][:, 3] == 1]
         if len(w) == 0 or (len(p) == 0 and not single):
             raise SystemExit(f"launch {i}: no records (was the timeline library loaded?)")
         rel = w[:, 1].min()
-        d = dict(gemv_release=rel, gemv_end=w[:, 2].max(), ends=np.sort(w[:, 2] - rel) / 1e3,
-                 end=(w[:, 2] - rel) / 1e3, cta=cta, warp=warp, start_min=w[:, 0].min())
+        end_all = max(w[:, 2].max(), fold[:, 2].max()) if len(fold) else w[:, 2].max()
+        d = dict(gemv_release=rel, gemv_end=end_all, ends=np.sort(w[:, 2] - rel) / 1e3,
+                 end=(w[:, 2] - rel) / 1e3, cta=cta, warp=warp, start_min=w[:, 0].min(),
+                 fold_end=(fold[:, 2] - rel) / 1e3 if len(fold) else None)
         if single:
             d.update(quant=(w[:, 6] - w[:, 1]) / 1e3, plan=(w[:, 7] - w[:, 0]) / 1e3)
-            # phases in the records of warp + 8: plan barrier, status barrier, quantizer end
-            dd = G[i][cta, warp + 8] if warp.max() < 8 else None
-            if dd is not None and dd[:, 0].min() > 0:
-                d.update(ph_sync1=(dd[:, 0] - w[:, 1]) / 1e3, ph_sync2=(dd[:, 1] - dd[:, 0]) / 1e3,
-                         ph_quant=(dd[:, 2] - dd[:, 1]) / 1e3, ph_sync3=(w[:, 6] - dd[:, 2]) / 1e3)
+            # phases in the records of warp + 8 (warps 0..5): plan barrier,
+            # status barrier, quantizer end
+            m = warp < 6
+            dd = G[i][cta[m], warp[m] + 8]
+            if m.any() and dd[:, 0].min() > 0:
+                wm = w[m]
+                d.update(ph_sync1=(dd[:, 0] - wm[:, 1]) / 1e3, ph_sync2=(dd[:, 1] - dd[:, 0]) / 1e3,
+                         ph_quant=(dd[:, 2] - dd[:, 1]) / 1e3, ph_sync3=(wm[:, 6] - dd[:, 2]) / 1e3)
         else:
             d.update(prep_release=p[:, 1].min(), prep_end=p[:, 2].max())
         per.append(d)
@@ -103,6 +119,8 @@ def summarize(G, Pr, n, single=False):
                      prep_end_to_gemv_release=(b["gemv_release"] - b["prep_end"]) / 1e3)
         r.update(end_p10=float(np.percentile(b["ends"], 10)), end_p50=float(np.percentile(b["ends"], 50)),
                  end_p90=float(np.percentile(b["ends"], 90)), end_max=float(b["ends"][-1]))
+        if b["fold_end"] is not None:
+            r.update(fold_end_p50=float(np.percentile(b["fold_end"], 50)), fold_end_max=float(b["fold_end"].max()))
         rows.append(r)
     keys = [k for k in rows[0] if k != "launch"]
     mean = {k: float(np.mean([r[k] for r in rows])) for k in keys}
@@ -141,7 +159,10 @@ def main():
     launches = build_step(q4k, bench, torch, args.config, args.ncols, args.reverse, dev)
     if len(launches) > q4k.TL_SLOTS:
         raise SystemExit(f"{len(launches)} launches per step > {q4k.TL_SLOTS} timeline slots")
-    ws = q4k.Workspace(max(q4k.batch_workspace_bytes(L["tasks"], args.ncols) for L in launches), dev)
+    if args.single and any(L["fused"] for L in launches):
+        raise SystemExit("--single: plain Q4_K batches only")
+    ws = q4k.Workspace(max((q4k.batch_ex_workspace_bytes if L["fused"] else q4k.batch_workspace_bytes)(
+        L["tasks"], args.ncols) for L in launches), dev)
     stream = torch.cuda.Stream(device=dev)
 
     if args.single:
@@ -151,6 +172,8 @@ def main():
         for L in launches:
             if args.single:
                 q4k.gemv_batch_persistent(L["tasks"], args.ncols, ws, stream=stream)
+            elif L["fused"]:
+                q4k.gemv_batch_ex(L["tasks"], args.ncols, ws, stream=stream)
             else:
                 q4k.gemv_batch(L["tasks"], args.ncols, ws, stream=stream)
 
