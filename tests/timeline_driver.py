@@ -122,8 +122,10 @@ def summarize(G, Pr, n, single=False):
         if b["fold_end"] is not None:
             r.update(fold_end_p50=float(np.percentile(b["fold_end"], 50)), fold_end_max=float(b["fold_end"].max()))
         rows.append(r)
-    keys = [k for k in rows[0] if k != "launch"]
-    mean = {k: float(np.mean([r[k] for r in rows])) for k in keys}
+    # (launches of a mixed workload differ in their keys: the flushing warp's
+    # end exists for the launches with a fused task only)
+    keys = [k for k in dict.fromkeys(k for r in rows for k in r) if k != "launch"]
+    mean = {k: float(np.mean([r[k] for r in rows if k in r])) for k in keys}
     # worker end times by warp (ring slot of the CTA) and by CTA index, launches 1..n-1
     end = np.concatenate([r["end"] for r in per[1:]])
     warp = np.concatenate([r["warp"] for r in per[1:]])
@@ -201,9 +203,9 @@ def main():
         print(json.dumps(out))
         return
     print(f"config {args.config}, ncols {args.ncols}, {n} launches per step, graph replay; us")
-    print("launch  " + "  ".join(k for k in rows[0] if k != "launch"))
+    print("launch  " + "  ".join(keys))
     for r in rows:
-        print(f"{r['launch']:6d} " + "  ".join(f"{v:7.2f}" for k, v in r.items() if k != "launch"))
+        print(f"{r['launch']:6d} " + "  ".join(f"{r[k]:7.2f}" if k in r else "      -" for k in keys))
     print("mean   " + "  ".join(f"{k} {v:.2f}" for k, v in mean.items()))
     print("mean worker end by ring slot: " + "  ".join(f"{k}:{v:.2f}" for k, v in ring.items()))
     print("mean worker end by CTA index: " + "  ".join(f"{k}:{v:.2f}" for k, v in cta.items()))
