@@ -99,6 +99,21 @@ enum GemvMode : int {
 #define Q4K_R2_MIN 3
 #endif
 constexpr int kR2Min = Q4K_R2_MIN;
+// Two-row atoms of Q4K_R2_MMA_MIN or more columns take their integer sums
+// from int8 tensor-core MMAs (fewer columns: dp4a); each warp then needs a
+// 4 KB scratch after the rings.  Measured on B200 (Mistral layer): 8 columns
+// 20 % faster than dp4a, 4 columns 5 % slower (the MMA's 8 columns are half
+// padding there).
+#ifndef Q4K_R2_MMA
+#define Q4K_R2_MMA 1
+#endif
+#ifndef Q4K_R2_MMA_MIN
+#define Q4K_R2_MMA_MIN 6
+#endif
+constexpr int kR2MmaMin = Q4K_R2_MMA_MIN;
+__host__ __device__ constexpr int r2_scr_bytes(int ncols, int mode) {
+    return (Q4K_R2_MMA && mode == kModeR2 && ncols >= kR2MmaMin) ? kMaxWarps * 2 * 64 * 8 * 4 : 0;
+}
 
 // Q6_K (210-byte super-blocks: ql[128], qh[64], int8 scales[16], fp16 d).  A
 // 210-byte row chunk is never a multiple of 16 bytes, 8 super-blocks (1680 B)
@@ -182,9 +197,17 @@ __host__ __device__ constexpr int round128(int b) { return (b + 127) / 128 * 128
 __host__ __device__ constexpr int q_stage_bytes(int ncols, int mode) {
     return mode == kModeActSmem ? kWStageBytes : round128(kWStageBytes + ncols * q_col_pitch(mode));
 }
+// Plain and single-launch kernels: one more warp, the boundary warp, takes
+// the row groups a compute warp shares with another CTA (at most two per
+// warp: ncols floats per lane each, placed after the rings).
+__host__ __device__ constexpr bool has_xhelp(int mode) { return mode == kModePlain || mode == kModeActSmem; }
+__host__ __device__ constexpr int xh_bytes(int ncols, int mode) {
+    return has_xhelp(mode) ? kMaxWarps * 2 * ncols * 128 : 0;
+}
 __host__ __device__ constexpr int q_rings(int ncols, int mode) {
     int r = kMaxWarps;
-    while (r > 1 && r * kStages * q_stage_bytes(ncols, mode) + (is_queue(mode) ? q_aux_bytes(ncols, mode) : 0) >
+    while (r > 1 && r * kStages * q_stage_bytes(ncols, mode) + (is_queue(mode) ? q_aux_bytes(ncols, mode) : 0) +
+                            xh_bytes(ncols, mode) + r2_scr_bytes(ncols, mode) >
                         kSmemLimit - kQueueStatic)
         --r;
     return r;
@@ -192,13 +215,14 @@ __host__ __device__ constexpr int q_rings(int ncols, int mode) {
 static_assert(q_rings(8, kModeR2) == kMaxWarps && q_rings(2, kModePlain) == kMaxWarps, "rings per CTA");
 static_assert(q_rings(8, kModeGated) >= 6, "epilogue variant: ring too small for 8 columns");
 // Single-launch mode: up to kActSmemMaxCols columns; shared memory beyond the
-// rings (8 warps x kStages x one weight stage) holds the CTA's activation
-// records, at most kActSmemCap bytes (the rest of the 227 KB, less a reserve
-// for the kernel's static shared memory).
+// rings (8 warps x kStages x one weight stage) and the boundary warp's
+// entries holds the CTA's activation records, at most kActSmemCap bytes (the
+// rest of the 227 KB, less a reserve for the kernel's static shared memory).
 constexpr int kActSmemMaxCols = 2;
 constexpr int kActSmemRings = kMaxWarps;
 constexpr int kActSmemStatic = 2048;
-constexpr int kActSmemCap = kSmemLimit - kActSmemRings * kStages * kWStageBytes - kActSmemStatic;
+constexpr int kActSmemCap =
+    kSmemLimit - kActSmemRings * kStages * kWStageBytes - xh_bytes(kActSmemMaxCols, kModeActSmem) - kActSmemStatic;
 constexpr int kMaxPlanCtas = 256;  // launches of more CTAs (SMs) run the two-launch sequence
 static_assert(kActSmemCap > 0, "no room for activations beside the rings");
 __host__ __device__ constexpr int stage_bytes_m(int ncols, int mode) {
@@ -210,9 +234,10 @@ __host__ __device__ constexpr int rings_m(int ncols, int mode) {
            : mode == kModeActSmem  ? kActSmemRings
                                    : q_rings(ncols, mode);
 }
-// threads per CTA / 32: the epilogue variant adds the folding and the flushing warp
+// threads per CTA / 32: the epilogue variant adds the folding and the
+// flushing warp, the plain and single-launch kernels the boundary warp
 __host__ __device__ constexpr int warps_m(int ncols, int mode) {
-    return rings_m(ncols, mode) + (is_queue(mode) ? 2 : 0);
+    return rings_m(ncols, mode) + (is_queue(mode) ? 2 : has_xhelp(mode) ? 1 : 0);
 }
 // The single-launch mode keeps the plain kernel's partition (same rings per
 // CTA), so both paths give bit-identical results.
@@ -221,7 +246,7 @@ static_assert(q_rings(1, kModePlain) == kActSmemRings && q_rings(2, kModePlain) 
               "single-launch partition differs from the two-launch one");
 __host__ __device__ constexpr int smem_m(int ncols, int mode) {
     return rings_m(ncols, mode) * kStages * stage_bytes_m(ncols, mode) +
-           (is_queue(mode) ? q_aux_bytes(ncols, mode) : 0);
+           (is_queue(mode) ? q_aux_bytes(ncols, mode) : 0) + xh_bytes(ncols, mode) + r2_scr_bytes(ncols, mode);
 }
 
 // Device status codes (match q4k_status).

@@ -629,6 +629,110 @@ __device__ __forceinline__ void pair_dot2(uint32_t pA, uint32_t pB, uint32_t act
     }
 }
 
+#if Q4K_R2_MMA
+// ---- two-row atoms on the tensor cores (ncols >= kR2Min) ---------------------
+// The integer sub-block sums of a 64-row atom come from int8 MMAs instead of
+// dp4a: per sub-block pair c, for each 16-row tile of the atom,
+// D(16 x 8) = nibbles(16 x 32, u8) x q8(32 x 8 columns, s8), once for the
+// even sub-block (low nibbles) and once for the odd one (high nibbles).
+// Fragments (mma.m16n8k32, g = lane / 4, t = lane % 4): A words = 4 weight
+// bytes of rows g and g + 8 at k = 4t and 16 + 4t (the row's 32 qs bytes of
+// the pair); B words = 4 q8 values of column g at the same k; D = rows g and
+// g + 8, columns 2t and 2t + 1.  The exact integer sums go through a
+// per-warp scratch [2 sub-blocks][64 rows][8 columns] (int32, 16-byte
+// halves of a row swapped on rows 4-7 mod 8 so that neither the stores nor
+// the row reads conflict) and come back lane = row, where the float
+// combination is pair_dot2's, operation for operation (bit-identical sums).
+__device__ __forceinline__ void mma_u8s8(uint32_t (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void sts64u(uint32_t a, uint32_t x, uint32_t y) {
+    asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
+constexpr int kR2ScrBytes = 2 * 64 * 8 * 4;  // per warp
+static_assert(r2_scr_bytes(8, kModeR2) == kMaxWarps * kR2ScrBytes, "two-row scratch size");
+// byte address of (sub-block e, row r, column col) in a warp's scratch
+__device__ __forceinline__ uint32_t r2_scr(uint32_t scr, int e, int r, int col) {
+    return scr + static_cast<uint32_t>(((e * 64 + r) * 8 + (col ^ (((r >> 2) & 1) * 4))) * 4);
+}
+
+template <int NC>
+__device__ __forceinline__ void pair_dot2_mma(uint32_t box, uint32_t act, uint32_t scr, int lane, int c,
+                                              const SbHead &A, const SbHead &B, uint64_t (&accA)[NC],
+                                              uint64_t (&accB)[NC]) {
+    const int g = lane >> 2, t = lane & 3;
+    uint32_t bE0 = 0u, bE1 = 0u, bO0 = 0u, bO1 = 0u;  // columns >= NC stay zero
+    if (g < NC) {
+        const uint32_t aj = act + static_cast<uint32_t>(g * q_col_pitch(kModeR2) + 64 * c + 4 * t);
+        bE0 = lds32(aj);
+        bE1 = lds32(aj + 16);
+        bO0 = lds32(aj + 32);
+        bO1 = lds32(aj + 48);
+    }
+    __syncwarp();  // the previous pair's scratch reads are done
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t p = box + static_cast<uint32_t>((i >> 1) * kBoxBytes + (16 * (i & 1) + g) * kPitch + 16 +
+                                                       32 * c + 4 * t);
+        const uint32_t w0 = lds32(p), w1 = lds32(p + 8 * kPitch), w2 = lds32(p + 16), w3 = lds32(p + 8 * kPitch + 16);
+        const uint32_t aE[4] = {w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, w2 & 0x0F0F0F0Fu, w3 & 0x0F0F0F0Fu};
+        const uint32_t aO[4] = {(w0 >> 4) & 0x0F0F0F0Fu, (w1 >> 4) & 0x0F0F0F0Fu, (w2 >> 4) & 0x0F0F0F0Fu,
+                                (w3 >> 4) & 0x0F0F0F0Fu};
+        uint32_t dE[4], dO[4];
+        mma_u8s8(dE, aE, bE0, bE1);
+        mma_u8s8(dO, aO, bO0, bO1);
+        const int r = 16 * i + g;
+        sts64u(r2_scr(scr, 0, r, 2 * t), dE[0], dE[1]);
+        sts64u(r2_scr(scr, 0, r + 8, 2 * t), dE[2], dE[3]);
+        sts64u(r2_scr(scr, 1, r, 2 * t), dO[0], dO[1]);
+        sts64u(r2_scr(scr, 1, r + 8, 2 * t), dO[2], dO[3]);
+    }
+    __syncwarp();
+    // lane = row: rows lane (A) and 32 + lane (B), columns 0 .. NC-1
+    int eA[8], oA[8], eB[8], oB[8];
+#pragma unroll
+    for (int h = 0; h < (NC + 3) / 4; ++h) {
+        const uint4 v0 = lds128(r2_scr(scr, 0, lane, 4 * h)), v1 = lds128(r2_scr(scr, 1, lane, 4 * h));
+        const uint4 v2 = lds128(r2_scr(scr, 0, 32 + lane, 4 * h)), v3 = lds128(r2_scr(scr, 1, 32 + lane, 4 * h));
+        eA[4 * h] = v0.x; eA[4 * h + 1] = v0.y; eA[4 * h + 2] = v0.z; eA[4 * h + 3] = v0.w;
+        oA[4 * h] = v1.x; oA[4 * h + 1] = v1.y; oA[4 * h + 2] = v1.z; oA[4 * h + 3] = v1.w;
+        eB[4 * h] = v2.x; eB[4 * h + 1] = v2.y; eB[4 * h + 2] = v2.z; eB[4 * h + 3] = v2.w;
+        oB[4 * h] = v3.x; oB[4 * h + 1] = v3.y; oB[4 * h + 2] = v3.z; oB[4 * h + 3] = v3.w;
+    }
+    const int b0 = (c & 1) * 2;
+    const uint32_t scA = c < 2 ? A.sc03 : A.sc47, mA = c < 2 ? A.m03 : A.m47;
+    const uint32_t scB = c < 2 ? B.sc03 : B.sc47, mB = c < 2 ? B.m03 : B.m47;
+    const uint64_t dscA = f2_pack(fmaf(byte_magic(scA, b0), A.d, A.nd23), fmaf(byte_magic(scA, b0 + 1), A.d, A.nd23));
+    const uint64_t ndmA =
+        f2_pack(fmaf(byte_magic(mA, b0), -A.dmin, A.pm23), fmaf(byte_magic(mA, b0 + 1), -A.dmin, A.pm23));
+    const uint64_t dscB = f2_pack(fmaf(byte_magic(scB, b0), B.d, B.nd23), fmaf(byte_magic(scB, b0 + 1), B.d, B.nd23));
+    const uint64_t ndmB =
+        f2_pack(fmaf(byte_magic(mB, b0), -B.dmin, B.pm23), fmaf(byte_magic(mB, b0 + 1), -B.dmin, B.pm23));
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+        const uint4 meta = lds128(act + j * q_col_pitch(kModeR2) + kActMetaOff + 16 * c);
+        const uint64_t f = f2_pack(__uint_as_float(meta.x), __uint_as_float(meta.y));
+        const uint64_t a = f2_pack(__uint_as_float(meta.z), __uint_as_float(meta.w));
+        // the odd sum as pair_dot2 forms it (on 16 x nibble): exact in fp32
+        const uint64_t gA = f2_mul(f2_pack(static_cast<float>(eA[j]), static_cast<float>(oA[j] * 16)), f);
+        const uint64_t gB = f2_mul(f2_pack(static_cast<float>(eB[j]), static_cast<float>(oB[j] * 16)), f);
+        accA[j] = f2_fma(a, ndmA, f2_fma(gA, dscA, accA[j]));
+        accB[j] = f2_fma(a, ndmB, f2_fma(gB, dscB, accB[j]));
+    }
+}
+
+template <int NC>
+__device__ __forceinline__ void sb_dot2_mma(uint32_t box, uint32_t act, uint32_t scr, int lane,
+                                            uint64_t (&accA)[NC], uint64_t (&accB)[NC]) {
+    const SbHead A = sb_head(box + lane * kPitch), B = sb_head(box + kBoxBytes + lane * kPitch);
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) pair_dot2_mma<NC>(box, act, scr, lane, c, A, B, accA, accB);
+}
+#endif
+
 // One super-block of two rows (weights at pA and pB) against NC activation
 // records: sb_dot for both, with the activation loads shared.
 template <int NC>
@@ -786,8 +890,17 @@ __device__ __forceinline__ void compute_atom(const GemvParams &P, const AtomCurs
         uint64_t sbA[NCW], sbB[NCW];
 #pragma unroll
         for (int j = 0; j < NCW; ++j) sbA[j] = sbB[j] = 0ull;
-        sb_dot2<NCW>(stage + lane * kPitch, stage + kBoxBytes + lane * kPitch, stage + Stage<NC, MODE>::kActOff, sbA,
-                     sbB);
+#if Q4K_R2_MMA
+        if constexpr (NC >= kR2MmaMin) {
+            // (the warp's scratch follows the rings: one per ring, ring = warp)
+            sb_dot2_mma<NCW>(stage, stage + Stage<NC, MODE>::kActOff,
+                             AV.base + static_cast<uint32_t>((threadIdx.x >> 5) * kR2ScrBytes), lane, sbA, sbB);
+        } else
+#endif
+        {
+            sb_dot2<NCW>(stage + lane * kPitch, stage + kBoxBytes + lane * kPitch, stage + Stage<NC, MODE>::kActOff,
+                         sbA, sbB);
+        }
         add_sb(acc, sbA);
         add_sb(gacc, sbB);
     } else {
@@ -915,10 +1028,27 @@ __device__ __forceinline__ void store_final(const GemvParams &P, const OutDesc &
 // belong to this CTA count arrivals in shared memory under block-scope
 // ordering; otherwise a device-scope acquire-release counter in the workspace
 // is used.
+// Row groups split with another CTA (plain and single-launch kernels): the
+// device-scope arrival (and, for the last contributor, the sum) stalls the
+// warp ~1-2 us, so a compute warp hands them to the CTA's boundary warp
+// instead.  A worker has at most two split groups (the one it began inside,
+// slot 0, and the one it ends inside, slot 1): one entry each per compute
+// warp -- the NC main sums per lane in shared memory, the group's task and
+// row group -- announced by the arrival of all 32 lanes on the entry's
+// mbarrier (block-scope release).  The boundary warp knows from the workers'
+// atom ranges which entries will come and waits for each on its mbarrier.
+struct XHelp {
+    uint32_t vals;  // [kR][2][NC][32] floats
+    uint32_t bar;   // uint64 [kR][2]: one mbarrier per entry (32 arrivals)
+    uint32_t tg;    // int [kR][2][2]: task, row group
+    int w;          // this compute warp's ring
+};
+
 template <int NCW, int NC, int MODE>
 __device__ __forceinline__ void flush_values(const GemvParams &P, const AtomCursor &cur, const float (&v)[NCW],
                                              const float (&gv)[NCW], int64_t worker, int64_t a0, int64_t a1, int lane,
-                                             int j0, int64_t cta_w0, int64_t cta_w1, int *cta_cnt) {
+                                             int j0, int64_t cta_w0, int64_t cta_w1, int *cta_cnt,
+                                             const XHelp *xh = nullptr) {
     constexpr int kSplit = split_for(NC);
     constexpr bool DUMP = MODE == kModeDump;
     constexpr bool R2 = MODE == kModeR2;
@@ -948,6 +1078,21 @@ __device__ __forceinline__ void flush_values(const GemvParams &P, const AtomCurs
     // for a gated task, the gate sums after them (two-row launch: the second
     // row's sums).  pcols: 2 * NC in launches with a gate or two rows per lane.
     const int slot = (a0 > sg) ? 0 : 1;  // 0: group began before this worker, 1: it covers the start
+    const int64_t w1 = worker_of(P, sg), w2 = worker_of(P, eg - 1);
+    const bool local = P.packed && w1 >= cta_w0 && w2 <= cta_w1;
+    if (xh != nullptr && !local) {
+        // to the boundary warp (it deposits, arrives and, if last, adds up)
+        const uint32_t dst = xh->vals + static_cast<uint32_t>(((xh->w * 2 + slot) * NCW) * 128 + lane * 4);
+#pragma unroll
+        for (int j = 0; j < NCW; ++j) sts32f(dst + j * 128, v[j]);
+        if (lane == 0) {
+            st_volatile_s32(xh->tg + static_cast<uint32_t>((xh->w * 2 + slot) * 8), cur.t);
+            st_volatile_s32(xh->tg + static_cast<uint32_t>((xh->w * 2 + slot) * 8 + 4), cur.g);
+        }
+        __syncwarp();
+        mbar_arrive(xh->bar + static_cast<uint32_t>((xh->w * 2 + slot) * 8));
+        return;
+    }
     const int64_t pc = P.pcols;
     float *mine = P.partials + ((worker * 2 + slot) * pc + j0) * 32;
 #pragma unroll
@@ -956,9 +1101,7 @@ __device__ __forceinline__ void flush_values(const GemvParams &P, const AtomCurs
 #pragma unroll
         for (int j = 0; j < NCW; ++j) mine[(NC + j) * 32 + lane] = gv[j];
     }
-    const int64_t w1 = worker_of(P, sg), w2 = worker_of(P, eg - 1);
     const int last = kSplit * static_cast<int>(w2 - w1 + 1) - 1;
-    const bool local = P.packed && w1 >= cta_w0 && w2 <= cta_w1;
     int old = 0;
     if (local) {
         __threadfence_block();
@@ -1008,7 +1151,8 @@ template <int NCW, int NC, int MODE>
 __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCursor &cur, const RowAcc<NCW> &acc,
                                             const RowAcc<NCW> &gacc, const RowAccD<NCW> &dacc, int64_t worker,
                                             int64_t a0, int64_t a1,
-                                            int lane, int j0, int64_t cta_w0, int64_t cta_w1, int *cta_cnt) {
+                                            int lane, int j0, int64_t cta_w0, int64_t cta_w1, int *cta_cnt,
+                                            const XHelp *xh = nullptr) {
     constexpr bool Q6 = MODE == kModeQ6;
     float v[NCW], gv[NCW];
 #pragma unroll
@@ -1022,7 +1166,7 @@ __device__ __forceinline__ void flush_group(const GemvParams &P, const AtomCurso
             v[j] = static_cast<float>(t);
         }
     }
-    flush_values<NCW, NC, MODE>(P, cur, v, gv, worker, a0, a1, lane, j0, cta_w0, cta_w1, cta_cnt);
+    flush_values<NCW, NC, MODE>(P, cur, v, gv, worker, a0, a1, lane, j0, cta_w0, cta_w1, cta_cnt, xh);
 }
 
 // Per-warp pipeline state of one worker.
@@ -1097,7 +1241,7 @@ template <int NC, int NCW, int MODE>
 __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, int64_t worker, int lane, int j0,
                                             bool issuer, const uint32_t (&full)[kStages],
                                             const uint32_t (&empty)[kStages], int64_t cta_w0, int64_t cta_w1,
-                                            int *cta_cnt, const ActView &AV) {
+                                            int *cta_cnt, const ActView &AV, const XHelp *xh) {
     constexpr int kSB = Stage<NC, MODE>::kBytes;
     constexpr bool kShared = split_for(NC) > 1;
     const int n = W.n;
@@ -1126,7 +1270,7 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
             if (open_t >= 0) {
                 AtomCursor o{open_t, open_g, 0};
                 flush_group<NCW, NC, MODE>(P, o, acc, gacc, dacc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1,
-                                           cta_cnt);
+                                           cta_cnt, xh);
             }
             open_t = cur.t;
             open_g = cur.g;
@@ -1166,9 +1310,11 @@ __device__ __forceinline__ void worker_main(const GemvParams &P, WorkerPipe &W, 
         if (i + 1 < n) step(P, cur, W.back);
     }
     if (open_t >= 0) {
+        // the last group: this warp is done, so it does its own hand-off
+        // (handing it over would only serialise it behind the boundary warp)
         AtomCursor o{open_t, open_g, 0};
         flush_group<NCW, NC, MODE>(P, o, acc, gacc, dacc, worker, W.a0, W.a1, lane, j0, cta_w0, cta_w1,
-                                   cta_cnt);
+                                   cta_cnt, nullptr);
     }
 }
 
@@ -1238,9 +1384,6 @@ __device__ __forceinline__ void ldg_cg_f8(const float *p, float (&v)[8]) {
 }
 __device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
     asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
-}
-__device__ __forceinline__ void sts32f(uint32_t a, float v) {
-    asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
 }
 
 // One half of a q8_1 block per lane: lanes 2i and 2i+1 take values [0, 16)
@@ -1398,6 +1541,14 @@ __device__ __forceinline__ void gemv_per_warp(const GemvParams &P) {
     constexpr bool ASM = MODE == kModeActSmem;
     __shared__ ActPlan act_plan[1];  // single-launch mode only
     __shared__ int plan_ok;
+    // plain and single-launch kernels: warp kR is the boundary warp (row
+    // groups split with another CTA, XHelp); its entries' values follow the
+    // rings in dynamic shared memory
+    constexpr bool XH = has_xhelp(MODE);
+    static_assert(!XH || kSplit == 1, "boundary-warp entries are per ring: one warp per ring");
+    constexpr int kXH = XH ? kR : 1;
+    __shared__ int xh_tg[kXH][2][2];
+    __shared__ __align__(8) uint64_t xh_bar[kXH][2];
 
 #if Q4K_TIMELINE
     const uint64_t tl_start = globaltimer_ns();
@@ -1412,6 +1563,10 @@ __device__ __forceinline__ void gemv_per_warp(const GemvParams &P) {
     const int half = warp - rid * kSplit;    // 0: issuer, columns [0, kNC0); 1: columns [kNC0, NC)
     if (threadIdx.x < kR) {
         cta_cnt[threadIdx.x] = 0;
+        if constexpr (XH) {
+            mbar_init(smem_addr(&xh_bar[threadIdx.x][0]), 32);
+            mbar_init(smem_addr(&xh_bar[threadIdx.x][1]), 32);
+        }
 #pragma unroll
         for (int s = 0; s < kStages; ++s) {
             mbar_init(smem_addr(&full_bars[threadIdx.x][s]), 1);
@@ -1426,13 +1581,13 @@ __device__ __forceinline__ void gemv_per_warp(const GemvParams &P) {
                                     : static_cast<int64_t>(rid) * gridDim.x + blockIdx.x;
     const int64_t cta_w0 = static_cast<int64_t>(blockIdx.x) * kR;
     const int64_t cta_w1 = cta_w0 + kR - 1;
-    const bool active = worker < P.nworkers;
+    const bool active = rid < kR && worker < P.nworkers;  // (warp kR: the boundary warp)
     const bool issuer = half == 0;
     uint32_t full[kStages], empty[kStages];
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
-        full[s] = smem_addr(&full_bars[rid][s]);
-        empty[s] = smem_addr(&empty_bars[rid][s]);
+        full[s] = smem_addr(&full_bars[rid < kR ? rid : 0][s]);
+        empty[s] = smem_addr(&empty_bars[rid < kR ? rid : 0][s]);
     }
     WorkerPipe W;
     if (active) {
@@ -1473,7 +1628,9 @@ __device__ __forceinline__ void gemv_per_warp(const GemvParams &P) {
 #if Q4K_TIMELINE
     const uint64_t tl_wait = globaltimer_ns();
 #endif
-    const ActView AV{smem_addr(smem) + static_cast<uint32_t>(kR * kStages * kSB), ASM ? act_plan[0].task_off : nullptr};
+    const uint32_t xh_vals = smem_addr(smem) + static_cast<uint32_t>(kR * kStages * kSB);
+    // (the single-launch activation table follows the boundary warp's entries)
+    const ActView AV{xh_vals + static_cast<uint32_t>(xh_bytes(NC, MODE)), ASM ? act_plan[0].task_off : nullptr};
 #if Q4K_TIMELINE
     uint64_t tl_d[3] = {0, 0, 0};  // single-launch mode: after the plan barrier, before / after quantizing
 #endif
@@ -1511,18 +1668,86 @@ __device__ __forceinline__ void gemv_per_warp(const GemvParams &P) {
 #if Q4K_TIMELINE
     const uint64_t tl_quant = globaltimer_ns();
 #endif
+    const XHelp xh{xh_vals, smem_addr(&xh_bar[0][0]), smem_addr(&xh_tg[0][0][0]), rid};
     if (active) {
         if (issuer) {
-            worker_main<NC, kNC0, MODE>(P, W, worker, lane, 0, true, full, empty, cta_w0, cta_w1, cta_cnt, AV);
+            worker_main<NC, kNC0, MODE>(P, W, worker, lane, 0, true, full, empty, cta_w0, cta_w1, cta_cnt, AV,
+                                        XH ? &xh : nullptr);
         } else if constexpr (kSplit > 1) {
             worker_main<NC, NC - kNC0, MODE>(P, W, worker, lane, kNC0, false, full, empty, cta_w0, cta_w1,
-                                             cta_cnt, AV);
+                                             cta_cnt, AV, XH ? &xh : nullptr);
+        }
+    }
+    if constexpr (XH) {
+        static_assert(2 * kR <= 32, "one lane of the boundary warp per entry");
+        if (rid == kR) {
+            // The boundary warp.  Lane L < 2 kR stands for entry (ring L / 2,
+            // slot L % 2): whether that compute warp hands over a split group
+            // in that slot (from its atom range, as flush_values decides), and
+            // after how many of its atoms it does so (the order to wait in).
+            bool expect = false;
+            int key = 0;
+            if (lane < 2 * kR) {
+                const int w = lane >> 1, e = lane & 1;
+                const int64_t wk = P.packed ? static_cast<int64_t>(blockIdx.x) * kR + w
+                                            : static_cast<int64_t>(w) * gridDim.x + blockIdx.x;
+                const int64_t a0 = wk < P.nworkers ? worker_begin(P, wk) : 0;
+                const int64_t a1 = wk < P.nworkers ? worker_begin(P, wk + 1) : 0;
+                if (a1 > a0) {
+                    const bool back = walks_back(wk);
+                    // slot 0: the group holding a0, if it began before a0;
+                    // slot 1: the group holding a1 - 1, if it begins at or
+                    // after a0 and ends after a1
+                    const AtomCursor c = locate_atom(P, e == 0 ? a0 : a1 - 1);
+                    const TaskDesc &T = P.task[c.t];
+                    const int64_t sg = T.atom_base + static_cast<int64_t>(c.g) * T.apr, eg = sg + T.apr;
+                    const bool split = e == 0 ? sg < a0 : (sg >= a0 && eg > a1);
+                    // handed over only before the warp's last atom (its last
+                    // group it flushes itself)
+                    const int64_t at = e == 0 ? (back ? a1 - a0 : (eg < a1 ? eg : a1) - a0)
+                                              : (back ? a1 - sg : a1 - a0);
+                    if (split && at < a1 - a0) {
+                        const int64_t w1 = worker_of(P, sg), w2 = worker_of(P, eg - 1);
+                        expect = !(P.packed && w1 >= cta_w0 && w2 <= cta_w1);
+                        key = static_cast<int>(at);
+                    }
+                }
+            }
+            uint32_t pend = __ballot_sync(0xffffffffu, expect);
+            bool ok = true;
+            while (pend != 0u) {
+                const bool mine = (pend >> lane) & 1u;
+                const int kmin = static_cast<int>(__reduce_min_sync(0xffffffffu, mine ? static_cast<unsigned>(key)
+                                                                                      : 0x7fffffffu));
+                const int b = __ffs(static_cast<int>(__ballot_sync(0xffffffffu, mine && key == kmin))) - 1;
+                pend &= ~(1u << b);
+                const int w = b >> 1, e = b & 1;
+                if (!wait_phase(smem_addr(&xh_bar[w][e]), 0u, kWaitLimitNs)) {
+                    ok = false;
+                    break;
+                }
+                float v[NC], gv[NC];
+#pragma unroll
+                for (int j = 0; j < NC; ++j) {
+                    v[j] = lds32f(xh_vals + static_cast<uint32_t>(((w * 2 + e) * NC + j) * 128 + lane * 4));
+                    gv[j] = 0.0f;
+                }
+                const AtomCursor cur{ld_volatile_s32(smem_addr(&xh_tg[w][e][0])),
+                                     ld_volatile_s32(smem_addr(&xh_tg[w][e][1])), 0};
+                const int64_t wk = P.packed ? static_cast<int64_t>(blockIdx.x) * kR + w
+                                            : static_cast<int64_t>(w) * gridDim.x + blockIdx.x;
+                flush_values<NC, NC, MODE>(P, cur, v, gv, wk, worker_begin(P, wk), worker_begin(P, wk + 1), lane, 0,
+                                           cta_w0, cta_w1, cta_cnt);
+            }
+            if (!ok && lane == 0) atomicExch(P.status, kStatusTimeout);
         }
     }
 #if Q4K_TIMELINE
+    // (the boundary warp: record 14, word 3 = 0)
+    const int rec = rid < kR ? warp : 14;
     if (lane == 0 && P.tl != nullptr && blockIdx.x < Q4K_TIMELINE_CTAS && warp < 16) {
         unsigned long long *o =
-            P.tl + ((static_cast<int64_t>(P.tl_slot) * Q4K_TIMELINE_CTAS + blockIdx.x) * 16 + warp) * 8;
+            P.tl + ((static_cast<int64_t>(P.tl_slot) * Q4K_TIMELINE_CTAS + blockIdx.x) * 16 + rec) * 8;
         uint32_t smid;
         asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
         o[0] = tl_start;
@@ -1610,11 +1835,6 @@ __device__ __forceinline__ void atom_sums(const GemvParams &P, const AtomCursor 
     }
 }
 
-__device__ __forceinline__ float lds32f(uint32_t a) {
-    float v;
-    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
-    return v;
-}
 
 template <int NC, int MODE>
 __device__ __forceinline__ void gemv_queue(const GemvParams &P) {

@@ -203,6 +203,7 @@ def main():
         print(json.dumps(out))
         return
     print(f"config {args.config}, ncols {args.ncols}, {n} launches per step, graph replay; us")
+    keys = list(mean)
     print("launch  " + "  ".join(keys))
     for r in rows:
         print(f"{r['launch']:6d} " + "  ".join(f"{r[k]:7.2f}" if k in r else "      -" for k in keys))
