@@ -119,6 +119,8 @@ def lib() -> ctypes.CDLL:
             "q4k_workspace_status": (None, [_P, ctypes.POINTER(_I), _P]),
             "q4k_mul_mat_vec_noalloc": (None, [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P]),
             "q4k_noalloc_scratch_bytes": (_SZ, []),
+            "q4k_sharded_workspace_bytes": (_SZ, [_I64, _I64, _I, _I]),
+            "q4k_gemv_sharded": (None, [_P, _P, _P, _I64, _I64, _I, _I64, _I64, _I64, _P, _I, _I, _P, _SZ, _P]),
             "q4k_gemv_batch_allgather": (None, [TP, _I, _I, GP, _P, _SZ, _P]),
             "q4k_gather_wait": (None, [GP, _P, _SZ, _P]),
             "q4k_workspace_init": (None, [_P, _SZ, _P]),
@@ -296,6 +298,30 @@ def mul_mat_vec_q_noalloc(W, x, out=None, stream=None):
         out = torch.empty((ncols, nrows), dtype=torch.float32, device=x.device)
     _check(lib().q4k_mul_mat_vec_noalloc(W.data_ptr(), x.data_ptr(), out.data_ptr(), K, nrows, ncols,
                                          W.stride(0) // BLOCK_BYTES, x.stride(0), out.stride(0), _stream(stream)))
+    return out
+
+
+def sharded_workspace_bytes(nrows: int, K: int, ncols: int, world: int) -> int:
+    return int(lib().q4k_sharded_workspace_bytes(nrows, K, ncols, world))
+
+
+def gemv_sharded(W_shard, x, nrows: int, nccl_comm: int, rank: int, world: int, out=None,
+                 ws: Workspace | None = None, stream=None):
+    """Row-sharded y = W @ x gathered over an NCCL communicator (its ncclComm_t
+    as an integer): this rank's rows W_shard (shard_rows(nrows, rank, world)),
+    the same fp32 x (ncols, K) on every rank; returns all (ncols, nrows) rows."""
+    import torch
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    assert x.is_cuda and x.dtype == torch.float32 and x.stride(1) == 1
+    ncols, K = x.shape
+    if out is None:
+        out = torch.empty((ncols, nrows), dtype=torch.float32, device=x.device)
+    w = _ws_for(sharded_workspace_bytes(nrows, K, ncols, world), ws, x.device)
+    wptr = W_shard.data_ptr() if W_shard is not None and W_shard.numel() else None
+    rs = W_shard.stride(0) // BLOCK_BYTES if W_shard is not None and W_shard.dim() == 2 else K // QK_K
+    _check(lib().q4k_gemv_sharded(wptr, x.data_ptr(), out.data_ptr(), K, nrows, ncols, rs, x.stride(0),
+                                  out.stride(0), nccl_comm, rank, world, w.ptr, w.nbytes, _stream(stream)))
     return out
 
 

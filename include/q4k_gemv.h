@@ -327,6 +327,29 @@ Q4K_API int q4k_ipc_handle(const void *ptr, void *handle64);
 Q4K_API int q4k_ipc_open(const void *handle64, void **ptr);
 Q4K_API int q4k_ipc_close(void *ptr);
 
+/* ---- row-sharded GEMV over an NCCL communicator ------------------------------ */
+
+/* Replaces the row-split call ggml_cuda_op_mul_mat_vec_q (mmvq.cu:764-793)
+ * plus upstream ggml's copy of the slices into one tensor, for a runtime
+ * that holds one NCCL communicator per device (nccl_comm: its ncclComm_t).
+ * Rank r owns rows [r*S, min(r*S + S, nrows)) of the nrows x K matrix,
+ * S = ceil(nrows / world) (the last ranks may own fewer rows, or none);
+ * W_shard holds those rows (stride_row_x super-blocks apart; unused when the
+ * rank owns none).  Every rank passes the same fp32 activations x (ncols
+ * columns, stride_col_x apart) and receives all nrows rows of every column
+ * in y (stride_col_y apart).  Stream-ordered: the rank's GEMV, one
+ * ncclAllGather on the caller's stream, and one small kernel that places the
+ * rows; every rank of the communicator must make the same calls in the same
+ * order.  The communicator's size and rank must equal world and rank
+ * (Q4K_EINVAL otherwise); an NCCL failure returns Q4K_ENCCL.  The library
+ * uses the NCCL already loaded in the process (the one that created the
+ * communicator), else loads libnccl.so.2. */
+#define Q4K_MAX_SHARD_RANKS 1024
+Q4K_API size_t q4k_sharded_workspace_bytes(int64_t nrows, int64_t K, int ncols, int world);
+Q4K_API int q4k_gemv_sharded(const void *W_shard, const float *x, float *y, int64_t K, int64_t nrows, int ncols,
+                             int64_t stride_row_x, int64_t stride_col_x, int64_t stride_col_y, void *nccl_comm,
+                             int rank, int world, void *workspace, size_t workspace_bytes, q4k_stream_t stream);
+
 /* ---- callers that cannot allocate --------------------------------------------- */
 
 /* q4k_mul_mat_vec without a caller workspace.  No counterpart in the reference.

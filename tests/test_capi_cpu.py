@@ -206,3 +206,26 @@ def test_kernel_choice_rejects_bad_tasks(q4k):
     assert b"K" in L.q4k_last_error()
     with pytest.raises(q4k.Q4KError):
         q4k.batch_kernel(bad, 1, num_sms=148)
+
+
+def test_sharded_argument_checks(q4k):
+    """q4k_gemv_sharded refuses bad ranks, communicators, shapes and
+    workspaces before it touches NCCL or a device."""
+    L = q4k.lib()
+    assert L.q4k_sharded_workspace_bytes(100, 4096, 1, 0) == 0
+    assert L.q4k_sharded_workspace_bytes(0, 4096, 1, 2) == 0
+    assert L.q4k_sharded_workspace_bytes(100, 100, 1, 2) == 0  # K % 256
+    # staging for 4 ranks x 2 columns x ceil(100 / 4) rows beside the shard's GEMV workspace
+    assert L.q4k_sharded_workspace_bytes(100, 4096, 2, 4) >= q4k.gemv_workspace_bytes(25, 4096, 2) + 4 * 2 * 25 * 4
+
+    def call(W=256, x=512, y=1024, K=4096, nrows=100, ncols=1, srx=16, scx=4096, scy=100, comm=4096, rank=0,
+             world=2, ws=4096, wsb=1 << 30):
+        return L.q4k_gemv_sharded(W, x, y, K, nrows, ncols, srx, scx, scy, comm, rank, world, ws, wsb, None)
+
+    for kw in [dict(world=0), dict(world=1025), dict(rank=2), dict(rank=-1), dict(comm=None), dict(ncols=0),
+               dict(ncols=9), dict(nrows=0), dict(y=None), dict(x=None), dict(ncols=2, scy=99), dict(K=100)]:
+        assert call(**kw) == EINVAL, kw
+        assert len(L.q4k_last_error()) > 0
+    assert call(ws=None) == EWORKSPACE
+    assert call(wsb=64) == EWORKSPACE
+    assert call(ws=4096 + 16) == EWORKSPACE  # not 256-byte aligned
