@@ -38,11 +38,14 @@ def main():
     uid = NcclUniqueId()
     if rank == 0:
         assert N.ncclGetUniqueId(ctypes.byref(uid)) == 0
-    box = [bytes(uid.internal) if rank == 0 else None]
+    # the raw 128 bytes (the c_char array's value would stop at the first zero byte)
+    box = [ctypes.string_at(ctypes.addressof(uid), 128) if rank == 0 else None]
     dist.broadcast_object_list(box, src=0)
-    ctypes.memmove(ctypes.addressof(uid), box[0], 128)
+    if rank != 0:
+        ctypes.memmove(ctypes.addressof(uid), box[0], 128)
     comm = ctypes.c_void_p()
-    assert N.ncclCommInitRank(ctypes.byref(comm), world, uid, rank) == 0
+    rc = N.ncclCommInitRank(ctypes.byref(comm), world, uid, rank)
+    assert rc == 0, f"ncclCommInitRank: {rc}"
     try:
         rng = np.random.default_rng(1234)  # identical on every rank
         for nrows, K, ncols in [(1001, 4096, 1), (4099, 4096, 2), (77, 2048, 8)]:
