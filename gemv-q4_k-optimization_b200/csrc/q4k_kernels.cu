@@ -659,10 +659,9 @@ __device__ __forceinline__ uint32_t r2_scr(uint32_t scr, int e, int r, int col) 
     return scr + static_cast<uint32_t>(((e * 64 + r) * 8 + (col ^ (((r >> 2) & 1) * 4))) * 4);
 }
 
+// The 8 MMAs of sub-block pair c: d[e][i] = sums of sub-block 2c + e, tile i.
 template <int NC>
-__device__ __forceinline__ void pair_dot2_mma(uint32_t box, uint32_t act, uint32_t scr, int lane, int c,
-                                              const SbHead &A, const SbHead &B, uint64_t (&accA)[NC],
-                                              uint64_t (&accB)[NC]) {
+__device__ __forceinline__ void pair_mma(uint32_t box, uint32_t act, int lane, int c, uint32_t (&d)[2][4][4]) {
     const int g = lane >> 2, t = lane & 3;
     uint32_t bE0 = 0u, bE1 = 0u, bO0 = 0u, bO1 = 0u;  // columns >= NC stay zero
     if (g < NC) {
@@ -672,7 +671,6 @@ __device__ __forceinline__ void pair_dot2_mma(uint32_t box, uint32_t act, uint32
         bO0 = lds32(aj + 32);
         bO1 = lds32(aj + 48);
     }
-    __syncwarp();  // the previous pair's scratch reads are done
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const uint32_t p = box + static_cast<uint32_t>((i >> 1) * kBoxBytes + (16 * (i & 1) + g) * kPitch + 16 +
@@ -681,17 +679,31 @@ __device__ __forceinline__ void pair_dot2_mma(uint32_t box, uint32_t act, uint32
         const uint32_t aE[4] = {w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, w2 & 0x0F0F0F0Fu, w3 & 0x0F0F0F0Fu};
         const uint32_t aO[4] = {(w0 >> 4) & 0x0F0F0F0Fu, (w1 >> 4) & 0x0F0F0F0Fu, (w2 >> 4) & 0x0F0F0F0Fu,
                                 (w3 >> 4) & 0x0F0F0F0Fu};
-        uint32_t dE[4], dO[4];
-        mma_u8s8(dE, aE, bE0, bE1);
-        mma_u8s8(dO, aO, bO0, bO1);
-        const int r = 16 * i + g;
-        sts64u(r2_scr(scr, 0, r, 2 * t), dE[0], dE[1]);
-        sts64u(r2_scr(scr, 0, r + 8, 2 * t), dE[2], dE[3]);
-        sts64u(r2_scr(scr, 1, r, 2 * t), dO[0], dO[1]);
-        sts64u(r2_scr(scr, 1, r + 8, 2 * t), dO[2], dO[3]);
+        mma_u8s8(d[0][i], aE, bE0, bE1);
+        mma_u8s8(d[1][i], aO, bO0, bO1);
     }
-    __syncwarp();
-    // lane = row: rows lane (A) and 32 + lane (B), columns 0 .. NC-1
+}
+
+// Pair c's sums into the warp's scratch (every lane's reads of the previous
+// pair are done: the caller's __syncwarp).
+__device__ __forceinline__ void pair_store(uint32_t scr, int lane, const uint32_t (&d)[2][4][4]) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = 16 * i + g;
+            sts64u(r2_scr(scr, e, r, 2 * t), d[e][i][0], d[e][i][1]);
+            sts64u(r2_scr(scr, e, r + 8, 2 * t), d[e][i][2], d[e][i][3]);
+        }
+    }
+}
+
+// Pair c's sums back lane = row (rows lane and 32 + lane), combined as
+// pair_dot2 combines them.
+template <int NC>
+__device__ __forceinline__ void pair_combine(uint32_t act, uint32_t scr, int lane, int c, const SbHead &A,
+                                             const SbHead &B, uint64_t (&accA)[NC], uint64_t (&accB)[NC]) {
     int eA[8], oA[8], eB[8], oB[8];
 #pragma unroll
     for (int h = 0; h < (NC + 3) / 4; ++h) {
@@ -724,12 +736,27 @@ __device__ __forceinline__ void pair_dot2_mma(uint32_t box, uint32_t act, uint32
     }
 }
 
+// The 4 pairs of a super-block, software-pipelined: pair c + 1's loads and
+// MMAs are issued before pair c's scratch round trip and float combination.
 template <int NC>
 __device__ __forceinline__ void sb_dot2_mma(uint32_t box, uint32_t act, uint32_t scr, int lane,
                                             uint64_t (&accA)[NC], uint64_t (&accB)[NC]) {
     const SbHead A = sb_head(box + lane * kPitch), B = sb_head(box + kBoxBytes + lane * kPitch);
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) pair_dot2_mma<NC>(box, act, scr, lane, c, A, B, accA, accB);
+    uint32_t d0[2][4][4], d1[2][4][4];
+    pair_mma<NC>(box, act, lane, 0, d0);
+#pragma unroll
+    for (int c = 0; c < 4; c += 2) {
+        __syncwarp();  // the previous pair's scratch reads are done
+        pair_store(scr, lane, d0);
+        pair_mma<NC>(box, act, lane, c + 1, d1);
+        __syncwarp();
+        pair_combine<NC>(act, scr, lane, c, A, B, accA, accB);
+        __syncwarp();
+        pair_store(scr, lane, d1);
+        if (c + 2 < 4) pair_mma<NC>(box, act, lane, c + 2, d0);
+        __syncwarp();
+        pair_combine<NC>(act, scr, lane, c + 1, A, B, accA, accB);
+    }
 }
 #endif
 
