@@ -192,7 +192,9 @@ __host__ __device__ constexpr int q_aux_bytes(int ncols, int mode) {
 }
 // activation records per column in a ring stage: a two-row atom covers one
 // super-block, the others kKS (ring geometry of the static kernel's variants)
-__host__ __device__ constexpr int q_col_pitch(int mode) { return (mode == kModeR2 ? 1 : kKS) * kActSBBytes; }
+// (two-row atoms: 336, an odd number of 16-byte units, so the MMA operand
+// loads of 8 columns at the same offset hit 8 different bank groups)
+__host__ __device__ constexpr int q_col_pitch(int mode) { return mode == kModeR2 ? kActSBBytes + 16 : kKS * kActSBBytes; }
 __host__ __device__ constexpr int round128(int b) { return (b + 127) / 128 * 128; }
 __host__ __device__ constexpr int q_stage_bytes(int ncols, int mode) {
     return mode == kModeActSmem ? kWStageBytes : round128(kWStageBytes + ncols * q_col_pitch(mode));
