@@ -744,6 +744,7 @@ __device__ __forceinline__ void sb_dot2_mma(uint32_t box, uint32_t act, uint32_t
     const SbHead A = sb_head(box + lane * kPitch), B = sb_head(box + kBoxBytes + lane * kPitch);
     uint32_t d0[2][4][4], d1[2][4][4];
     pair_mma<NC>(box, act, lane, 0, d0);
+    // (unrolled: rolled, it measured 4 % slower at 8 columns)
 #pragma unroll
     for (int c = 0; c < 4; c += 2) {
         __syncwarp();  // the previous pair's scratch reads are done
