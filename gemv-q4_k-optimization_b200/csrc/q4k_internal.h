@@ -101,14 +101,14 @@ enum GemvMode : int {
 constexpr int kR2Min = Q4K_R2_MIN;
 // Two-row atoms of Q4K_R2_MMA_MIN or more columns take their integer sums
 // from int8 tensor-core MMAs (fewer columns: dp4a); each warp then needs a
-// 4 KB scratch after the rings.  Measured on B200 (Mistral layer): 8 columns
-// 20 % faster than dp4a, 4 columns 5 % slower (the MMA's 8 columns are half
-// padding there).
+// 4 KB scratch after the rings.  Measured on B200 (Mistral-7B layer launch,
+// us): ncols 3 33.3 dp4a / 35.1 MMA, 4 37.2 / 35.3, 5 43.9 / 39.2, 8 58.9 /
+// 45.4 (the MMA always computes 8 columns, padding included).
 #ifndef Q4K_R2_MMA
 #define Q4K_R2_MMA 1
 #endif
 #ifndef Q4K_R2_MMA_MIN
-#define Q4K_R2_MMA_MIN 6
+#define Q4K_R2_MMA_MIN 4
 #endif
 constexpr int kR2MmaMin = Q4K_R2_MMA_MIN;
 __host__ __device__ constexpr int r2_scr_bytes(int ncols, int mode) {
