@@ -111,6 +111,13 @@ constexpr int kR2Min = Q4K_R2_MIN;
 #define Q4K_R2_MMA_MIN 4
 #endif
 constexpr int kR2MmaMin = Q4K_R2_MMA_MIN;
+// Register cap of the two-row MMA variants (k_gemv's max_regs_m): measured
+// on B200, 14336x4096 chain ncols 4 18.7 -> 16.2 us, ncols 8 21.3 -> 19.2 us
+// (the next quantization launch runs beside the GEMV's tail); the Mistral
+// layer chain 2 % slower at ncols 4 and 8.
+#ifndef Q4K_R2_MMA_MAXREG
+#define Q4K_R2_MMA_MAXREG 216
+#endif
 __host__ __device__ constexpr int r2_scr_bytes(int ncols, int mode) {
     return (Q4K_R2_MMA && mode == kModeR2 && ncols >= kR2MmaMin) ? kMaxWarps * 2 * 64 * 8 * 4 : 0;
 }

@@ -2273,8 +2273,15 @@ __device__ __forceinline__ void gemv_queue(const GemvParams &P) {
     if (P.gworld > 1) gather_epilogue(P);
 }
 
+// Registers per thread: the two-row MMA variants are capped so that the next
+// launch's quantization CTA (256 threads x 32 registers) fits on the SM
+// beside a GEMV CTA and runs during its tail (216 x 256 + 8192 <= 65536).
+__host__ __device__ constexpr int max_regs_m(int ncols, int mode) {
+    return (Q4K_R2_MMA && mode == kModeR2 && ncols >= kR2MmaMin) ? Q4K_R2_MMA_MAXREG : 255;
+}
 template <int NC, int MODE>
-__global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) k_gemv(const __grid_constant__ GemvParams P) {
+__global__ void __launch_bounds__(warps_m(NC, MODE) * 32, 1) __maxnreg__(max_regs_m(NC, MODE))
+    k_gemv(const __grid_constant__ GemvParams P) {
     if constexpr (is_queue(MODE))
         gemv_queue<NC, MODE>(P);
     else
