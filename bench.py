@@ -791,13 +791,58 @@ def main():
         h2d = sum(h.numel() * 4 for h in h_x)
         d2h = sum(h.numel() * 4 for h in h_y)
 
+        # One GPU: the copies run on a second stream, overlapped with the
+        # launches: the activations arrive in three chunks of launch groups
+        # (the first group's alone, so the first launch starts after a
+        # ~100 KB copy), and the outputs leave in three chunks as their groups
+        # complete; the step ends when its last outputs are on the host.
+        pipelined = world == 1 and not C.peer and len(W.L) >= 4
+        cs = torch.cuda.Stream(device=C.dev)
+
+        def group_range(t0, t1, key):
+            """[lo, hi) element range of x_all / y_all used by groups t0..t1-1."""
+            views = [v for G in W.L[t0:t1] for v in (G["xs"].values() if key == "x" else [G["ybuf"]])]
+            return (min(v.storage_offset() for v in views),
+                    max(v.storage_offset() + v.numel() for v in views))
+
+        ng = len(W.L)
+        x_chunks = [(a, b) for a, b in [(0, 1), (1, 4), (4, ng)] if a < b]
+        y_chunks = [(a, b) for a, b in [(0, ng // 2), (ng // 2, ng - 2), (ng - 2, ng)] if a < b]
+        x_rng = [group_range(a, b, "x") for a, b in x_chunks] if pipelined else []
+        y_rng = [group_range(a, b, "y") for a, b in y_chunks] if pipelined else []
+        if pipelined:  # the bytes the chunks move (the outputs without the buffer's tail padding)
+            h2d = sum(hi - lo for lo, hi in x_rng) * 4
+            d2h = sum(hi - lo for lo, hi in y_rng) * 4
+        ev_x = [torch.cuda.Event() for _ in x_chunks]
+        ev_y = [torch.cuda.Event() for _ in y_chunks]
+
         def e2e_step():
+            if not pipelined:
+                with torch.cuda.stream(W.stream):
+                    for h, d in zip(h_x, xs_all):
+                        d.copy_(h, non_blocking=True)
+                    W.run_step()
+                    for h, d in zip(h_y, ys_all):
+                        h.copy_(d, non_blocking=True)
+                return
+            x_dev, x_host, y_dev, y_host = xs_all[0], h_x[0], ys_all[0], h_y[0]
+            cs.wait_stream(W.stream)  # the previous step (launches and copies) is done
+            with torch.cuda.stream(cs):
+                for (lo, hi), e in zip(x_rng, ev_x):
+                    x_dev[lo:hi].copy_(x_host[lo:hi], non_blocking=True)
+                    e.record(cs)
             with torch.cuda.stream(W.stream):
-                for h, d in zip(h_x, xs_all):
-                    d.copy_(h, non_blocking=True)
-                W.run_step()
-                for h, d in zip(h_y, ys_all):
-                    h.copy_(d, non_blocking=True)
+                for (a, b), e in zip(x_chunks, ev_x):
+                    W.stream.wait_event(e)
+                    for gi in range(a, b):
+                        W.gemv(W.L[gi]["tasks"])
+                        for (ya, yb), (lo, hi), ey in zip(y_chunks, y_rng, ev_y):
+                            if gi + 1 == yb:
+                                ey.record(W.stream)
+                                cs.wait_event(ey)
+                                with torch.cuda.stream(cs):
+                                    y_host[lo:hi].copy_(y_dev[lo:hi], non_blocking=True)
+            W.stream.wait_stream(cs)  # the step ends with its outputs on the host
 
         for _ in range(args.warmup):
             e2e_step()
@@ -812,10 +857,15 @@ def main():
         e_ms = C.max_over_ranks([a.elapsed_time(b) / args.steps])[0]
         e2e = {"value": step_total / (e_ms * 1e-3) / 1e12, "unit": "TB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms,
-               "path": "batch C-ABI calls (ctypes), one per launch group, eager (no graph); every step one copy "
-                       "of all its activations pinned host -> device before the calls and one copy of all its "
-                       "outputs device -> pinned host after them" +
-                       ("; the gather wait before the copy back" if C.peer else "")}
+               "path": ("batch C-ABI calls (ctypes), one per launch group, eager (no graph); every step all its "
+                        "activations copied pinned host -> device in 3 chunks of launch groups on a copy stream "
+                        "(group 0, groups 1-3, the rest), each chunk before its groups' calls, and all its outputs "
+                        "copied device -> pinned host in 3 chunks as their groups complete; the step ends when the "
+                        "last outputs are on the host" if pipelined else
+                        "batch C-ABI calls (ctypes), one per launch group, eager (no graph); every step one copy "
+                        "of all its activations pinned host -> device before the calls and one copy of all its "
+                        "outputs device -> pinned host after them" +
+                        ("; the gather wait before the copy back" if C.peer else ""))}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
