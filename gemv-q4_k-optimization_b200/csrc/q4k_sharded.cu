@@ -44,7 +44,7 @@ int fail(int status, const char *fmt, ...) {
     return status;
 }
 
-// ---- the NCCL entry points, resolved once per process ------------------------
+// ---- the NCCL entry points ---------------------------------------------------
 struct NcclApi {
     ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*comm_count)(const ncclComm_t, int *) = nullptr;
@@ -54,23 +54,26 @@ struct NcclApi {
     char why[200] = {0};
 };
 
+// Resolved on first use; a failed lookup is retried on the next call (the
+// process may load NCCL later), a successful one is kept.
 const NcclApi &nccl_api() {
     static NcclApi api;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);  // the process's own NCCL
-        if (h == nullptr) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
-        if (h == nullptr) {
-            snprintf(api.why, sizeof(api.why), "libnccl.so.2 not loadable: %s", dlerror());
-            return;
-        }
-        api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
-        api.comm_count = reinterpret_cast<decltype(api.comm_count)>(dlsym(h, "ncclCommCount"));
-        api.comm_user_rank = reinterpret_cast<decltype(api.comm_user_rank)>(dlsym(h, "ncclCommUserRank"));
-        api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
-        api.ok = api.all_gather && api.comm_count && api.comm_user_rank && api.error_string;
-        if (!api.ok) snprintf(api.why, sizeof(api.why), "libnccl.so.2 lacks ncclAllGather / ncclCommCount");
-    });
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (api.ok) return api;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);  // the process's own NCCL
+    if (h == nullptr) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (h == nullptr) {
+        const char *why = dlerror();
+        snprintf(api.why, sizeof(api.why), "libnccl.so.2 not loadable: %s", why ? why : "unknown");
+        return api;
+    }
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+    api.comm_count = reinterpret_cast<decltype(api.comm_count)>(dlsym(h, "ncclCommCount"));
+    api.comm_user_rank = reinterpret_cast<decltype(api.comm_user_rank)>(dlsym(h, "ncclCommUserRank"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    api.ok = api.all_gather && api.comm_count && api.comm_user_rank && api.error_string;
+    if (!api.ok) snprintf(api.why, sizeof(api.why), "libnccl.so.2 lacks ncclAllGather / ncclCommCount");
     return api;
 }
 
