@@ -630,7 +630,7 @@ __device__ __forceinline__ void pair_dot2(uint32_t pA, uint32_t pB, uint32_t act
 }
 
 #if Q4K_R2_MMA
-// ---- two-row atoms on the tensor cores (ncols >= kR2Min) ---------------------
+// ---- two-row atoms on the tensor cores (ncols >= kR2MmaMin) ------------------
 // The integer sub-block sums of a 64-row atom come from int8 MMAs instead of
 // dp4a: per sub-block pair c, for each 16-row tile of the atom,
 // D(16 x 8) = nibbles(16 x 32, u8) x q8(32 x 8 columns, s8), once for the
