@@ -454,7 +454,8 @@ def batch_ex_workspace_bytes(tasks, ncols: int) -> int:
 
 
 KERNEL_NAMES = {0: "k_gemv", 2: "k_gemv (epilogue)", 3: "k_gemv (two rows per lane)", 5: "k_gemv_dyn",
-                6: "k_gemv_dyn (epilogue)", 7: "k_gemv (single launch)"}
+                6: "k_gemv_dyn (epilogue)", 7: "k_gemv (single launch)",
+                8: "k_gemv (two rows per lane, int8 MMA)"}
 
 
 def batch_kernel(tasks, ncols: int, num_sms: int | None = None) -> str:

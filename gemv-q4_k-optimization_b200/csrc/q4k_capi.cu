@@ -921,6 +921,12 @@ int q4k_gemv_batch(const q4k_task *tasks, int ntasks, int ncols, void *workspace
     return run(jobs, ntasks, ncols, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
+// Kernel id of a plan: its variant, told apart for two-row launches by
+// where their integer sums run.
+static int kernel_id(int mode, int ncols) {
+    return (mode == kModeR2 && Q4K_R2_MMA && ncols >= kR2MmaMin) ? Q4K_KERNEL_STATIC_TWO_ROW_MMA : mode;
+}
+
 int q4k_batch_ex_kernel(const q4k_task_ex *tasks, int ntasks, int ncols, int num_sms) {
     if (!tasks || ntasks < 1 || ntasks > kMaxTasks) {
         fail(Q4K_EINVAL, "ntasks=%d outside 1..16", ntasks);
@@ -940,7 +946,7 @@ int q4k_batch_ex_kernel(const q4k_task_ex *tasks, int ntasks, int ncols, int num
                       Q4K_KERNEL_STATIC_TWO_ROW == kModeR2 && Q4K_KERNEL_DYNAMIC == kModeDynPlain &&
                       Q4K_KERNEL_DYNAMIC_GATED == kModeDynGated,
                   "kernel ids");
-    return P.mode;
+    return kernel_id(P.mode, ncols);
 }
 
 int q4k_batch_persistent_kernel(const q4k_task *tasks, int ntasks, int ncols, int num_sms) {
@@ -960,7 +966,7 @@ int q4k_batch_persistent_kernel(const q4k_task *tasks, int ntasks, int ncols, in
     // the decision run() makes for q4k_gemv_batch_persistent
     if (make_plan(jobs, ntasks, ncols, nullptr, num_sms, P, nullptr, false, 0, false, true) != Q4K_OK) return -1;
     static_assert(Q4K_KERNEL_SINGLE_LAUNCH == kModeActSmem, "kernel ids");
-    return P.mode;
+    return kernel_id(P.mode, ncols);
 }
 
 size_t q4k_batch_ex_workspace_bytes(const q4k_task_ex *tasks, int ntasks, int ncols) {

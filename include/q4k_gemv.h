@@ -16,6 +16,8 @@
  *                                      -> q4k_quantize_q8_1()
  *   kernels/mmvq.cu:764-793            ggml_cuda_op_mul_mat_vec_q (row-split
  *                                      slice per device) -> q4k_op_mul_mat_vec_q()
+ *                                      (with the slices gathered over an NCCL
+ *                                      communicator) -> q4k_gemv_sharded()
  *
  * Data formats (unchanged from ggml, so tensors pass through untouched):
  *   Q4_K super-block, 144 bytes per 256 weights: half d, half dmin,
@@ -383,6 +385,7 @@ Q4K_API size_t q4k_noalloc_scratch_bytes(void);
 #define Q4K_KERNEL_DYNAMIC 5         /* whole row groups per CTA from a ticket queue */
 #define Q4K_KERNEL_DYNAMIC_GATED 6   /* the same with the bias / GLU epilogue */
 #define Q4K_KERNEL_SINGLE_LAUNCH 7   /* static partition, activations quantized in the GEMV launch */
+#define Q4K_KERNEL_STATIC_TWO_ROW_MMA 8 /* two rows per lane, integer sums on int8 tensor-core MMAs (ncols >= 4) */
 Q4K_API int q4k_batch_ex_kernel(const q4k_task_ex *tasks, int ntasks, int ncols, int num_sms);
 /* The same question for q4k_gemv_batch_persistent: Q4K_KERNEL_SINGLE_LAUNCH
  * when the tasks run as one launch, else the kernel of its two-launch

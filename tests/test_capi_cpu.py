@@ -185,7 +185,7 @@ MISTRAL_SPECS = [(4096, 4096, 0, False), (1024, 4096, 0, False), (1024, 4096, 0,
     (MISTRAL_SPECS, 3, "k_gemv (two rows per lane)"),
     ([(14336, 4096, 0, False)], 1, "k_gemv_dyn"),             # one matrix, spread thinly: dynamic
     ([(14336, 4096, 0, False)], 2, "k_gemv_dyn"),
-    ([(14336, 4096, 0, False)], 4, "k_gemv (two rows per lane)"),
+    ([(14336, 4096, 0, False)], 4, "k_gemv (two rows per lane, int8 MMA)"),
     ([(4096, 4096, 0, False)], 1, "k_gemv"),                  # too few row groups for the queue
     ([(14336, 4096, 0, True)], 1, "k_gemv (epilogue)"),        # fused gate/up: K run over both matrices
     (MISTRAL_SPECS[:4] + [(14336, 4096, 2, True)] + MISTRAL_SPECS[6:], 1, "k_gemv (epilogue)"),  # a layer
